@@ -1,0 +1,392 @@
+#!/usr/bin/env python
+"""Benchmark of the decode-attention hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2]
+
+A step is one decode-attention call of the engine (the fused QK-norm/RoPE/KV-append prologue plus
+split-K GQA attention over the paged cache) for one batch. The default workload is BASELINE config
+c2 (B=16, 4096 cached keys + 1 appended, 32 query / 8 kv heads, d=128) per GPU. For N > 1 the kv
+heads are sharded 8/N per GPU and the batch grows to 16N (weak scaling: per-GPU work fixed), and
+each step all-gathers the head outputs over NCCL, as the engine does before o_proj.
+
+value: whole-job algorithmic bytes / device time (TB/s), inputs resident in HBM, back-to-back
+launches timed with CUDA events on the launching stream, max over ranks. Each step reads a different
+layer's cache (`--layers` caches in rotation, together far larger than the 126 MB L2).
+e2e: the same metric through the public call with host buffers: each step copies the new token's
+qkv and positions from pinned host memory, runs the step and copies the output back.
+--impl reference: the reference's CPU path (Transformers' q/k norm + RoPE + sdpa, oracle/cpu_path.py)
+on the same config, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode-attn achieved HBM TB/s (% of peak), us/call; Qwen3-4B decode tokens/s"
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+TRAFFIC_FILE = ROOT / "profiles" / "ncu_traffic.json"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4"], default="c2")
+    ap.add_argument("--layers", type=int, default=8, help="layer caches rotated across steps")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--soak-ms", type=float, default=600.0,
+                    help="untimed launches before the timed region, for the clock samples")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------------- plumbing
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world, local):
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        return dist
+    return None
+
+
+def max_over_ranks(dist, x: float) -> float:
+    if dist is None:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def peaks():
+    try:
+        p = json.loads(PEAKS_FILE.read_text())
+        return float(p["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, torch copy_ burst)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback 6.65 TB/s (no MEASURED_PEAKS.json)"
+
+
+def ncu_traffic(key: str):
+    try:
+        return json.loads(TRAFFIC_FILE.read_text()).get(key)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 50 ms for this process's GPU."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.proc = None
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", uuid, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, pw, reasons = [], [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+                pw.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, f[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "power_w_max": max(pw), "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------------------------- our arm
+class StepLauncher:
+    """Prebuilt C-ABI arguments for every layer, so a step costs one ctypes call."""
+
+    def __init__(self, case, attn, layers, out):
+        from kernel_optim_b200 import _lib
+        from kernel_optim_b200.fused import _ptr
+        self.fn = _lib.lib().kopt_decode_attn_fused
+        self.check = _lib.check
+        t = case.tensors
+        self.descs = [t["cache"].descriptor(i) for i in range(layers)]
+        self.common = (ctypes.byref(attn.plan), _ptr(t["qkv"]), _ptr(t["q_norm_w"]),
+                       _ptr(t["k_norm_w"]), _ptr(t["cos"]), _ptr(t["sin"]), t["cos"].shape[0])
+        self.tail = (_ptr(t["pos"]), _ptr(out), None, _ptr(attn.ws), ctypes.c_float(attn.scale),
+                     ctypes.c_float(attn.eps))
+        self.stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        self.layers = layers
+
+    def __call__(self, step: int):
+        rc = self.fn(*self.common, ctypes.byref(self.descs[step % self.layers]), *self.tail, self.stream)
+        if rc:
+            self.check(rc, "kopt_decode_attn_fused")
+
+
+def run_ours(args):
+    from kernel_optim_b200.paged import PagedDecodeAttention
+    from kernel_optim_b200.workloads import build_case
+    world, rank, local = dist_env()
+    dist = init_dist(world, local)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    n = world
+    case = build_case(args.workload, dev, seed=0, paged=True, batch_scale=n, kv_shard=n,
+                      kv_rank=rank, layers=args.layers)
+    t = case.tensors
+    B = case.B
+    attn = PagedDecodeAttention(B, case.nq, case.nkv, 128, dev)
+    out = torch.empty(B, case.nq * 128, dtype=torch.bfloat16, device=dev)
+    gathered = torch.empty(n, B, case.nq * 128, dtype=torch.bfloat16, device=dev) if n > 1 else None
+    launch = StepLauncher(case, attn, args.layers, out)
+    bytes_rank = case.algorithmic_bytes()
+    bytes_job = bytes_rank * n
+
+    def step(i):
+        launch(i)
+        if dist is not None:
+            dist.all_gather_into_tensor(gathered, out)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    err = attn.read_error()
+    if err:
+        raise RuntimeError(f"device error word {err} after warm-up")
+
+    sampler = ClockSampler(local)
+    # soak: untimed launches so the clock samples see the GPU under this load
+    t_end = time.perf_counter() + args.soak_ms / 1e3
+    i = 0
+    while time.perf_counter() < t_end:
+        step(i)
+        i += 1
+        if i % 64 == 0:
+            torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.steps):
+        step(i)
+    ev1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    if dist is not None:
+        dist.barrier()
+    ms = max_over_ranks(dist, ev0.elapsed_time(ev1))
+    ms_step = ms / args.steps
+    value_tbs = bytes_job / (ms_step * 1e-3) / 1e12
+
+    # kernel-only duration (no collective) for the roofline, same stream, back-to-back launches
+    torch.cuda.synchronize()
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record()
+    for i in range(args.steps):
+        launch(i)
+    k1.record()
+    torch.cuda.synchronize()
+    kern_ms = max_over_ranks(dist, k0.elapsed_time(k1)) / args.steps
+    err = attn.read_error()
+    if err:
+        raise RuntimeError(f"device error word {err} after the timed region")
+
+    peak, peak_src = peaks()
+    achieved = bytes_rank / (kern_ms * 1e-3) / 1e9
+    traffic = ncu_traffic(args.workload)
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "frac_of_8TBs_nominal": round(achieved / 8000, 4),
+                "traffic": traffic, "peak_source": peak_src,
+                "kernel": "decode_attn_kernel<PAGED=1,FUSED=1>", "kernel_us": round(kern_ms * 1e3, 2),
+                "algorithmic_bytes_per_launch": bytes_rank}
+
+    e2e = None if args.no_e2e else run_e2e(args, case, attn, launch, out, gathered, dist, bytes_job)
+    cpu = None
+    if n == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(case, bytes_rank)
+
+    line = {
+        "metric": METRIC, "value": round(value_tbs, 4), "unit": "TB/s", "n_gpus": n,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+        "us_per_call": round(ms_step * 1e3, 2), "pct_of_peak": round(100 * value_tbs * 1e3 / peak, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) bf16 cache and new-token q/k/v, unit norm weights, "
+                "Transformers Qwen3 RoPE tables (theta 5e6)",
+        "config": {
+            "workload": f"{args.workload} per GPU" + (f", weak-scaled x{n}" if n > 1 else ""),
+            "B": B, "keys_per_seq": (max(case.keys) if len(set(case.keys)) == 1 else "ragged"),
+            "q_heads_per_gpu": case.nq, "kv_heads_per_gpu": case.nkv, "head_dim": 128,
+            "paged": True, "page_size": 16, "layers_rotated": args.layers,
+            "parallelism": f"kv-head shard x{n} + NCCL all-gather" if n > 1 else "single GPU",
+            "l2": f"inputs larger than L2: {args.layers} layer caches of "
+                  f"{bytes_rank / 1e6:.0f} MB read in rotation, one per step",
+            "launch": "back-to-back C-ABI calls on one stream",
+        },
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, case, attn, launch, out, gathered, dist, bytes_job):
+    """Same steps through host buffers: pinned H2D of qkv + pos, the step, D2H of the output."""
+    t = case.tensors
+    qkv_h = t["qkv"].cpu().pin_memory()
+    pos_h = t["pos"].cpu().pin_memory()
+    res = gathered if gathered is not None else out
+    out_h = torch.empty(res.shape, dtype=res.dtype, pin_memory=True)
+
+    def step(i):
+        t["qkv"].copy_(qkv_h, non_blocking=True)
+        t["pos"].copy_(pos_h, non_blocking=True)
+        launch(i)
+        if dist is not None:
+            dist.all_gather_into_tensor(gathered, out)
+        out_h.copy_(res, non_blocking=True)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(dist, e0.elapsed_time(e1)) / args.steps
+    return {"value": round(bytes_job / (ms * 1e-3) / 1e12, 4), "unit": "TB/s",
+            "us_per_call": round(ms * 1e3, 2),
+            "h2d_bytes_per_step": qkv_h.numel() * 2 + pos_h.numel() * 4,
+            "d2h_bytes_per_step": out_h.numel() * 2}
+
+
+# --------------------------------------------------------------------------- CPU reference
+def _cpu_step_for(case, form):
+    from oracle.cpu_path import CpuDecodeStep
+    t = case.tensors
+    cache = t["cache"]
+    k_ctx, v_ctx = [], []
+    for b, L in enumerate(case.cached):
+        kb, vb = cache.gather(0, b, L)
+        k_ctx.append(kb.cpu())
+        v_ctx.append(vb.cpu())
+    return CpuDecodeStep(t["qkv"], t["q_norm_w"], t["k_norm_w"], t["cos"][: max(case.keys)],
+                         t["sin"][: max(case.keys)], t["pos"], k_ctx, v_ctx, case.nq, case.nkv,
+                         form=form)
+
+
+def cpu_baseline(case, bytes_step):
+    """The reference's CPU path on the full step, bounded to a few seconds per form."""
+    from oracle.cpu_path import time_steps
+    res = {}
+    for form, reps in (("repeat_kv", 10), ("enable_gqa", 30)):
+        st = _cpu_step_for(case, form)
+        secs = time_steps(st, reps, 2)
+        res[form] = secs / reps
+    per = res["repeat_kv"]
+    return {"value": round(bytes_step / per / 1e12, 6), "unit": "TB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": (f"full {case.name} step (B={case.B}) on the host: Transformers Qwen3RMSNorm + "
+                       f"apply_rotary_pos_emb + cache write + sdpa; repeat_kv form (pinned "
+                       f"Transformers 4.51.3) {per * 1e3:.1f} ms/step x10; enable_gqa form (installed "
+                       f"5.5.0) {res['enable_gqa'] * 1e3:.1f} ms/step x30")}
+
+
+def run_reference(args):
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    from kernel_optim_b200.workloads import build_case
+    from oracle.cpu_path import time_steps
+    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    n = world
+    case = build_case(args.workload, dev, seed=0, paged=True, batch_scale=n, kv_shard=1, layers=1)
+    st = _cpu_step_for(case, "repeat_kv")
+    secs = time_steps(st, args.steps, args.warmup)
+    per = secs / args.steps
+    bytes_step = case.algorithmic_bytes()
+    v = bytes_step / per / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(v, 6), "unit": "TB/s", "n_gpus": n,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per * 1e3, 3),
+        "us_per_call": round(per * 1e6, 1), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (same seeded inputs as ours)",
+        "config": {"workload": f"{args.workload} per GPU" + (f", weak-scaled x{n}" if n > 1 else ""),
+                   "B": case.B, "keys_per_seq": max(case.keys), "q_heads": case.nq,
+                   "kv_heads": case.nkv, "head_dim": 128},
+        "cpu_baseline": {"value": round(v, 6), "unit": "TB/s", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"full {case.name} step per timed step on the host: Transformers "
+                                   "Qwen3 q/k norm + RoPE + cache write + repeat_kv sdpa"},
+        "e2e": {"value": round(v, 6), "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

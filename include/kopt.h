@@ -1,0 +1,135 @@
+/*
+ * kopt.h -- C ABI of the B200 (sm_100a) decode-attention path for the Qwen3-4B engine.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (as void*), launches
+ * asynchronously on that stream, allocates nothing and returns an int status (KOPT_OK == 0).
+ * All tensors are bf16 unless stated; head_dim is 128 and the GQA group is 4 (nq == 4 * nkv).
+ *
+ * Reference interfaces replaced (GodRishUniverse/kernel_optim, paths inside that project):
+ *   kopt_decode_attn_plan  <- DecodeAttention.__init__      engine/kernels/fused.py:209-219
+ *   kopt_decode_attn       <- DecodeAttention.__call__      engine/kernels/fused.py:221-234
+ *                             (_decode_attn_kernel fused.py:138-185 + _decode_combine_kernel
+ *                              fused.py:188-201 in one launch)
+ *   kopt_qk_norm_rope      <- qk_norm_rope                  engine/kernels/fused.py:99-106
+ *                             (_qk_norm_rope_kernel fused.py:54-96)
+ *   kopt_decode_attn_fused <- qk_norm_rope + DecodeAttention.__call__ as called back to back in
+ *                             Engine._layers, engine/engine.py:328-330 (and engine.py:283-286)
+ */
+#ifndef KOPT_H_
+#define KOPT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KOPT_API __attribute__((visibility("default")))
+#else
+#define KOPT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------------- */
+#define KOPT_OK 0
+#define KOPT_ERR_ARG 1         /* bad shape, unsupported head_dim/group, bad pointer alignment */
+#define KOPT_ERR_CUDA 2        /* a CUDA runtime call failed (launch, attribute, device query) */
+#define KOPT_ERR_WORKSPACE 3   /* workspace too small for the plan */
+
+/* Bits of the device-side error word (read back with kopt_read_error). The kernels never trap:
+ * a bad page id or length is recorded here and the access is skipped or clamped. */
+#define KOPT_DEV_ERR_PAGE 1    /* block-table entry outside [0, num_pages) */
+#define KOPT_DEV_ERR_LEN 2     /* pos[b] + T outside [1, cap] (clamped) */
+#define KOPT_DEV_ERR_TIMEOUT 4 /* an mbarrier wait ran past its time limit */
+#define KOPT_DEV_ERR_ROPE 8    /* pos[b] + t outside the RoPE table (clamped) */
+
+/* ---- KV cache descriptor ---------------------------------------------------------------- *
+ * Contiguous (block_table == NULL): one layer's cache [B, nkv, cap, 128] bf16 with arbitrary
+ *   batch/head strides (elements, multiples of 8) and token stride 128, as engine/engine.py:186
+ *   allocates it and as DecodeAttention receives k_cache[i] (engine.py:395).
+ * Paged (block_table != NULL): one layer's page pool [num_pages, nkv, 16, 128] bf16; token t of
+ *   sequence b lives in page block_table[b * bt_stride + t / 16], row t % 16. cap is the largest
+ *   sequence length the table can address (bt_stride * 16). */
+typedef struct kopt_kv_cache {
+  void* k;
+  void* v;
+  int64_t stride_b;          /* contiguous only: elements between sequences */
+  int64_t stride_h;          /* contiguous only: elements between kv heads */
+  int32_t cap;               /* max tokens per sequence */
+  int32_t num_pages;         /* paged only */
+  const int32_t* block_table;/* paged only: [B, bt_stride] int32, device */
+  int32_t bt_stride;
+  int32_t page_size;         /* must be 16 */
+} kopt_kv_cache;
+
+/* ---- launch plan -------------------------------------------------------------------------- *
+ * Filled by kopt_decode_attn_plan for a fixed (B, T, nkv) and reused by every call, so the grid
+ * and workspace stay fixed across CUDA-graph replays. The split of each sequence's keys into
+ * units is decided on the device from the live lengths (pos[b] + T) at every call. */
+typedef struct kopt_plan {
+  int32_t B;
+  int32_t T;
+  int32_t nkv;
+  int32_t grid;              /* CTAs launched: slots_per_head * nkv */
+  int32_t slots_per_head;    /* co-resident CTAs per kv head */
+  int32_t waves;             /* units per slot when one balanced wave does not fit */
+  int32_t max_units;         /* partial-result slots in the workspace */
+  int32_t device;
+  int64_t ws_bytes;          /* workspace bytes the caller must provide (zeroed once) */
+} kopt_plan;
+
+/* Plan a decode-attention launch: B sequences, T query tokens each (T == 1), nq = 4 * nkv query
+ * heads of dim d == 128. target_ctas <= 0 lets the plan fill the device (SM count x resident
+ * CTAs per SM). Replaces DecodeAttention.__init__ (engine/kernels/fused.py:209-219). */
+KOPT_API int kopt_decode_attn_plan(int device, int B, int T, int nq, int nkv, int d, int target_ctas,
+                          kopt_plan* plan);
+
+/* Zero a workspace of plan->ws_bytes bytes (split counters and the error word). Call once after
+ * allocating it, and again after kopt_read_error reported a timeout. */
+KOPT_API int kopt_workspace_init(const kopt_plan* plan, void* ws, void* stream);
+
+/* Copy the device error word (KOPT_DEV_ERR_* bits) to *err_out and clear it. Synchronises the
+ * stream. */
+KOPT_API int kopt_read_error(const kopt_plan* plan, void* ws, int* err_out, void* stream);
+
+/* Split-K GQA decode attention over a cache whose new K/V are already written at pos[b]:
+ * out[b, h*128:(h+1)*128] = softmax(q_h . K[b, h/4, 0..pos[b]]^T * scale) V[b, h/4, 0..pos[b]].
+ * q, out: [B*T, nq*128] bf16 contiguous; pos: [B] int32 device. Writes out and the workspace.
+ * Replaces DecodeAttention.__call__(q, k_cache, v_cache, pos, out) (engine/kernels/fused.py:221). */
+KOPT_API int kopt_decode_attn(const kopt_plan* plan, const void* q, const kopt_kv_cache* cache,
+                     const int32_t* pos, void* out, void* ws, float scale, void* stream);
+
+/* Per-head QK-RMSNorm + RoPE + KV append (no attention), reference cast order:
+ * qkv [B*T, (nq + 2 nkv) * 128]; q heads -> q_out [B*T, nq*128]; k heads -> cache k at
+ * pos[b] + t; v heads copied to cache v at pos[b] + t. cos/sin: [rope_len, 128] bf16.
+ * Replaces qk_norm_rope(qkv, q_w, k_w, cos, sin, pos, q_out, k_cache, v_cache, T, eps, nq, nkv, d)
+ * (engine/kernels/fused.py:99-106). */
+KOPT_API int kopt_qk_norm_rope(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                      const void* cos, const void* sin, int rope_len, const int32_t* pos,
+                      void* q_out, const kopt_kv_cache* cache, int B, int T, int nq, int nkv,
+                      int d, float eps, int* dev_err, int device, void* stream);
+
+/* The engine's decode attention step in one launch: the QK-norm/RoPE prologue of the 4 query
+ * heads of each group, the new token's K (normed, roped) and V appended to the cache at pos[b]
+ * by the CTA that owns that position, and split-K attention over keys 0..pos[b] with the
+ * cross-split LSE combine done by the last CTA of each (sequence, kv head).
+ * qkv [B, (nq + 2 nkv) * 128] (T == 1); out [B, nq*128]; q_out optional (NULL) receives the
+ * roped q. Replaces engine/engine.py:328-330: qk_norm_rope (fused.py:99) then attn1
+ * (fused.py:221). */
+KOPT_API int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, const void* q_norm_w,
+                           const void* k_norm_w, const void* cos, const void* sin, int rope_len,
+                           const kopt_kv_cache* cache, const int32_t* pos, void* out, void* q_out,
+                           void* ws, float scale, float eps, void* stream);
+
+/* Human-readable text for a KOPT_* status. */
+KOPT_API const char* kopt_strerror(int status);
+
+/* ABI version of this library (bumped on any signature change). */
+KOPT_API int kopt_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KOPT_H_ */

@@ -1,0 +1,132 @@
+"""ctypes binding of libkopt.so (the C ABI declared in include/kopt.h).
+
+The library is built in-tree by kernel_optim_b200/build.py. There is no fallback: if the library is
+missing or fails to load, every entry point raises KoptError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libkopt.so"
+
+KOPT_OK = 0
+KOPT_ERR_ARG = 1
+KOPT_ERR_CUDA = 2
+KOPT_ERR_WORKSPACE = 3
+
+DEV_ERR_PAGE = 1
+DEV_ERR_LEN = 2
+DEV_ERR_TIMEOUT = 4
+DEV_ERR_ROPE = 8
+
+#: every symbol include/kopt.h declares
+EXPORTED = (
+    "kopt_abi_version",
+    "kopt_strerror",
+    "kopt_decode_attn_plan",
+    "kopt_workspace_init",
+    "kopt_read_error",
+    "kopt_decode_attn",
+    "kopt_qk_norm_rope",
+    "kopt_decode_attn_fused",
+)
+
+
+class KoptError(RuntimeError):
+    """A kopt entry point returned a non-zero status, or the library is unavailable."""
+
+
+class KvCache(ctypes.Structure):
+    """Mirror of struct kopt_kv_cache."""
+
+    _fields_ = [
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("stride_b", ctypes.c_int64),
+        ("stride_h", ctypes.c_int64),
+        ("cap", ctypes.c_int32),
+        ("num_pages", ctypes.c_int32),
+        ("block_table", ctypes.c_void_p),
+        ("bt_stride", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+    ]
+
+
+class Plan(ctypes.Structure):
+    """Mirror of struct kopt_plan."""
+
+    _fields_ = [
+        ("B", ctypes.c_int32),
+        ("T", ctypes.c_int32),
+        ("nkv", ctypes.c_int32),
+        ("grid", ctypes.c_int32),
+        ("slots_per_head", ctypes.c_int32),
+        ("waves", ctypes.c_int32),
+        ("max_units", ctypes.c_int32),
+        ("device", ctypes.c_int32),
+        ("ws_bytes", ctypes.c_int64),
+    ]
+
+
+_lock = threading.Lock()
+_lib = None
+
+_vp, _i32, _i64, _f32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+_SIGS = {
+    "kopt_abi_version": (_i32, []),
+    "kopt_strerror": (ctypes.c_char_p, [_i32]),
+    "kopt_decode_attn_plan": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(Plan)]),
+    "kopt_workspace_init": (_i32, [ctypes.POINTER(Plan), _vp, _vp]),
+    "kopt_read_error": (_i32, [ctypes.POINTER(Plan), _vp, ctypes.POINTER(ctypes.c_int), _vp]),
+    "kopt_decode_attn": (_i32, [ctypes.POINTER(Plan), _vp, ctypes.POINTER(KvCache), _vp, _vp, _vp,
+                                _f32, _vp]),
+    "kopt_qk_norm_rope": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, ctypes.POINTER(KvCache),
+                                 _i32, _i32, _i32, _i32, _i32, _f32, _vp, _i32, _vp]),
+    "kopt_decode_attn_fused": (_i32, [ctypes.POINTER(Plan), _vp, _vp, _vp, _vp, _vp, _i32,
+                                      ctypes.POINTER(KvCache), _vp, _vp, _vp, _vp, _f32, _f32, _vp]),
+}
+
+
+def lib() -> ctypes.CDLL:
+    """Load libkopt.so once and declare every signature. Raises KoptError if it is unavailable."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise KoptError(
+                    f"{LIB_PATH.name} is not built: run `python -m kernel_optim_b200.build` "
+                    "(or __graft_entry__.build()); there is no CPU fallback")
+            try:
+                handle = ctypes.CDLL(str(LIB_PATH))
+            except OSError as e:  # pragma: no cover - depends on the host
+                raise KoptError(f"cannot load {LIB_PATH}: {e}") from e
+            for name, (res, args) in _SIGS.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != KOPT_OK:
+        msg = lib().kopt_strerror(rc).decode()
+        raise KoptError(f"{what} failed: status {rc} ({msg})")
+
+
+def dev_error_text(bits: int) -> str:
+    names = []
+    if bits & DEV_ERR_PAGE:
+        names.append("block-table page id out of range")
+    if bits & DEV_ERR_LEN:
+        names.append("position outside the cache capacity (clamped)")
+    if bits & DEV_ERR_TIMEOUT:
+        names.append("mbarrier wait timed out")
+    if bits & DEV_ERR_ROPE:
+        names.append("position outside the RoPE table (clamped)")
+    return ", ".join(names) or "none"

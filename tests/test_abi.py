@@ -1,0 +1,74 @@
+"""CPU: the C-ABI library builds for sm_100a, loads, exports every declared symbol and rejects
+bad arguments before touching the GPU."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from kernel_optim_b200 import _lib
+from kernel_optim_b200.build import build
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "kopt.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _lib.lib()
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kopt_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_functions()
+    assert names, "no declarations parsed"
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in kopt.h but not exported"
+    assert set(names) == set(_lib.EXPORTED)
+
+
+def test_abi_version_and_strerror(lib):
+    assert lib.kopt_abi_version() == 1
+    assert lib.kopt_strerror(0) == b"ok"
+    assert b"argument" in lib.kopt_strerror(_lib.KOPT_ERR_ARG)
+    assert lib.kopt_strerror(999) == b"unknown kopt status"
+
+
+def test_struct_layouts_match_header():
+    # kopt_kv_cache: 2 pointers, 2 int64, 2 int32, pointer, 2 int32 -> 56 bytes on LP64
+    assert ctypes.sizeof(_lib.KvCache) == 56
+    assert ctypes.sizeof(_lib.Plan) == 40
+
+
+@pytest.mark.parametrize("args", [
+    (0, 16, 1, 32, 8, 64, 0),     # head_dim 64 unsupported
+    (0, 16, 1, 24, 8, 128, 0),    # group != 4
+    (0, 0, 1, 32, 8, 128, 0),     # empty batch
+    (0, 257, 1, 32, 8, 128, 0),   # batch above the plan limit
+    (0, 16, 2, 32, 8, 128, 0),    # T > 1 not built yet
+])
+def test_plan_rejects_bad_shapes(lib, args):
+    plan = _lib.Plan()
+    assert lib.kopt_decode_attn_plan(*args, ctypes.byref(plan)) == _lib.KOPT_ERR_ARG
+
+
+def test_launchers_reject_null_arguments(lib):
+    plan = _lib.Plan()
+    cache = _lib.KvCache()
+    assert lib.kopt_decode_attn(None, None, None, None, None, None, 1.0, None) == _lib.KOPT_ERR_ARG
+    assert lib.kopt_decode_attn(ctypes.byref(plan), None, ctypes.byref(cache), None, None, None,
+                                1.0, None) == _lib.KOPT_ERR_ARG
+    assert lib.kopt_decode_attn_fused(ctypes.byref(plan), None, None, None, None, None, 0,
+                                      ctypes.byref(cache), None, None, None, None, 1.0, 1e-6,
+                                      None) == _lib.KOPT_ERR_ARG
+    assert lib.kopt_qk_norm_rope(None, None, None, None, None, 1, None, None, ctypes.byref(cache),
+                                 1, 1, 32, 8, 128, 1e-6, None, 0, None) == _lib.KOPT_ERR_ARG
+    assert lib.kopt_workspace_init(None, None, None) == _lib.KOPT_ERR_ARG
+    err = ctypes.c_int(0)
+    assert lib.kopt_read_error(None, None, ctypes.byref(err), None) == _lib.KOPT_ERR_ARG
