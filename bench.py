@@ -50,6 +50,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c2", "c3", "c4"], default="c2")
     ap.add_argument("--layers", type=int, default=8, help="layer caches rotated across steps")
+    ap.add_argument("--layout", choices=["paged", "contiguous"], default="paged")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--soak-ms", type=float, default=600.0,
@@ -150,16 +151,21 @@ class ClockSampler:
 class StepLauncher:
     """Prebuilt C-ABI arguments for every layer, so a step costs one ctypes call."""
 
-    def __init__(self, case, attn, layers, out):
+    def __init__(self, case, attn, layers, out, qkv=None, pos=None):
         from kernel_optim_b200 import _lib
-        from kernel_optim_b200.fused import _ptr
+        from kernel_optim_b200.fused import _ptr, contiguous_cache
         self.fn = _lib.lib().kopt_decode_attn_fused
         self.check = _lib.check
         t = case.tensors
-        self.descs = [t["cache"].descriptor(i) for i in range(layers)]
-        self.common = (ctypes.byref(attn.plan), _ptr(t["qkv"]), _ptr(t["q_norm_w"]),
+        qkv = t["qkv"] if qkv is None else qkv
+        pos = t["pos"] if pos is None else pos
+        if "cache" in t:
+            self.descs = [t["cache"].descriptor(i) for i in range(layers)]
+        else:
+            self.descs = [contiguous_cache(t["k_cache"][i], t["v_cache"][i]) for i in range(layers)]
+        self.common = (ctypes.byref(attn.plan), _ptr(qkv), _ptr(t["q_norm_w"]),
                        _ptr(t["k_norm_w"]), _ptr(t["cos"]), _ptr(t["sin"]), t["cos"].shape[0])
-        self.tail = (_ptr(t["pos"]), _ptr(out), None, _ptr(attn.ws), ctypes.c_float(attn.scale),
+        self.tail = (_ptr(pos), _ptr(out), None, _ptr(attn.ws), ctypes.c_float(attn.scale),
                      ctypes.c_float(attn.eps))
         self.stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         self.layers = layers
@@ -178,11 +184,12 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     n = world
-    case = build_case(args.workload, dev, seed=0, paged=True, batch_scale=n, kv_shard=n,
-                      kv_rank=rank, layers=args.layers)
+    case = build_case(args.workload, dev, seed=0, paged=args.layout == "paged", batch_scale=n,
+                      kv_shard=n, kv_rank=rank, layers=args.layers)
     t = case.tensors
     B = case.B
-    attn = PagedDecodeAttention(B, case.nq, case.nkv, 128, dev)
+    cap = t["cache"].capacity if "cache" in t else t["k_cache"].shape[3]
+    attn = PagedDecodeAttention(B, case.nq, case.nkv, 128, dev, cap)
     out = torch.empty(B, case.nq * 128, dtype=torch.bfloat16, device=dev)
     gathered = torch.empty(n, B, case.nq * 128, dtype=torch.bfloat16, device=dev) if n > 1 else None
     launch = StepLauncher(case, attn, args.layers, out)
@@ -214,11 +221,13 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.profiler.start()       # ncu --profile-from-start off captures the timed region only
     ev0.record()
     for i in range(args.steps):
         step(i)
     ev1.record()
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
     clocks = sampler.stop()
     if dist is not None:
         dist.barrier()
@@ -250,7 +259,7 @@ def run_ours(args):
 
     e2e = None if args.no_e2e else run_e2e(args, case, attn, launch, out, gathered, dist, bytes_job)
     cpu = None
-    if n == 1 and rank == 0 and not args.no_cpu_baseline:
+    if n == 1 and rank == 0 and not args.no_cpu_baseline and args.layout == "paged":
         cpu = cpu_baseline(case, bytes_rank)
 
     line = {
@@ -264,7 +273,7 @@ def run_ours(args):
             "workload": f"{args.workload} per GPU" + (f", weak-scaled x{n}" if n > 1 else ""),
             "B": B, "keys_per_seq": (max(case.keys) if len(set(case.keys)) == 1 else "ragged"),
             "q_heads_per_gpu": case.nq, "kv_heads_per_gpu": case.nkv, "head_dim": 128,
-            "paged": True, "page_size": 16, "layers_rotated": args.layers,
+            "paged": args.layout == "paged", "page_size": 16, "layers_rotated": args.layers,
             "parallelism": f"kv-head shard x{n} + NCCL all-gather" if n > 1 else "single GPU",
             "l2": f"inputs larger than L2: {args.layers} layer caches of "
                   f"{bytes_rank / 1e6:.0f} MB read in rotation, one per step",
@@ -284,17 +293,23 @@ def run_ours(args):
 
 
 def run_e2e(args, case, attn, launch, out, gathered, dist, bytes_job):
-    """Same steps through host buffers: pinned H2D of qkv + pos, the step, D2H of the output."""
+    """Same steps through host buffers: one pinned H2D copy of the new token's qkv and positions,
+    the step, and a D2H copy of the (gathered) output."""
     t = case.tensors
-    qkv_h = t["qkv"].cpu().pin_memory()
-    pos_h = t["pos"].cpu().pin_memory()
+    qkv_b = t["qkv"].numel() * 2
+    host_in = torch.empty(qkv_b + t["pos"].numel() * 4, dtype=torch.uint8, pin_memory=True)
+    host_in[:qkv_b].view(torch.bfloat16).copy_(t["qkv"].reshape(-1).cpu())
+    host_in[qkv_b:].view(torch.int32).copy_(t["pos"].cpu())
+    dev_in = torch.empty_like(host_in, device=out.device)
+    qkv_d = dev_in[:qkv_b].view(torch.bfloat16).view(t["qkv"].shape)
+    pos_d = dev_in[qkv_b:].view(torch.int32)
+    e2e_launch = StepLauncher(case, attn, args.layers, out, qkv=qkv_d, pos=pos_d)
     res = gathered if gathered is not None else out
     out_h = torch.empty(res.shape, dtype=res.dtype, pin_memory=True)
 
     def step(i):
-        t["qkv"].copy_(qkv_h, non_blocking=True)
-        t["pos"].copy_(pos_h, non_blocking=True)
-        launch(i)
+        dev_in.copy_(host_in, non_blocking=True)
+        e2e_launch(i)
         if dist is not None:
             dist.all_gather_into_tensor(gathered, out)
         out_h.copy_(res, non_blocking=True)
@@ -313,8 +328,7 @@ def run_e2e(args, case, attn, launch, out, gathered, dist, bytes_job):
     ms = max_over_ranks(dist, e0.elapsed_time(e1)) / args.steps
     return {"value": round(bytes_job / (ms * 1e-3) / 1e12, 4), "unit": "TB/s",
             "us_per_call": round(ms * 1e3, 2),
-            "h2d_bytes_per_step": qkv_h.numel() * 2 + pos_h.numel() * 4,
-            "d2h_bytes_per_step": out_h.numel() * 2}
+            "h2d_bytes_per_step": host_in.numel(), "d2h_bytes_per_step": out_h.numel() * 2}
 
 
 # --------------------------------------------------------------------------- CPU reference

@@ -64,26 +64,32 @@ typedef struct kopt_kv_cache {
 } kopt_kv_cache;
 
 /* ---- launch plan -------------------------------------------------------------------------- *
- * Filled by kopt_decode_attn_plan for a fixed (B, T, nkv) and reused by every call, so the grid
- * and workspace stay fixed across CUDA-graph replays. The split of each sequence's keys into
- * units is decided on the device from the live lengths (pos[b] + T) at every call. */
+ * Filled by kopt_decode_attn_plan for a fixed (B, T, nkv, max_len) and reused by every call, so the
+ * grid and workspace stay fixed across CUDA-graph replays. How the keys are split between CTAs is
+ * decided on the device at every call from the live lengths (pos[b] + T): each (sequence, kv
+ * head) pair is cut into chunks of chunk_tokens keys; CTA c takes chunk c and then claims further
+ * chunks from a counter in the workspace, so faster SMs take more of them. */
 typedef struct kopt_plan {
   int32_t B;
   int32_t T;
   int32_t nkv;
-  int32_t grid;              /* CTAs launched: slots_per_head * nkv */
-  int32_t slots_per_head;    /* co-resident CTAs per kv head */
-  int32_t waves;             /* units per slot when one balanced wave does not fit */
-  int32_t max_units;         /* partial-result slots in the workspace */
+  int32_t grid;              /* CTAs launched: one wave, SM count x resident CTAs per SM */
+  int32_t ctas_per_sm;       /* resident CTAs per SM reported by the occupancy query */
+  int32_t tile_tokens;       /* keys per pipeline stage */
+  int32_t max_units;         /* partial-result slots in the workspace (chunks at max_len) */
   int32_t device;
+  int32_t max_len;           /* largest cache capacity (keys per sequence) a call may pass */
+  int32_t chunk_tokens;      /* keys per dynamically scheduled chunk */
   int64_t ws_bytes;          /* workspace bytes the caller must provide (zeroed once) */
 } kopt_plan;
 
-/* Plan a decode-attention launch: B sequences, T query tokens each (T == 1), nq = 4 * nkv query
- * heads of dim d == 128. target_ctas <= 0 lets the plan fill the device (SM count x resident
- * CTAs per SM). Replaces DecodeAttention.__init__ (engine/kernels/fused.py:209-219). */
-KOPT_API int kopt_decode_attn_plan(int device, int B, int T, int nq, int nkv, int d, int target_ctas,
-                          kopt_plan* plan);
+/* Plan a decode-attention launch: B sequences of at most max_len keys, T query tokens each
+ * (T == 1), nq = 4 * nkv query heads of dim d == 128. target_ctas <= 0 launches one CTA per
+ * resident slot (SM count x resident CTAs per SM); a positive value fixes the grid instead.
+ * Replaces DecodeAttention.__init__ (engine/kernels/fused.py:209-219), which also sizes its
+ * scratch from the capacity. */
+KOPT_API int kopt_decode_attn_plan(int device, int B, int T, int nq, int nkv, int d, int max_len,
+                                   int target_ctas, kopt_plan* plan);
 
 /* Zero a workspace of plan->ws_bytes bytes (split counters and the error word). Call once after
  * allocating it, and again after kopt_read_error reported a timeout. */

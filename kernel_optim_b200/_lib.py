@@ -63,10 +63,12 @@ class Plan(ctypes.Structure):
         ("T", ctypes.c_int32),
         ("nkv", ctypes.c_int32),
         ("grid", ctypes.c_int32),
-        ("slots_per_head", ctypes.c_int32),
-        ("waves", ctypes.c_int32),
+        ("ctas_per_sm", ctypes.c_int32),
+        ("tile_tokens", ctypes.c_int32),
         ("max_units", ctypes.c_int32),
         ("device", ctypes.c_int32),
+        ("max_len", ctypes.c_int32),
+        ("chunk_tokens", ctypes.c_int32),
         ("ws_bytes", ctypes.c_int64),
     ]
 
@@ -78,7 +80,8 @@ _vp, _i32, _i64, _f32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_
 _SIGS = {
     "kopt_abi_version": (_i32, []),
     "kopt_strerror": (ctypes.c_char_p, [_i32]),
-    "kopt_decode_attn_plan": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(Plan)]),
+    "kopt_decode_attn_plan": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                                     ctypes.POINTER(Plan)]),
     "kopt_workspace_init": (_i32, [ctypes.POINTER(Plan), _vp, _vp]),
     "kopt_read_error": (_i32, [ctypes.POINTER(Plan), _vp, ctypes.POINTER(ctypes.c_int), _vp]),
     "kopt_decode_attn": (_i32, [ctypes.POINTER(Plan), _vp, ctypes.POINTER(KvCache), _vp, _vp, _vp,

@@ -9,26 +9,34 @@
 //   _decode_combine_kernel (fused.py:188-201): LSE merge of the splits, bf16 output.
 //
 // How this file does it on B200:
-//   * One persistent-style grid of (co-resident CTAs) = slots_per_head * nkv CTAs. Every CTA plans
-//     the call on the device from the live lengths pos[b] + 1 (no empty splits, unlike the
-//     reference's capacity-sized NSPLIT, fused.py:211-214): if one balanced wave fits, each
-//     (sequence, kv head) gets floor(L_b * P / sum L) splits of equal length; otherwise units of a
-//     fixed chunk ~ sum L / (P * waves) are dealt round-robin to the CTAs.
-//   * Warp 4 is a producer: it streams 64-token K and V tiles (four 16-token pages, 4 KiB each)
-//     with cp.async.bulk global->shared copies into a 3-stage ring guarded by mbarriers (no TMA
-//     multicast anywhere). Warps 0-3 consume one 16-token page each per tile.
-//   * Consumers keep the 4 query rows of the group in registers (16 dims x 4 rows per lane), compute
-//     q.k with packed fp32 FMA (fma.rn.f32x2, Blackwell), reduce over 8 lanes with a shuffle
-//     reduce-scatter, run an fp32 online softmax (exp2 domain) and accumulate p.v with packed FMA.
+//   * One wave of one CTA per SM, balanced dynamically. Every CTA plans the call on the device from
+//     the live lengths pos[b] + 1 (never from the capacity, unlike fused.py:211-214): the keys of
+//     each (sequence, kv head) pair are cut into chunks of 32 pages (512 keys); CTA c takes chunk c,
+//     then claims further chunks from a global atomic counter, one chunk ahead so its copies never
+//     stop. An SM that the memory system serves faster simply takes more chunks. The last CTA to
+//     finish resets the counter; no CTA ever waits for another.
+//   * 8 warps; tile i of a unit is 128 keys = 8 pages and warp w owns page w of every tile. Each
+//     warp streams its own pages with tiled TMA (cp.async.bulk.tensor, 128-byte swizzle, no
+//     multicast) into a private 3-deep ring of shared-memory slots, each slot guarded by an
+//     mbarrier; the refill of a slot is issued as soon as the warp has consumed it, two tiles ahead
+//     and across unit boundaries. A page of one kv head arrives as two 16 x 64 boxes (dims 0-63,
+//     64-127) for K and two for V. No warp waits on another warp between unit boundaries.
+//   * Each warp consumes its page with mma.sync m16n8k16 (bf16 in, fp32
+//     accumulate): S = Q K^T with the 4 query rows of the group in the 16-row A tile, an fp32
+//     online softmax in the exp2 domain on the accumulator fragments (4-lane shuffles), then
+//     O += P V with P rounded to bf16 as the reference does (fused.py:179). Swizzled ldmatrix loads
+//     are bank-conflict free. The 12 idle rows of the A tile cost nothing: the path is HBM-bound.
 //   * The fused variant computes the QK-norm/RoPE prologue in the CTA, appends the new token's K/V
-//     to the cache from the CTA that owns position pos[b] and injects that token from shared memory.
+//     to the cache from the CTA that owns position pos[b] and folds that token in from shared
+//     memory (it is never read back from HBM).
 //   * Splits of one (sequence, kv head) are merged by the last CTA to finish (atomic counter, no
 //     waiting on other CTAs), so the reference's separate combine launch disappears.
 //   * Every mbarrier wait is bounded in time; on expiry the kernel records KOPT_DEV_ERR_TIMEOUT,
 //     stops issuing copies, waits (bounded) for copies in flight and runs to completion.
 
-#include <cuda_runtime.h>
+#include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "kopt.h"
@@ -36,14 +44,16 @@
 namespace kopt {
 
 constexpr int kD = 128;                 // head dim
+constexpr int kHalf = 64;               // dims per TMA box (128-byte rows for the 128B swizzle)
 constexpr int kGroup = 4;               // query heads per kv head
 constexpr int kPage = 16;               // tokens per page (and per consumer warp per tile)
-constexpr int kNW = 4;                  // consumer warps
+constexpr int kNW = 8;                  // consumer warps
 constexpr int kTile = kPage * kNW;      // tokens per pipeline stage
 constexpr int kStages = 3;
-constexpr int kThreads = (kNW + 1) * 32;
+constexpr int kThreads = kNW * 32;
 constexpr int kMaxB = 256;
-constexpr int kDefaultWaves = 4;
+constexpr int kBoxBytes = kPage * kHalf * 2;   // 2 KiB: one TMA box
+constexpr int kChunkPages = 32;                // dynamic scheduling granule: 512 keys of one pair
 constexpr unsigned long long kTimeoutNs = 1000000000ull;  // 1 s per mbarrier wait
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegBig = -1.0e30f;     // running-max seed (finite, as fused.py:164)
@@ -51,14 +61,16 @@ constexpr float kNegBig = -1.0e30f;     // running-max seed (finite, as fused.py
 typedef __nv_bfloat16 bf16;
 
 struct Params {
-  const bf16* q;         // [B*T, q_stride] (unfused)
+  CUtensorMap tmk;       // K cache: paged {128, pages*nkv*16} or contiguous {128, cap, nkv, B}
+  CUtensorMap tmv;       // V cache, same geometry
+  const bf16* q;         // [B*T, nq*128] (unfused)
   const bf16* qkv;       // [B, (nq + 2 nkv) * 128] (fused)
   const bf16* qw;        // q_norm weight [128]
   const bf16* kw;        // k_norm weight [128]
   const bf16* cos;       // [rope_len, 128]
   const bf16* sin;
   bf16* q_out;           // optional roped q [B, nq*128]
-  bf16* kc;              // cache K (layer base or page pool)
+  bf16* kc;              // cache K (layer base or page pool), for the appended row
   bf16* vc;
   long long sb, sh;      // contiguous strides (elements)
   const int* bt;         // block table or nullptr
@@ -67,35 +79,37 @@ struct Params {
   float* ws_o;           // [max_units, 4, 128]
   float2* ws_ml;         // [max_units, 4]
   int* ws_cnt;           // [B * nkv]
-  int* ws_err;
+  int* ws_err;           // error word; ws_err[1] = next dynamic chunk, ws_err[2] = CTAs done
   int bt_stride, num_pages, cap, rope_len;
   int B, T, nkv;
-  int slots_per_head, waves;
   float scale_log2, eps;
 };
 
-struct __align__(128) Smem {
-  bf16 k[kStages][kTile * kD];          // 3 x 16 KiB
-  bf16 v[kStages][kTile * kD];          // 3 x 16 KiB
+// One stage: [page 0..7][half 0..1][16 tokens x 64 dims] for K and for V. Every 2 KiB box starts
+// on a 1 KiB boundary, as the 128-byte swizzle pattern (16-byte chunk ^= row % 8) requires.
+struct __align__(1024) Smem {
+  bf16 k[kStages][kNW][2][kPage * kHalf];
+  bf16 v[kStages][kNW][2][kPage * kHalf];
   union {
-    float q[kGroup][kD];                // unit prologue: scaled q rows
+    bf16 q[kGroup][kD];                 // unit prologue: roped q rows (bf16, the reference's q)
     float o[kNW][kGroup][kD];           // unit epilogue: per-warp partial outputs
   } u;
   float red_m[kNW][kGroup];
   float red_l[kNW][kGroup];
-  float p[kNW][kPage][kGroup];
-  float alpha[kNW][kGroup];
   bf16 knew[kD];
   bf16 vnew[kD];
-  int prefix[kMaxB + 1];
-  int chunk[kMaxB];
-  int lens[kMaxB];
-  unsigned long long full[kStages];
-  unsigned long long empty[kStages];
-  int total_units;
+  int cstart[kMaxB + 1];                // first chunk of pair (b, kv head 0)
+  int npages[kMaxB];                    // pages streamed per (b, kv head)
+  int lens[kMaxB];                      // keys attended by sequence b
+  int ring[4];                          // the CTA's k-th claimed chunk in ring[k % 4] (-1: none)
+  unsigned long long full[kStages][kNW];   // per-warp ring: slot filled by this warp's TMA
+  int total_chunks;
+  volatile int nclaimed;                // ring entries 0 .. nclaimed-1 are valid
   int last_flag;
   volatile int abort;
 };
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + slack to align the base to 1 KiB
+static_assert(kSmemBytes <= 227 * 1024, "shared memory above the 227 KiB per-CTA limit");
 
 // ------------------------------------------------------------------------------- PTX helpers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -142,13 +156,21 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, Smem& s
     }
   }
 }
-// 1-D bulk copy global -> shared, completion counted on an mbarrier (no multicast).
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
-                                         uint64_t policy) {
+// Tiled TMA loads (no multicast), completion counted on an mbarrier in this CTA.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, "
-      "[%3], %4;" ::"r"(dst),
-      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            int z, int w, uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar), "l"(policy)
       : "memory");
 }
 __device__ __forceinline__ uint64_t evict_first_policy() {
@@ -159,6 +181,28 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
 __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D += A B, m16n8k16, bf16 inputs, fp32 accumulate, for rows 0-7 only: rows 8-15 of A are zero
+// (a1 = a3 = 0) and their results go to scratch outputs, so only d0/d1 stay live in registers.
+__device__ __forceinline__ void mma16816(float& d0, float& d1, uint32_t a0, uint32_t a2, uint32_t b0,
+                                         uint32_t b1) {
+  float x2, x3;
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%10, %11, %12, %13};"
+      : "=f"(d0), "=f"(d1), "=f"(x2), "=f"(x3)
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(d0), "f"(d1), "f"(0.f), "f"(0.f));
+}
 
 // bf16x2 word -> (low element, high element) as fp32; exact.
 __device__ __forceinline__ float2 bf2f(uint32_t w) {
@@ -166,6 +210,10 @@ __device__ __forceinline__ float2 bf2f(uint32_t w) {
 }
 __device__ __forceinline__ float bf16r(float x) {  // round to bf16 (RNE) and back
   return __bfloat162float(__float2bfloat16_rn(x));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
 }
 
 // ---------------------------------------------------------------- QK-norm + RoPE of one head
@@ -203,21 +251,21 @@ __device__ __forceinline__ void norm_rope_head(const bf16* __restrict__ src, con
 }
 
 __device__ __forceinline__ void store4_bf16(bf16* dst, const float y[4]) {
-  __nv_bfloat162 a = __floats2bfloat162_rn(y[0], y[1]);
-  __nv_bfloat162 b = __floats2bfloat162_rn(y[2], y[3]);
   uint2 u;
-  u.x = *reinterpret_cast<uint32_t*>(&a);
-  u.y = *reinterpret_cast<uint32_t*>(&b);
+  u.x = pack_bf16(y[0], y[1]);
+  u.y = pack_bf16(y[2], y[3]);
   *reinterpret_cast<uint2*>(dst) = u;
 }
 
 // ---------------------------------------------------------------------------- device plan
 __device__ __forceinline__ int ceil_div_i(int a, int b) { return (a + b - 1) / b; }
-__device__ __forceinline__ int round16(int a) { return (a + 15) & ~15; }
 
-// Warp 0 fills s.lens / s.chunk / s.prefix / s.total_units from pos[].
+// Warp 0 derives the chunk list from pos[]: sequence b streams Ls_b keys from the cache (all L_b
+// keys, or L_b - 1 when the fused prologue appends the last one itself) = max(1, ceil(Ls_b/16))
+// pages per kv head, cut into ceil(pages / 32) chunks; pair (b, kvh) owns chunks
+// [cstart[b] + kvh * nch_b, + nch_b).
+template <bool FUSED>
 __device__ void compute_plan(const Params& p, Smem& s, int lane) {
-  long long tot = 0;
   int err = 0;
   for (int b = lane; b < p.B; b += 32) {
     int L = p.pos[b] + p.T;
@@ -226,279 +274,357 @@ __device__ void compute_plan(const Params& p, Smem& s, int lane) {
       L = L < 1 ? 1 : p.cap;
     }
     s.lens[b] = L;
-    tot += L;
+    const int Ls = FUSED ? L - 1 : L;
+    s.npages[b] = Ls > 0 ? ceil_div_i(Ls, kPage) : 1;
   }
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, off);
   if (err && blockIdx.x == 0) atomicOr(p.ws_err, err);
-  const int P = p.slots_per_head;
-  // Candidate 1: one balanced wave.
-  int sum1 = 0, maxc = 0;
-  for (int b = lane; b < p.B; b += 32) {
-    const int L = s.lens[b];
-    int n = static_cast<int>((static_cast<long long>(L) * P) / tot);
-    n = n < 1 ? 1 : n;
-    const int c = round16(ceil_div_i(L, n));
-    n = ceil_div_i(L, c);
-    s.chunk[b] = c;
-    s.prefix[b + 1] = n;
-    sum1 += n;
-    maxc = maxc > c ? maxc : c;
-  }
-  sum1 = __reduce_add_sync(0xffffffffu, sum1);
-  maxc = __reduce_max_sync(0xffffffffu, maxc);
-  const bool one_wave =
-      sum1 <= P && static_cast<long long>(maxc) * sum1 * 4 <= tot * 5 + 64ll * sum1;
-  if (!one_wave) {
-    const long long per = static_cast<long long>(P) * p.waves;
-    long long C = (tot + per - 1) / per;
-    if (C > p.cap) C = p.cap;
-    const int c = round16(static_cast<int>(C));
-    for (int b = lane; b < p.B; b += 32) {
-      s.chunk[b] = c;
-      s.prefix[b + 1] = ceil_div_i(s.lens[b], c);
-    }
-  }
   __syncwarp();
   int carry = 0;
   for (int base = 0; base < p.B; base += 32) {
     const int b = base + lane;
-    const int n = b < p.B ? s.prefix[b + 1] : 0;
+    const int n = b < p.B ? ceil_div_i(s.npages[b], kChunkPages) * p.nkv : 0;
     int incl = n;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const int t = __shfl_up_sync(0xffffffffu, incl, off);
       if (lane >= off) incl += t;
     }
-    if (b < p.B) s.prefix[b + 1] = carry + incl;
+    if (b < p.B) s.cstart[b + 1] = carry + incl;
     carry += __shfl_sync(0xffffffffu, incl, 31);
   }
   if (lane == 0) {
-    s.prefix[0] = 0;
-    s.total_units = carry * p.nkv;
+    s.cstart[0] = 0;
+    s.total_chunks = carry;
   }
 }
 
 struct Unit {
-  int b, kvh, j, n, t0, t1, L;
+  int b, kvh, q;      // sequence, kv head, pair index b * nkv + kvh
+  int t0, t1;         // keys streamed from the cache: [t0, t1)
+  int L;              // keys attended by the sequence
+  int g;              // chunk index = workspace slot of this unit's partial result
+  int c0, n;          // the pair's chunks: c0 .. c0 + n - 1
+  bool last;          // last chunk of the pair (owns the appended token in the fused path)
 };
 
-__device__ __forceinline__ Unit unit_of(int u, const Params& p, const Smem& s) {
-  Unit r;
-  r.kvh = u % p.nkv;
-  const int v = u / p.nkv;
-  int lo = 0, hi = p.B;
+template <bool FUSED>
+__device__ __forceinline__ Unit chunk_unit(const Params& p, const Smem& s, int g) {
+  int lo = 0, hi = p.B;   // largest b with cstart[b] <= g
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (s.prefix[mid] <= v) lo = mid; else hi = mid;
+    if (s.cstart[mid] <= g) lo = mid; else hi = mid;
   }
-  r.b = lo;
-  r.j = v - s.prefix[lo];
-  r.n = s.prefix[lo + 1] - s.prefix[lo];
-  r.L = s.lens[lo];
-  const int c = s.chunk[lo];
-  r.t0 = r.j * c;
-  r.t1 = min(r.L, r.t0 + c);
-  return r;
+  Unit U;
+  const int b = lo, np = s.npages[b], nch = ceil_div_i(np, kChunkPages);
+  const int r = g - s.cstart[b];
+  const int kvh = r / nch, j = r % nch;
+  U.b = b;
+  U.kvh = kvh;
+  U.q = b * p.nkv + kvh;
+  U.L = s.lens[b];
+  const int Ls = FUSED ? U.L - 1 : U.L;
+  U.t0 = j * kChunkPages * kPage;
+  U.t1 = max(U.t0, min((j + 1) * kChunkPages * kPage, Ls));
+  U.g = g;
+  U.c0 = s.cstart[b] + kvh * nch;
+  U.n = nch;
+  U.last = j == nch - 1;
+  return U;
 }
 
-// Address (elements) of token t's row for (b, kvh); -1 when the page id is out of range.
-template <bool PAGED>
+// Claim the next chunk for this CTA (thread 0 only): chunk index or -1 when none are left.
+__device__ __forceinline__ int claim_chunk(const Params& p, int total) {
+  const int g = static_cast<int>(gridDim.x) + atomicAdd(p.ws_err + 1, 1);
+  return g < total ? g : -1;
+}
+
+// Element offset of token t's row of (b, kvh) in the cache, or -1 for a page id out of range.
 __device__ __forceinline__ long long row_offset(const Params& p, int b, int kvh, int t) {
-  if (PAGED) {
+  if (p.bt != nullptr) {
     const int pid = p.bt[static_cast<long long>(b) * p.bt_stride + t / kPage];
     if (pid < 0 || pid >= p.num_pages) return -1;
     return ((static_cast<long long>(pid) * p.nkv + kvh) * kPage + (t % kPage)) * kD;
-  } else {
-    return static_cast<long long>(b) * p.sb + static_cast<long long>(kvh) * p.sh +
-           static_cast<long long>(t) * kD;
+  }
+  return static_cast<long long>(b) * p.sb + static_cast<long long>(kvh) * p.sh +
+         static_cast<long long>(t) * kD;
+}
+
+// ---------------------------------------------------------------- consumer: one 16-token page
+// Fragment layout (m16n8k16): lane l holds rows r = l/4 and r + 8, columns 2(l%4), 2(l%4)+1.
+// Only rows 0-3 (the GQA group's query heads) are live, i.e. lanes 0-15 in c0/c1; the rest of
+// the tile is zero and its results are ignored.
+struct WarpState {
+  float o[16][2];   // O[row l/4][8j + 2(l%4) + {0,1}]
+  float m;          // running max of row l/4 (exp2 domain)
+  float l;          // this lane's partial softmax denominator
+};
+
+__device__ __forceinline__ void page_step(uint32_t kbase, uint32_t vbase, int ntok,
+                                          const uint32_t (&qa)[8][2], float scale_log2,
+                                          WarpState& st, int lane) {
+  const int mi = lane >> 3, ri = lane & 7;
+  // ---- S = Q K^T over this page's 16 tokens: two n-blocks (tokens 0-7, 8-15), 8 k-steps.
+  float s0a[2] = {0.f, 0.f}, s0b[2] = {0.f, 0.f};
+  float s1a[2] = {0.f, 0.f}, s1b[2] = {0.f, 0.f};
+  {
+    // ldmatrix.x4 matrices: (tokens 0-7, chunk c), (0-7, c+1), (8-15, c), (8-15, c+1)
+    const int tok = 8 * (mi >> 1) + ri;
+    const uint32_t row = kbase + tok * 128;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int h = ks >> 2, c = 2 * (ks & 3) + (mi & 1);
+      uint32_t b00, b01, b10, b11;
+      ldsm_x4(row + h * kBoxBytes + ((c ^ ri) << 4), b00, b01, b10, b11);
+      if (ks & 1) {
+        mma16816(s0b[0], s0b[1], qa[ks][0], qa[ks][1], b00, b01);
+        mma16816(s1b[0], s1b[1], qa[ks][0], qa[ks][1], b10, b11);
+      } else {
+        mma16816(s0a[0], s0a[1], qa[ks][0], qa[ks][1], b00, b01);
+        mma16816(s1a[0], s1a[1], qa[ks][0], qa[ks][1], b10, b11);
+      }
+    }
+  }
+  const int t0 = 2 * (lane & 3);
+  float sv[4];
+  sv[0] = (t0 < ntok) ? (s0a[0] + s0b[0]) * scale_log2 : -INFINITY;
+  sv[1] = (t0 + 1 < ntok) ? (s0a[1] + s0b[1]) * scale_log2 : -INFINITY;
+  sv[2] = (t0 + 8 < ntok) ? (s1a[0] + s1b[0]) * scale_log2 : -INFINITY;
+  sv[3] = (t0 + 9 < ntok) ? (s1a[1] + s1b[1]) * scale_log2 : -INFINITY;
+  // ---- online softmax of row lane/4 (4 lanes share a row)
+  float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  const float m_new = fmaxf(st.m, mx);
+  const float alpha = exp2f(st.m - m_new);
+  float pr[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) pr[i] = exp2f(sv[i] - m_new);
+  st.l = st.l * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
+  st.m = m_new;
+  if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      st.o[j][0] *= alpha;
+      st.o[j][1] *= alpha;
+    }
+  }
+  const uint32_t pa0 = pack_bf16(pr[0], pr[1]);   // P[row][t0, t0+1]      (k 0-7)
+  const uint32_t pa2 = pack_bf16(pr[2], pr[3]);   // P[row][t0+8, t0+9]    (k 8-15)
+  // ---- rows past the live tokens may hold anything: zero them so 0 * V stays 0
+  if (ntok < kPage) {
+    for (int idx = lane; idx < (kPage - ntok) * 16; idx += 32) {
+      const int r = ntok + (idx >> 4), part = idx & 15;   // 16 chunks of 16 B per row (2 boxes)
+      const uint32_t a = vbase + (part >> 3) * kBoxBytes + r * 128 + ((part & 7) << 4);
+      asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+    }
+    __syncwarp();
+  }
+  // ---- O += P V: 16 n-blocks of 8 dims, k = the page's 16 tokens
+  {
+    // ldmatrix.x4.trans matrices: (tokens 0-7, chunk j), (8-15, j), (0-7, j+1), (8-15, j+1)
+    const int tok = 8 * (mi & 1) + ri;
+    const uint32_t row = vbase + tok * 128;
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      const int c = j + (mi >> 1);
+      uint32_t b0a, b1a, b0b, b1b;
+      ldsm_x4_t(row + (c >> 3) * kBoxBytes + (((c & 7) ^ ri) << 4), b0a, b1a, b0b, b1b);
+      mma16816(st.o[j][0], st.o[j][1], pa0, pa2, b0a, b1a);
+      mma16816(st.o[j + 1][0], st.o[j + 1][1], pa0, pa2, b0b, b1b);
+    }
   }
 }
 
-// ------------------------------------------------------------------- consumer: one 16-token slab
-// ks/vs: up to 16 rows of 128 bf16 in shared memory. Lane layout for q.k: ts = lane/8 picks the
-// token within a group of 4, ds = lane%8 the 16 dims {8ds..8ds+7, 64+8ds..64+8ds+7}. For p.v the
-// lane owns dims 4*lane..4*lane+3 of all 4 rows.
-__device__ __forceinline__ void slab(const bf16* __restrict__ ks, const bf16* __restrict__ vs, int ntok,
-                                     const float2 (&qa)[kGroup][4], const float2 (&qb)[kGroup][4],
-                                     float& m_row, float& l_part, float2 (&o2)[kGroup][2],
-                                     float* __restrict__ p_s, float* __restrict__ alpha_s, int lane) {
-  const int ts = lane >> 3, ds = lane & 7;
-  const bool hi4 = (ds & 4) != 0, hi2 = (ds & 2) != 0;
-  float sc[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int t = ts + 4 * k;
-    uint4 ka = make_uint4(0, 0, 0, 0), kb = make_uint4(0, 0, 0, 0);
-    if (t < ntok) {
-      ka = *reinterpret_cast<const uint4*>(ks + t * kD + ds * 8);
-      kb = *reinterpret_cast<const uint4*>(ks + t * kD + 64 + ds * 8);
-    }
-    const uint32_t kw[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
-    float2 acc[kGroup];
-#pragma unroll
-    for (int r = 0; r < kGroup; ++r) acc[r] = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 kf = bf2f(kw[i]);
-#pragma unroll
-      for (int r = 0; r < kGroup; ++r) acc[r] = __ffma2_rn(qa[r][i], kf, acc[r]);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 kf = bf2f(kw[4 + i]);
-#pragma unroll
-      for (int r = 0; r < kGroup; ++r) acc[r] = __ffma2_rn(qb[r][i], kf, acc[r]);
-    }
-    float a[kGroup];
-#pragma unroll
-    for (int r = 0; r < kGroup; ++r) a[r] = acc[r].x + acc[r].y;
-    // reduce-scatter over the 8 ds lanes: rows {0,1}|{2,3} by bit 2, then one row by bit 1
-    float keep0 = hi4 ? a[2] : a[0], keep1 = hi4 ? a[3] : a[1];
-    const float send0 = hi4 ? a[0] : a[2], send1 = hi4 ? a[1] : a[3];
-    keep0 += __shfl_xor_sync(0xffffffffu, send0, 4);
-    keep1 += __shfl_xor_sync(0xffffffffu, send1, 4);
-    float keep = hi2 ? keep1 : keep0;
-    const float send = hi2 ? keep0 : keep1;
-    keep += __shfl_xor_sync(0xffffffffu, send, 2);
-    keep += __shfl_xor_sync(0xffffffffu, keep, 1);
-    sc[k] = t < ntok ? keep : -INFINITY;  // row ds>>1, token ts + 4k
-  }
-  // online softmax for this lane's row over the slab (16 tokens live in the 4 ts lane groups)
-  float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-  const float m_new = fmaxf(m_row, mx);
-  const float alpha = exp2f(m_row - m_new);
-  float pr[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) pr[k] = exp2f(sc[k] - m_new);
-  l_part = l_part * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
-  m_row = m_new;
-  if ((ds & 1) == 0) {
-    const int row = ds >> 1;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) p_s[(ts + 4 * k) * kGroup + row] = pr[k];
-    if (ts == 0) alpha_s[row] = alpha;
-  }
-  __syncwarp();
-  const float4 al = *reinterpret_cast<const float4*>(alpha_s);
-  const float alv[4] = {al.x, al.y, al.z, al.w};
+// The appended token of the fused path, folded into warp 0's state on CUDA cores.
+__device__ __forceinline__ void inject_token(const Smem& s, float scale_log2, WarpState& st,
+                                             int lane) {
+  // s_r = q_r . k_new for the 4 rows; lane covers dims 4*lane .. 4*lane+3
+  const uint2 kr = *reinterpret_cast<const uint2*>(&s.knew[4 * lane]);
+  const float2 k01 = bf2f(kr.x), k23 = bf2f(kr.y);
+  float dot[kGroup];
 #pragma unroll
   for (int r = 0; r < kGroup; ++r) {
-    const float2 a2 = make_float2(alv[r], alv[r]);
-    o2[r][0] = __fmul2_rn(o2[r][0], a2);
-    o2[r][1] = __fmul2_rn(o2[r][1], a2);
+    const uint2 qr = *reinterpret_cast<const uint2*>(&s.u.q[r][4 * lane]);
+    const float2 q01 = bf2f(qr.x), q23 = bf2f(qr.y);
+    dot[r] = q01.x * k01.x + q01.y * k01.y + q23.x * k23.x + q23.y * k23.y;
   }
-  auto pv = [&](int t) {
-    const float4 pp = *reinterpret_cast<const float4*>(p_s + t * kGroup);
-    const uint2 vw = *reinterpret_cast<const uint2*>(vs + t * kD + lane * 4);
-    const float2 v01 = bf2f(vw.x), v23 = bf2f(vw.y);
-    const float pv4[4] = {pp.x, pp.y, pp.z, pp.w};
 #pragma unroll
-    for (int r = 0; r < kGroup; ++r) {
-      const float2 p2 = make_float2(pv4[r], pv4[r]);
-      o2[r][0] = __ffma2_rn(p2, v01, o2[r][0]);
-      o2[r][1] = __ffma2_rn(p2, v23, o2[r][1]);
-    }
-  };
-  if (ntok == kPage) {
+  for (int off = 16; off >= 1; off >>= 1)
 #pragma unroll
-    for (int t = 0; t < kPage; ++t) pv(t);
-  } else {
-    for (int t = 0; t < ntok; ++t) pv(t);
+    for (int r = 0; r < kGroup; ++r) dot[r] += __shfl_xor_sync(0xffffffffu, dot[r], off);
+  const int row = (lane >> 2) & 3;
+  const float sc = (row == 0 ? dot[0] : row == 1 ? dot[1] : row == 2 ? dot[2] : dot[3]) * scale_log2;
+  const float m_new = fmaxf(st.m, sc);
+  const float alpha = exp2f(st.m - m_new);
+  const float pr = bf16r(exp2f(sc - m_new));
+  st.l = st.l * alpha + ((lane & 3) == 0 ? pr : 0.f);
+  st.m = m_new;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float2 vv = bf2f(*reinterpret_cast<const uint32_t*>(&s.vnew[8 * j + 2 * (lane & 3)]));
+    st.o[j][0] = st.o[j][0] * alpha + pr * vv.x;
+    st.o[j][1] = st.o[j][1] * alpha + pr * vv.y;
   }
-  __syncwarp();
 }
 
 // ------------------------------------------------------------------------------- main kernel
+// Issue side of a warp's private pipeline: walks the CTA's claimed chunks in order and yields the
+// tiles in which this warp owns a page (page w of tile i = keys t0 + 128 i + 16 w ...).
 template <bool PAGED, bool FUSED>
-__global__ void __launch_bounds__(kThreads, 2) decode_attn_kernel(const Params p) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>(smem_raw);
+struct Issuer {
+  int k;              // next ring index to open
+  Unit U;
+  int ti, ntiles;     // current tile within U
+  int npg;            // pages streamed by U
+  const int* bt_row;  // block-table row of U, from U's first page
+  int win, win_next, win_base;  // page ids of this warp's pages of tiles win_base + lane
+
+  __device__ __forceinline__ void open_window(int warp, int lane, int base) {
+    win_base = base;
+    const int a = 8 * (base + lane) + warp, b = 8 * (base + 32 + lane) + warp;
+    win = a < npg ? bt_row[a] : 0;
+    win_next = b < npg ? bt_row[b] : 0;
+  }
+  // Advance to the next tile with a page of this warp: 1 = found, 0 = the next chunk is not
+  // claimed yet (retry later), -1 = no chunks left.
+  __device__ __forceinline__ int next(const Params& p, const Smem& s, int warp, int lane) {
+    while (true) {
+      ++ti;
+      while (ti >= ntiles) {
+        if (k >= s.nclaimed) return 0;
+        __threadfence_block();   // pairs with the fence between the ring write and nclaimed
+        const int g = const_cast<const volatile int*>(s.ring)[k & 3];
+        if (g < 0) return -1;
+        ++k;
+        U = chunk_unit<FUSED>(p, s, g);
+        ntiles = ceil_div_i(U.t1 - U.t0, kTile);
+        npg = ceil_div_i(U.t1 - U.t0, kPage);
+        ti = 0;
+        if (PAGED && ntiles > 0) {
+          bt_row = p.bt + static_cast<long long>(U.b) * p.bt_stride + U.t0 / kPage;
+          open_window(warp, lane, 0);
+        }
+      }
+      if (U.t0 + ti * kTile + warp * kPage < U.t1) return 1;
+    }
+  }
+  // TMA of this warp's page of the current tile into ring slot `slot` (lane 0 issues).
+  __device__ __forceinline__ void issue(const Params& p, Smem& s, int slot, int warp, int lane,
+                                        uint64_t pol) {
+    int row = 0;
+    bool ok = true;
+    if (PAGED) {
+      if (ti >= win_base + 32) {   // window exhausted: move on, prefetch the one after
+        win = win_next;
+        win_base += 32;
+        const int b = 8 * (win_base + 32 + lane) + warp;
+        win_next = b < npg ? bt_row[b] : 0;
+      }
+      const int pid = __shfl_sync(0xffffffffu, win, ti - win_base);
+      if (pid < 0 || pid >= p.num_pages) {
+        ok = false;
+      } else {
+        row = (pid * p.nkv + U.kvh) * kPage;
+      }
+    }
+    if (lane == 0) {
+      const uint32_t fb = smem_u32(&s.full[slot][warp]);
+      if (!ok) {
+        atomicOr(p.ws_err, KOPT_DEV_ERR_PAGE);
+        mbar_arrive_expect_tx(fb, 0);   // completes the phase without data
+        return;
+      }
+      // order this warp's earlier generic reads/writes of the slot before the async-proxy refill
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive_expect_tx(fb, 4u * kBoxBytes);
+      const int tq = U.t0 + ti * kTile + warp * kPage;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t dk = smem_u32(&s.k[slot][warp][h][0]);
+        const uint32_t dv = smem_u32(&s.v[slot][warp][h][0]);
+        if (PAGED) {
+          tma_load_2d(dk, &p.tmk, h * kHalf, row, fb, pol);
+          tma_load_2d(dv, &p.tmv, h * kHalf, row, fb, pol);
+        } else {
+          tma_load_4d(dk, &p.tmk, h * kHalf, tq, U.kvh, U.b, fb, pol);
+          tma_load_4d(dv, &p.tmv, h * kHalf, tq, U.kvh, U.b, fb, pol);
+        }
+      }
+    }
+  }
+};
+
+template <bool PAGED, bool FUSED>
+__global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_constant__ Params p) {
+  extern __shared__ unsigned char smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                     ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = p.nkv * kGroup;
 
-  if (warp == 0) compute_plan(p, s, lane);
+  if (warp == 0) compute_plan<FUSED>(p, s, lane);
   if (threadIdx.x == 32) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(smem_u32(&s.full[i]), 1);
-      mbar_init(smem_u32(&s.empty[i]), kNW);
-    }
+    for (int i = 0; i < kStages; ++i)
+      for (int w = 0; w < kNW; ++w) mbar_init(smem_u32(&s.full[i][w]), 1);
     s.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  __syncthreads();
-  const int total_units = s.total_units;
-
-  if (warp == kNW) {
-    // ------------------------------------------------------------------ producer warp
-    const uint64_t pol = evict_first_policy();
-    int it = 0;
-    bool stop = false;
-    for (int u = blockIdx.x; u < total_units && !stop; u += gridDim.x) {
-      const Unit U = unit_of(u, p, s);
-      const bool inject = FUSED && U.t1 == U.L;
-      const int se = inject ? U.L - 1 : U.t1;  // end of the keys streamed from the cache
-      const int ntiles = ceil_div_i(se - U.t0, kTile);
-      for (int i = 0; i < ntiles; ++i, ++it) {
-        const int stage = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        const int tq = U.t0 + i * kTile + lane * kPage;
-        int nt = lane < kNW ? min(max(se - tq, 0), kPage) : 0;
-        long long off = 0;
-        if (nt > 0) {
-          off = row_offset<PAGED>(p, U.b, U.kvh, tq);
-          if (off < 0) {
-            atomicOr(p.ws_err, KOPT_DEV_ERR_PAGE);
-            nt = 0;
-          }
-        }
-        const uint32_t bytes = static_cast<uint32_t>(nt) * kD * 2;
-        const uint32_t total = __reduce_add_sync(0xffffffffu, bytes) * 2;
-        int ok = 1;
-        if (lane == 0) {
-          ok = mbar_wait(smem_u32(&s.empty[stage]), ph ^ 1, s, p.ws_err, true);
-          if (ok) mbar_arrive_expect_tx(smem_u32(&s.full[stage]), total);
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) {
-          stop = true;
-          break;
-        }
-        if (nt > 0) {
-          const uint32_t fb = smem_u32(&s.full[stage]);
-          bulk_g2s(smem_u32(&s.k[stage][lane * kPage * kD]), p.kc + off, bytes, fb, pol);
-          bulk_g2s(smem_u32(&s.v[stage][lane * kPage * kD]), p.vc + off, bytes, fb, pol);
-        }
-      }
-    }
-    // Drain: wait (bounded, ignoring abort) for the copies still in flight into this CTA.
-    if (lane == 0) {
-      for (int k = 1; k <= kStages && k <= it; ++k) {
-        const int i2 = it - k;
-        mbar_wait(smem_u32(&s.full[i2 % kStages]), (i2 / kStages) & 1, s, p.ws_err, false);
-      }
-    }
-    return;
+  if (threadIdx.x == 64) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmk) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmv) : "memory");
   }
+  __syncwarp();
+  if (threadIdx.x == 0) {   // first chunk static, the next one claimed
+    const int total = s.total_chunks;
+    const int g0 = static_cast<int>(blockIdx.x) < total ? static_cast<int>(blockIdx.x) : -1;
+    s.ring[0] = g0;
+    s.ring[1] = g0 >= 0 ? claim_chunk(p, total) : -1;
+    s.nclaimed = 2;
+  }
+  __syncthreads();
+  const uint64_t pol = evict_first_policy();
 
-  // -------------------------------------------------------------------- consumer warps
-  const int ctid = threadIdx.x;  // 0..127
-  int it = 0;
-  float* p_s = &s.p[warp][0][0];
-  float* alpha_s = &s.alpha[warp][0];
-  for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
-    const Unit U = unit_of(u, p, s);
-    const bool inject = FUSED && U.t1 == U.L;
-    const int se = inject ? U.L - 1 : U.t1;
+  // This warp's ring: `state` tells whether the issue cursor stands on an unissued tile.
+  Issuer<PAGED, FUSED> iss;
+  iss.k = 0;
+  iss.ti = 0;
+  iss.ntiles = 0;
+  iss.npg = 0;
+  iss.bt_row = nullptr;
+  iss.win = iss.win_next = iss.win_base = 0;
+  int state = iss.next(p, s, warp, lane);
+  int issued = 0, consumed = 0;
+  auto pump = [&]() {
+    while (issued - consumed < kStages && !s.abort) {
+      if (state == 0) state = iss.next(p, s, warp, lane);
+      if (state != 1) break;
+      iss.issue(p, s, issued % kStages, warp, lane, pol);
+      ++issued;
+      state = iss.next(p, s, warp, lane);
+    }
+  };
+  pump();
+
+  const int ctid = threadIdx.x;
+  for (int kc = 0;; ++kc) {
+    const int g = const_cast<const volatile int*>(s.ring)[kc & 3];
+    if (g < 0) break;
+    // keep one chunk claimed ahead (thread 0; published by the prologue barrier below)
+    if (ctid == 0 && kc >= 1 && s.ring[kc & 3] >= 0) {
+      s.ring[(kc + 1) & 3] = claim_chunk(p, s.total_chunks);
+      __threadfence_block();
+      s.nclaimed = kc + 2;
+    }
+    const Unit U = chunk_unit<FUSED>(p, s, g);
+    const bool inject = FUSED && U.last;
+    const int se = U.t1;                          // keys streamed from the cache end here
     const int ntiles = ceil_div_i(se - U.t0, kTile);
-    const int qh = U.kvh * kGroup + warp;  // this warp's query head in the prologue
+    const int qh = U.kvh * kGroup + (warp & 3);  // query head computed by warps 0-3
 
     // ---- prologue: q rows (and the new K/V for the CTA owning position L-1)
     if (FUSED) {
-      const int row = (nq + 2 * p.nkv) * kD;
-      const bf16* src = p.qkv + static_cast<long long>(U.b) * row;
+      const int rowlen = (nq + 2 * p.nkv) * kD;
+      const bf16* src = p.qkv + static_cast<long long>(U.b) * rowlen;
       int rp = U.L - 1;
       if (rp >= p.rope_len) {
         if (lane == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_ROPE);
@@ -507,14 +633,14 @@ __global__ void __launch_bounds__(kThreads, 2) decode_attn_kernel(const Params p
       const bf16* cs = p.cos + static_cast<long long>(rp) * kD;
       const bf16* sn = p.sin + static_cast<long long>(rp) * kD;
       float y[4];
-      norm_rope_head(src + qh * kD, p.qw, cs, sn, p.eps, lane, y);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) s.u.q[warp][4 * lane + j] = y[j] * p.scale_log2;
-      if (p.q_out != nullptr && U.j == 0)
-        store4_bf16(p.q_out + static_cast<long long>(U.b) * nq * kD + qh * kD + 4 * lane, y);
-      if (inject && warp < 2) {
-        const long long off = row_offset<PAGED>(p, U.b, U.kvh, U.L - 1);
-        if (warp == 0) {
+      if (warp < kGroup) {
+        norm_rope_head(src + qh * kD, p.qw, cs, sn, p.eps, lane, y);
+        store4_bf16(&s.u.q[warp][4 * lane], y);
+        if (p.q_out != nullptr && U.t0 == 0)
+          store4_bf16(p.q_out + static_cast<long long>(U.b) * nq * kD + qh * kD + 4 * lane, y);
+      } else if (inject && warp < kGroup + 2) {
+        const long long off = row_offset(p, U.b, U.kvh, U.L - 1);
+        if (warp == kGroup) {
           norm_rope_head(src + (nq + U.kvh) * kD, p.kw, cs, sn, p.eps, lane, y);
           store4_bf16(&s.knew[4 * lane], y);
           if (off >= 0) store4_bf16(p.kc + off + 4 * lane, y);
@@ -526,128 +652,135 @@ __global__ void __launch_bounds__(kThreads, 2) decode_attn_kernel(const Params p
         }
         if (off < 0 && lane == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_PAGE);
       }
-    } else {
+    } else if (warp < kGroup) {
       const bf16* src = p.q + static_cast<long long>(U.b) * p.T * nq * kD + qh * kD;
-      const uint2 raw = *reinterpret_cast<const uint2*>(src + 4 * lane);
-      const float2 a = bf2f(raw.x), b = bf2f(raw.y);
-      s.u.q[warp][4 * lane + 0] = a.x * p.scale_log2;
-      s.u.q[warp][4 * lane + 1] = a.y * p.scale_log2;
-      s.u.q[warp][4 * lane + 2] = b.x * p.scale_log2;
-      s.u.q[warp][4 * lane + 3] = b.y * p.scale_log2;
+      *reinterpret_cast<uint2*>(&s.u.q[warp][4 * lane]) =
+          *reinterpret_cast<const uint2*>(src + 4 * lane);
     }
     named_bar(1, kNW * 32);
-    float2 qa[kGroup][4], qb[kGroup][4];
+    pump();   // the chunk claimed above is visible now
+    // A fragments of Q (rows 0-3 live on lanes 0-15): a0 = Q[r][16ks + 2(l%4) + {0,1}], a2 = +8
+    uint32_t qa[8][2];
     {
-      const int ds = lane & 7;
+      const int r = lane >> 2, c = 2 * (lane & 3);
 #pragma unroll
-      for (int r = 0; r < kGroup; ++r) {
-        const float4 a0 = *reinterpret_cast<const float4*>(&s.u.q[r][ds * 8]);
-        const float4 a1 = *reinterpret_cast<const float4*>(&s.u.q[r][ds * 8 + 4]);
-        const float4 b0 = *reinterpret_cast<const float4*>(&s.u.q[r][64 + ds * 8]);
-        const float4 b1 = *reinterpret_cast<const float4*>(&s.u.q[r][64 + ds * 8 + 4]);
-        qa[r][0] = make_float2(a0.x, a0.y); qa[r][1] = make_float2(a0.z, a0.w);
-        qa[r][2] = make_float2(a1.x, a1.y); qa[r][3] = make_float2(a1.z, a1.w);
-        qb[r][0] = make_float2(b0.x, b0.y); qb[r][1] = make_float2(b0.z, b0.w);
-        qb[r][2] = make_float2(b1.x, b1.y); qb[r][3] = make_float2(b1.z, b1.w);
+      for (int ks = 0; ks < 8; ++ks) {
+        qa[ks][0] = lane < 16 ? *reinterpret_cast<const uint32_t*>(&s.u.q[r & 3][16 * ks + c]) : 0u;
+        qa[ks][1] = lane < 16 ? *reinterpret_cast<const uint32_t*>(&s.u.q[r & 3][16 * ks + 8 + c]) : 0u;
       }
     }
     named_bar(1, kNW * 32);
 
-    float m_row = kNegBig, l_part = 0.f;
-    float2 o2[kGroup][2];
+    WarpState st;
+    st.m = kNegBig;
+    st.l = 0.f;
 #pragma unroll
-    for (int r = 0; r < kGroup; ++r) o2[r][0] = o2[r][1] = make_float2(0.f, 0.f);
+    for (int j = 0; j < 16; ++j) st.o[j][0] = st.o[j][1] = 0.f;
 
-    for (int i = 0; i < ntiles; ++i, ++it) {
-      const int stage = it % kStages;
-      const uint32_t ph = (it / kStages) & 1;
-      mbar_wait(smem_u32(&s.full[stage]), ph, s, p.ws_err, true);
-      const int tv = min(se - (U.t0 + i * kTile), kTile);
-      const int ntok = min(max(tv - warp * kPage, 0), kPage);
-      if (ntok > 0)
-        slab(&s.k[stage][warp * kPage * kD], &s.v[stage][warp * kPage * kD], ntok, qa, qb, m_row,
-             l_part, o2, p_s, alpha_s, lane);
+    for (int i = 0; i < ntiles; ++i) {
+      const int ntok = min(max(se - (U.t0 + i * kTile + warp * kPage), 0), kPage);
+      if (ntok == 0) continue;          // no page of this warp in this tile
+      if (issued == consumed) pump();   // this tile's copy must be in flight before waiting
+      const int slot = consumed % kStages;
+      mbar_wait(smem_u32(&s.full[slot][warp]), (consumed / kStages) & 1, s, p.ws_err, true);
+      page_step(smem_u32(&s.k[slot][warp][0][0]), smem_u32(&s.v[slot][warp][0][0]), ntok, qa,
+                p.scale_log2, st, lane);
+      ++consumed;
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&s.empty[stage]));
+      pump();                           // refill the slot just consumed
     }
-    if (inject && warp == 0)
-      slab(s.knew, s.vnew, 1, qa, qb, m_row, l_part, o2, p_s, alpha_s, lane);
+    if (inject && warp == 0) inject_token(s, p.scale_log2, st, lane);
 
     // ---- epilogue: merge the 4 warps, then the splits of this (b, kvh)
-    float l = l_part;
-    l += __shfl_xor_sync(0xffffffffu, l, 8);
-    l += __shfl_xor_sync(0xffffffffu, l, 16);
+    float l = st.l;
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    named_bar(1, kNW * 32);   // every warp is done reading s.u.q
+    if (lane < 16) {
+      const int r = lane >> 2, c = 2 * (lane & 3);
 #pragma unroll
-    for (int r = 0; r < kGroup; ++r)
-      *reinterpret_cast<float4*>(&s.u.o[warp][r][4 * lane]) =
-          make_float4(o2[r][0].x, o2[r][0].y, o2[r][1].x, o2[r][1].y);
-    if (lane < 8 && (lane & 1) == 0) {
-      s.red_m[warp][lane >> 1] = m_row;
-      s.red_l[warp][lane >> 1] = l;
+      for (int j = 0; j < 16; ++j)
+        *reinterpret_cast<float2*>(&s.u.o[warp][r][8 * j + c]) = make_float2(st.o[j][0], st.o[j][1]);
+      if ((lane & 3) == 0) {
+        s.red_m[warp][r] = st.m;
+        s.red_l[warp][r] = l;
+      }
     }
     named_bar(1, kNW * 32);
-    const int r = warp;  // output row handled by this thread: query head kvh*4 + r
+    // thread -> (output row r = query head kvh*4 + r, dims d .. d+1)
+    const int r = ctid >> 6, d = 2 * (ctid & 63);
     float M = kNegBig;
 #pragma unroll
     for (int w = 0; w < kNW; ++w) M = fmaxf(M, s.red_m[w][r]);
     float Lsum = 0.f;
-    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    float2 O = make_float2(0.f, 0.f);
 #pragma unroll
     for (int w = 0; w < kNW; ++w) {
       const float f = exp2f(s.red_m[w][r] - M);
       Lsum += f * s.red_l[w][r];
-      const float4 ow = *reinterpret_cast<const float4*>(&s.u.o[w][r][4 * lane]);
-      O.x += f * ow.x; O.y += f * ow.y; O.z += f * ow.z; O.w += f * ow.w;
+      const float2 ow = *reinterpret_cast<const float2*>(&s.u.o[w][r][d]);
+      O.x += f * ow.x;
+      O.y += f * ow.y;
     }
-    bf16* dst = p.out + static_cast<long long>(U.b) * p.T * nq * kD + (U.kvh * kGroup + r) * kD +
-                4 * lane;
+    bf16* dst = p.out + static_cast<long long>(U.b) * p.T * nq * kD + (U.kvh * kGroup + r) * kD + d;
     if (U.n == 1) {
       const float inv = 1.0f / Lsum;
-      const float y[4] = {O.x * inv, O.y * inv, O.z * inv, O.w * inv};
-      store4_bf16(dst, y);
+      *reinterpret_cast<uint32_t*>(dst) = pack_bf16(O.x * inv, O.y * inv);
     } else {
-      *reinterpret_cast<float4*>(&p.ws_o[(static_cast<long long>(u) * kGroup + r) * kD + 4 * lane]) = O;
-      if (lane == 0) p.ws_ml[static_cast<long long>(u) * kGroup + r] = make_float2(M, Lsum);
+      const long long slot = U.g;
+      *reinterpret_cast<float2*>(&p.ws_o[(slot * kGroup + r) * kD + d]) = O;
+      if ((ctid & 63) == 0) p.ws_ml[slot * kGroup + r] = make_float2(M, Lsum);
       __threadfence();
       named_bar(1, kNW * 32);
       if (ctid == 0) {
-        const int prev = atomicAdd(&p.ws_cnt[U.b * p.nkv + U.kvh], 1);
+        const int prev = atomicAdd(&p.ws_cnt[U.q], 1);
         s.last_flag = prev == U.n - 1;
       }
       named_bar(1, kNW * 32);
       if (s.last_flag) {
         __threadfence();
-        const int base = s.prefix[U.b];
         float Mt = kNegBig;
-        for (int jj = 0; jj < U.n; ++jj) {
-          const int slot = (base + jj) * p.nkv + U.kvh;
-          Mt = fmaxf(Mt, __ldcg(&p.ws_ml[static_cast<long long>(slot) * kGroup + r]).x);
+        for (int c = U.c0; c < U.c0 + U.n; ++c) {
+          const long long sl = c;
+          Mt = fmaxf(Mt, __ldcg(&p.ws_ml[sl * kGroup + r]).x);
         }
         float Lt = 0.f;
-        float4 Ot = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int jj = 0; jj < U.n; ++jj) {
-          const int slot = (base + jj) * p.nkv + U.kvh;
-          const float2 ml = __ldcg(&p.ws_ml[static_cast<long long>(slot) * kGroup + r]);
+        float2 Ot = make_float2(0.f, 0.f);
+        for (int c = U.c0; c < U.c0 + U.n; ++c) {
+          const long long sl = c;
+          const float2 ml = __ldcg(&p.ws_ml[sl * kGroup + r]);
           const float f = exp2f(ml.x - Mt);
           Lt += f * ml.y;
-          const float4 oj =
-              __ldcg(reinterpret_cast<const float4*>(&p.ws_o[(static_cast<long long>(slot) * kGroup + r) * kD + 4 * lane]));
-          Ot.x += f * oj.x; Ot.y += f * oj.y; Ot.z += f * oj.z; Ot.w += f * oj.w;
+          const float2 oj = __ldcg(reinterpret_cast<const float2*>(&p.ws_o[(sl * kGroup + r) * kD + d]));
+          Ot.x += f * oj.x;
+          Ot.y += f * oj.y;
         }
         const float inv = 1.0f / Lt;
-        const float y[4] = {Ot.x * inv, Ot.y * inv, Ot.z * inv, Ot.w * inv};
-        store4_bf16(dst, y);
-        if (ctid == 0) atomicExch(&p.ws_cnt[U.b * p.nkv + U.kvh], 0);
+        *reinterpret_cast<uint32_t*>(dst) = pack_bf16(Ot.x * inv, Ot.y * inv);
+        if (ctid == 0) atomicExch(&p.ws_cnt[U.q], 0);
       }
     }
     named_bar(1, kNW * 32);
+  }
+  // Drain: after an abort, copies issued into this warp's ring may still be in flight. The last
+  // phase issued to each slot is the newest one on its barrier, so waiting on it is exact.
+  if (lane == 0) {
+    for (int k = issued > kStages ? issued - kStages : 0; k < issued; ++k)
+      mbar_wait(smem_u32(&s.full[k % kStages][warp]), (k / kStages) & 1, s, p.ws_err, false);
+  }
+  // The last CTA to finish (all claims made) resets the chunk counter for the next call.
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(p.ws_err + 2, 1) == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(p.ws_err + 1, 0);
+      atomicExch(p.ws_err + 2, 0);
+    }
   }
 }
 
 // ------------------------------------------------------------- standalone QK-norm/RoPE/append
 // Grid (B*T, ceil((nq + 2 nkv) / 4)), 4 warps, one (token, head) per warp: fused.py:54-96.
-template <bool PAGED>
-__global__ void __launch_bounds__(128) qk_norm_rope_kernel(const Params p, int nheads) {
+__global__ void __launch_bounds__(128) qk_norm_rope_kernel(const __grid_constant__ Params p, int nheads) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y * 4 + warp;
   if (h >= nheads) return;
@@ -673,12 +806,12 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(const Params p, int n
     if (h < nq) {
       store4_bf16(p.q_out + static_cast<long long>(m) * nq * kD + h * kD + 4 * lane, y);
     } else {
-      const long long off = row_offset<PAGED>(p, b, h - nq, ps);
+      const long long off = row_offset(p, b, h - nq, ps);
       if (off >= 0) store4_bf16(p.kc + off + 4 * lane, y);
       else if (lane == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_PAGE);
     }
   } else {
-    const long long off = row_offset<PAGED>(p, b, h - nq - p.nkv, ps);
+    const long long off = row_offset(p, b, h - nq - p.nkv, ps);
     if (off >= 0)
       *reinterpret_cast<uint2*>(p.vc + off + 4 * lane) = *reinterpret_cast<const uint2*>(src + 4 * lane);
     else if (lane == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_PAGE);
@@ -709,12 +842,12 @@ int attn_occupancy(int device, int* blocks_per_sm) {
   auto kern = decode_attn_kernel<PAGED, FUSED>;
   if (!configured[device]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(sizeof(Smem))) != cudaSuccess)
+                             static_cast<int>(kSmemBytes)) != cudaSuccess)
       return KOPT_ERR_CUDA;
     configured[device] = 1;
   }
   if (blocks_per_sm) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kern, kThreads, sizeof(Smem)) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kern, kThreads, kSmemBytes) !=
         cudaSuccess)
       return KOPT_ERR_CUDA;
   }
@@ -755,6 +888,65 @@ int fill_cache(Params& p, const kopt_kv_cache* c) {
   return KOPT_OK;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// TMA maps over the K and V caches. Box = 16 tokens x 64 dims (128 B rows, 128-byte swizzle).
+//   paged:      2-D {128 dims, num_pages * nkv * 16 rows}, row stride 256 B
+//   contiguous: 4-D {128 dims, cap, nkv, B}, strides {256 B, stride_h * 2, stride_b * 2}
+// Out-of-range boxes (past cap) are zero-filled by the hardware.
+int encode_kv_maps(Params& p, int B, int nkv) {
+  EncodeTiledFn enc = encode_tiled();
+  if (enc == nullptr) return KOPT_ERR_CUDA;
+  const cuuint32_t elem[4] = {1, 1, 1, 1};
+  cuuint64_t dims[4];
+  cuuint64_t strides[3];
+  cuuint32_t box[4] = {kHalf, kPage, 1, 1};
+  cuuint32_t rank;
+  if (p.bt != nullptr) {
+    const unsigned long long rows = static_cast<unsigned long long>(p.num_pages) * nkv * kPage;
+    if (rows >= (1ull << 31)) return KOPT_ERR_ARG;
+    rank = 2;
+    dims[0] = kD;
+    dims[1] = rows;
+    strides[0] = kD * 2;
+  } else {
+    rank = 4;
+    dims[0] = kD;
+    dims[1] = static_cast<cuuint64_t>(p.cap);
+    dims[2] = static_cast<cuuint64_t>(nkv);
+    dims[3] = static_cast<cuuint64_t>(B);
+    strides[0] = kD * 2;
+    strides[1] = static_cast<cuuint64_t>(p.sh) * 2;
+    strides[2] = static_cast<cuuint64_t>(p.sb) * 2;
+  }
+  for (int which = 0; which < 2; ++which) {
+    CUtensorMap* map = which == 0 ? &p.tmk : &p.tmv;
+    void* base = which == 0 ? static_cast<void*>(p.kc) : static_cast<void*>(p.vc);
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, base, dims, strides, box,
+                           elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return KOPT_ERR_ARG;
+  }
+  return KOPT_OK;
+}
+
 int fill_ws(Params& p, const kopt_plan* plan, void* ws) {
   if (ws == nullptr || (reinterpret_cast<uintptr_t>(ws) & 255) != 0) return KOPT_ERR_WORKSPACE;
   const WsLayout w = ws_layout(plan->B, plan->nkv, plan->max_units);
@@ -773,7 +965,7 @@ int launch_attn(const kopt_plan* plan, Params& p, void* stream) {
   if (rc) return rc;
   rc = attn_occupancy<PAGED, FUSED>(plan->device, nullptr);
   if (rc) return rc;
-  decode_attn_kernel<PAGED, FUSED><<<plan->grid, kThreads, sizeof(Smem),
+  decode_attn_kernel<PAGED, FUSED><<<plan->grid, kThreads, kSmemBytes,
                                      static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
 }
@@ -797,37 +989,39 @@ const char* kopt_strerror(int status) {
   }
 }
 
-int kopt_decode_attn_plan(int device, int B, int T, int nq, int nkv, int d, int target_ctas,
-                          kopt_plan* plan) {
+int kopt_decode_attn_plan(int device, int B, int T, int nq, int nkv, int d, int max_len,
+                          int target_ctas, kopt_plan* plan) {
   if (plan == nullptr) return KOPT_ERR_ARG;
-  if (d != kD || nkv < 1 || nq != nkv * kGroup || B < 1 || B > kMaxB || T != 1) return KOPT_ERR_ARG;
+  if (d != kD || nkv < 1 || nq != nkv * kGroup || B < 1 || B > kMaxB || T != 1 || max_len < 1)
+    return KOPT_ERR_ARG;
   int rc = set_device(device);
   if (rc) return rc;
-  int slots = target_ctas;
-  if (slots <= 0) {
-    int sms = 0, occ = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
-      return KOPT_ERR_CUDA;
-    rc = attn_occupancy<true, true>(device, &occ);
-    if (rc) return rc;
-    // the four instantiations share block size and shared memory, so one occupancy serves all
-    rc = attn_occupancy<true, false>(device, nullptr);
-    if (rc) return rc;
-    rc = attn_occupancy<false, true>(device, nullptr);
-    if (rc) return rc;
-    rc = attn_occupancy<false, false>(device, nullptr);
-    if (rc) return rc;
-    slots = sms * (occ > 0 ? occ : 1);
-  }
-  const int P = slots / nkv > 0 ? slots / nkv : 1;
+  int sms = 0, occ = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+    return KOPT_ERR_CUDA;
+  rc = attn_occupancy<true, true>(device, &occ);
+  if (rc) return rc;
+  // the four instantiations share block size and shared memory, so one occupancy serves all
+  rc = attn_occupancy<true, false>(device, nullptr);
+  if (rc) return rc;
+  rc = attn_occupancy<false, true>(device, nullptr);
+  if (rc) return rc;
+  rc = attn_occupancy<false, false>(device, nullptr);
+  if (rc) return rc;
+  if (occ < 1) return KOPT_ERR_CUDA;
+  const long long pages = (static_cast<long long>(max_len) + kPage - 1) / kPage;
+  const long long units = static_cast<long long>(B) * nkv * ((pages + kChunkPages - 1) / kChunkPages);
+  if (units > (1ll << 30)) return KOPT_ERR_ARG;
   plan->B = B;
   plan->T = T;
   plan->nkv = nkv;
-  plan->slots_per_head = P;
-  plan->grid = P * nkv;
-  plan->waves = kDefaultWaves;
-  plan->max_units = nkv * (P * kDefaultWaves + B);
+  plan->grid = target_ctas > 0 ? target_ctas : sms * occ;
+  plan->ctas_per_sm = occ;
+  plan->tile_tokens = kTile;
+  plan->max_units = static_cast<int32_t>(units);
   plan->device = device;
+  plan->max_len = max_len;
+  plan->chunk_tokens = kChunkPages * kPage;
   plan->ws_bytes = ws_layout(B, nkv, plan->max_units).total;
   return KOPT_OK;
 }
@@ -868,6 +1062,7 @@ int kopt_decode_attn(const kopt_plan* plan, const void* q, const kopt_kv_cache* 
   Params p{};
   int rc = fill_cache(p, cache);
   if (rc) return rc;
+  if (p.cap > plan->max_len) return KOPT_ERR_ARG;
   rc = fill_ws(p, plan, ws);
   if (rc) return rc;
   p.q = static_cast<const bf16*>(q);
@@ -876,9 +1071,11 @@ int kopt_decode_attn(const kopt_plan* plan, const void* q, const kopt_kv_cache* 
   p.B = plan->B;
   p.T = plan->T;
   p.nkv = plan->nkv;
-  p.slots_per_head = plan->slots_per_head;
-  p.waves = plan->waves;
   p.scale_log2 = scale * kLog2e;
+  rc = set_device(plan->device);
+  if (rc) return rc;
+  rc = encode_kv_maps(p, plan->B, plan->nkv);
+  if (rc) return rc;
   return p.bt ? launch_attn<true, false>(plan, p, stream) : launch_attn<false, false>(plan, p, stream);
 }
 
@@ -896,6 +1093,7 @@ int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, const void* q
   Params p{};
   int rc = fill_cache(p, cache);
   if (rc) return rc;
+  if (p.cap > plan->max_len) return KOPT_ERR_ARG;
   rc = fill_ws(p, plan, ws);
   if (rc) return rc;
   p.qkv = static_cast<const bf16*>(qkv);
@@ -910,10 +1108,12 @@ int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, const void* q
   p.B = plan->B;
   p.T = plan->T;
   p.nkv = plan->nkv;
-  p.slots_per_head = plan->slots_per_head;
-  p.waves = plan->waves;
   p.scale_log2 = scale * kLog2e;
   p.eps = eps;
+  rc = set_device(plan->device);
+  if (rc) return rc;
+  rc = encode_kv_maps(p, plan->B, plan->nkv);
+  if (rc) return rc;
   return p.bt ? launch_attn<true, true>(plan, p, stream) : launch_attn<false, true>(plan, p, stream);
 }
 
@@ -949,10 +1149,7 @@ int kopt_qk_norm_rope(const void* qkv, const void* q_norm_w, const void* k_norm_
   p.eps = eps;
   const int nheads = nq + 2 * nkv;
   dim3 grid(B * T, (nheads + 3) / 4);
-  if (p.bt)
-    qk_norm_rope_kernel<true><<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p, nheads);
-  else
-    qk_norm_rope_kernel<false><<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p, nheads);
+  qk_norm_rope_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p, nheads);
   return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
 }
 

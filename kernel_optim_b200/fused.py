@@ -75,14 +75,13 @@ class DecodeAttention:
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self.plan = Plan()
-        check(_lib.lib().kopt_decode_attn_plan(self.device.index, B, T, nq, nkv, d,
+        check(_lib.lib().kopt_decode_attn_plan(self.device.index, B, T, nq, nkv, d, cap,
                                                int(target_ctas or 0), ctypes.byref(self.plan)),
               "kopt_decode_attn_plan")
         self.ws = torch.empty(self.plan.ws_bytes, dtype=torch.uint8, device=self.device)
         check(_lib.lib().kopt_workspace_init(ctypes.byref(self.plan), _ptr(self.ws),
                                              _stream(self.device)), "kopt_workspace_init")
         self.scale = d ** -0.5
-        self.nsplit_max = self.plan.max_units // max(1, B * nkv)
 
     def __call__(self, q, k_cache, v_cache, pos, out):
         """q: [B*T, NQ*D]; k/v_cache: [B, NKV, cap, D]; pos: [B] int32; out: [B*T, NQ*D]."""

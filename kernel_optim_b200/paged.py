@@ -36,6 +36,11 @@ class PagedKVCache:
         self.v = torch.zeros_like(self.k)
         self.block_table = torch.full((B, self.max_pages), -1, dtype=torch.int32, device=self.device)
 
+    @property
+    def capacity(self) -> int:
+        """Keys per sequence the block table can address (max_pages * 16)."""
+        return self.max_pages * PAGE
+
     # ------------------------------------------------------------------ page assignment
     def assign_pages(self, table: torch.Tensor) -> None:
         """Install a block table [B, max_pages] (entries in [0, num_pages), or -1 if unused)."""
@@ -103,7 +108,7 @@ class PagedKVCache:
         c = KvCache()
         c.k, c.v = self.k[layer].data_ptr(), self.v[layer].data_ptr()
         c.stride_b = c.stride_h = 0
-        c.cap = self.max_pages * PAGE
+        c.cap = self.capacity
         c.num_pages = self.num_pages
         c.block_table = self.block_table.data_ptr()
         c.bt_stride = self.block_table.stride(0)
@@ -119,15 +124,17 @@ class PagedDecodeAttention:
     token's K/V appended at pos[b], and split-K attention over keys 0..pos[b].
     """
 
-    def __init__(self, B, nq, nkv, d, device, target_ctas=None, eps=1e-6):
+    def __init__(self, B, nq, nkv, d, device, max_len, target_ctas=None, eps=1e-6):
+        """max_len: the largest cache capacity (keys per sequence) any call will pass."""
         self.B, self.nq, self.nkv, self.d, self.eps = B, nq, nkv, d, eps
+        self.max_len = max_len
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise KoptError("PagedDecodeAttention needs a CUDA device (no CPU path)")
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self.plan = Plan()
-        check(_lib.lib().kopt_decode_attn_plan(self.device.index, B, 1, nq, nkv, d,
+        check(_lib.lib().kopt_decode_attn_plan(self.device.index, B, 1, nq, nkv, d, max_len,
                                                int(target_ctas or 0), ctypes.byref(self.plan)),
               "kopt_decode_attn_plan")
         self.ws = torch.empty(self.plan.ws_bytes, dtype=torch.uint8, device=self.device)

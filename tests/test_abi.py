@@ -43,15 +43,16 @@ def test_abi_version_and_strerror(lib):
 def test_struct_layouts_match_header():
     # kopt_kv_cache: 2 pointers, 2 int64, 2 int32, pointer, 2 int32 -> 56 bytes on LP64
     assert ctypes.sizeof(_lib.KvCache) == 56
-    assert ctypes.sizeof(_lib.Plan) == 40
+    assert ctypes.sizeof(_lib.Plan) == 48
 
 
 @pytest.mark.parametrize("args", [
-    (0, 16, 1, 32, 8, 64, 0),     # head_dim 64 unsupported
-    (0, 16, 1, 24, 8, 128, 0),    # group != 4
-    (0, 0, 1, 32, 8, 128, 0),     # empty batch
-    (0, 257, 1, 32, 8, 128, 0),   # batch above the plan limit
-    (0, 16, 2, 32, 8, 128, 0),    # T > 1 not built yet
+    (0, 16, 1, 32, 8, 64, 4097, 0),     # head_dim 64 unsupported
+    (0, 16, 1, 24, 8, 128, 4097, 0),    # group != 4
+    (0, 0, 1, 32, 8, 128, 4097, 0),     # empty batch
+    (0, 257, 1, 32, 8, 128, 4097, 0),   # batch above the plan limit
+    (0, 16, 2, 32, 8, 128, 4097, 0),    # T > 1 not built yet
+    (0, 16, 1, 32, 8, 128, 0, 0),       # no capacity
 ])
 def test_plan_rejects_bad_shapes(lib, args):
     plan = _lib.Plan()

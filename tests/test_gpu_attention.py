@@ -59,7 +59,7 @@ def test_golden_paged_matches_contiguous_bitwise():
         pid = cache.block_table[b, t // PAGE].long()
         cache.k[0][pid, :, t % PAGE] = k[b, :, :L].to(DEV).permute(1, 0, 2)
         cache.v[0][pid, :, t % PAGE] = v[b, :, :L].to(DEV).permute(1, 0, 2)
-    attn = PagedDecodeAttention(B, NQ, NKV, D, DEV)
+    attn = PagedDecodeAttention(B, NQ, NKV, D, DEV, cache.capacity)
     qd = q.reshape(B, NQ * D).to(DEV).contiguous()
     out = torch.empty_like(qd)
     attn.attend(qd, cache, 0, torch.tensor(lens, dtype=torch.int32, device=DEV) - 1, out)
@@ -154,7 +154,7 @@ def test_c2_fused_paged_full_size():
     ctx = [cache.gather(0, b, L) for b, L in enumerate(case.cached)]
     ref_q, k_new, v_new, ref_out = _fused_reference(case, [c[0].cpu() for c in ctx],
                                                     [c[1].cpu() for c in ctx])
-    attn = PagedDecodeAttention(B, NQ, NKV, D, DEV)
+    attn = PagedDecodeAttention(B, NQ, NKV, D, DEV, cache.capacity)
     out = torch.empty(B, NQ * D, dtype=torch.bfloat16, device=DEV)
     q_out = torch.empty_like(out)
     attn(t["qkv"], t["q_norm_w"], t["k_norm_w"], t["cos"], t["sin"], cache, 0, t["pos"], out, q_out)
@@ -178,7 +178,7 @@ def test_c2_fused_contiguous_equals_paged():
         t = case.tensors
         out = torch.empty(B, NQ * D, dtype=torch.bfloat16, device=DEV)
         cache = t["cache"] if "cache" in t else (t["k_cache"][0], t["v_cache"][0])
-        a = PagedDecodeAttention(B, NQ, NKV, D, DEV)
+        a = PagedDecodeAttention(B, NQ, NKV, D, DEV, max(case.keys) + 16)
         a(t["qkv"], t["q_norm_w"], t["k_norm_w"], t["cos"], t["sin"], cache, 0, t["pos"], out)
         outs.append(out)
     torch.cuda.synchronize()
@@ -191,7 +191,7 @@ def test_c3_ragged_paged_full_size():
     B = case.B
     q, k_new, v_new, _ = qk_norm_rope_ref(t["qkv"], t["q_norm_w"], t["k_norm_w"], t["cos"],
                                           t["sin"], t["pos"], 1, NQ, NKV, 1e-6)
-    attn = PagedDecodeAttention(B, NQ, NKV, D, DEV)
+    attn = PagedDecodeAttention(B, NQ, NKV, D, DEV, cache.capacity)
     out = torch.empty(B, NQ * D, dtype=torch.bfloat16, device=DEV)
     attn(t["qkv"], t["q_norm_w"], t["k_norm_w"], t["cos"], t["sin"], cache, 0, t["pos"], out)
     torch.cuda.synchronize()
@@ -210,7 +210,7 @@ def test_c4_long_context_full_size():
     case = build_case("c4", DEV, seed=0, paged=False)
     t = case.tensors
     B = case.B
-    a = PagedDecodeAttention(B, NQ, NKV, D, DEV)
+    a = PagedDecodeAttention(B, NQ, NKV, D, DEV, t["k_cache"].shape[3])
     out = torch.empty(B, NQ * D, dtype=torch.bfloat16, device=DEV)
     q_out = torch.empty_like(out)
     a(t["qkv"], t["q_norm_w"], t["k_norm_w"], t["cos"], t["sin"],
@@ -242,7 +242,7 @@ def test_graph_capture_and_replay():
     qkv = torch.randn(B, (NQ + 2 * NKV) * D, generator=g, device=DEV).to(torch.bfloat16)
     pos = torch.full((B,), L0, dtype=torch.int32, device=DEV)
     out = torch.empty(B, NQ * D, dtype=torch.bfloat16, device=DEV)
-    attn = PagedDecodeAttention(B, NQ, NKV, D, DEV)
+    attn = PagedDecodeAttention(B, NQ, NKV, D, DEV, case_cache.capacity)
     eager = []
     for s in range(steps):
         pos.fill_(L0 + s)
@@ -275,7 +275,7 @@ def test_bad_page_id_is_reported_not_faulted():
     cache = PagedKVCache(1, 8, NKV, D, B, 64, DEV)
     cache.assign_sequential([L, L])
     cache.block_table[1, 1] = 1000           # outside [0, 8): never dereferenced
-    attn = PagedDecodeAttention(B, NQ, NKV, D, DEV)
+    attn = PagedDecodeAttention(B, NQ, NKV, D, DEV, cache.capacity)
     q = torch.randn(B, NQ * D, device=DEV).to(torch.bfloat16)
     out = torch.empty_like(q)
     attn.attend(q, cache, 0, torch.tensor([L - 1, L - 1], dtype=torch.int32, device=DEV), out)
