@@ -43,6 +43,7 @@ extern "C" {
 #define KOPT_DEV_ERR_LEN 2     /* pos[b] + T outside [1, cap] (clamped) */
 #define KOPT_DEV_ERR_TIMEOUT 4 /* an mbarrier wait ran past its time limit */
 #define KOPT_DEV_ERR_ROPE 8    /* pos[b] + t outside the RoPE table (clamped) */
+#define KOPT_DEV_ERR_PLAN 16   /* internal work-split invariant violated (work skipped) */
 
 /* ---- KV cache descriptor ---------------------------------------------------------------- *
  * Contiguous (block_table == NULL): one layer's cache [B, nkv, cap, 128] bf16 with arbitrary
@@ -66,9 +67,10 @@ typedef struct kopt_kv_cache {
 /* ---- launch plan -------------------------------------------------------------------------- *
  * Filled by kopt_decode_attn_plan for a fixed (B, T, nkv, max_len) and reused by every call, so the
  * grid and workspace stay fixed across CUDA-graph replays. How the keys are split between CTAs is
- * decided on the device at every call from the live lengths (pos[b] + T): each (sequence, kv
- * head) pair is cut into chunks of chunk_tokens keys; CTA c takes chunk c and then claims further
- * chunks from a counter in the workspace, so faster SMs take more of them. */
+ * decided on the device at every call from the live lengths (pos[b] + T): the pages of all
+ * (sequence, kv head) pairs are laid end to end; static_pct percent of that line is split into one
+ * static piece per CTA and the rest into chunks of chunk_tokens keys that CTAs claim from a
+ * counter in the workspace once their piece is done, so SMs served faster take more. */
 typedef struct kopt_plan {
   int32_t B;
   int32_t T;
@@ -76,10 +78,13 @@ typedef struct kopt_plan {
   int32_t grid;              /* CTAs launched: one wave, SM count x resident CTAs per SM */
   int32_t ctas_per_sm;       /* resident CTAs per SM reported by the occupancy query */
   int32_t tile_tokens;       /* keys per pipeline stage */
-  int32_t max_units;         /* partial-result slots in the workspace (chunks at max_len) */
+  int32_t max_units;         /* partial-result slots in the workspace */
   int32_t device;
   int32_t max_len;           /* largest cache capacity (keys per sequence) a call may pass */
   int32_t chunk_tokens;      /* keys per dynamically scheduled chunk */
+  int32_t static_pct;        /* share of the page line split statically, one piece per CTA
+                                (environment KOPT_STATIC_PCT overrides the default at plan time) */
+  int32_t reserved;
   int64_t ws_bytes;          /* workspace bytes the caller must provide (zeroed once) */
 } kopt_plan;
 

@@ -21,6 +21,7 @@ DEV_ERR_PAGE = 1
 DEV_ERR_LEN = 2
 DEV_ERR_TIMEOUT = 4
 DEV_ERR_ROPE = 8
+DEV_ERR_PLAN = 16
 
 #: every symbol include/kopt.h declares
 EXPORTED = (
@@ -69,6 +70,8 @@ class Plan(ctypes.Structure):
         ("device", ctypes.c_int32),
         ("max_len", ctypes.c_int32),
         ("chunk_tokens", ctypes.c_int32),
+        ("static_pct", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
         ("ws_bytes", ctypes.c_int64),
     ]
 
@@ -132,4 +135,6 @@ def dev_error_text(bits: int) -> str:
         names.append("mbarrier wait timed out")
     if bits & DEV_ERR_ROPE:
         names.append("position outside the RoPE table (clamped)")
+    if bits & DEV_ERR_PLAN:
+        names.append("internal work-split invariant violated")
     return ", ".join(names) or "none"

@@ -10,11 +10,13 @@
 //
 // How this file does it on B200:
 //   * One wave of one CTA per SM, balanced dynamically. Every CTA plans the call on the device from
-//     the live lengths pos[b] + 1 (never from the capacity, unlike fused.py:211-214): the keys of
-//     each (sequence, kv head) pair are cut into chunks of 32 pages (512 keys); CTA c takes chunk c,
-//     then claims further chunks from a global atomic counter, one chunk ahead so its copies never
-//     stop. An SM that the memory system serves faster simply takes more chunks. The last CTA to
-//     finish resets the counter; no CTA ever waits for another.
+//     the live lengths pos[b] + 1 (never from the capacity, unlike fused.py:211-214): the 16-token
+//     pages of every (sequence, kv head) pair are laid end to end on one line. The first
+//     static_pct of the line is cut into one equal piece per CTA; the rest into 32-page chunks that
+//     CTAs claim from a global counter, one ahead, once their piece is done. SMs that the memory system serves
+//     faster simply take more chunks. A pair cut by piece or chunk boundaries is split into units
+//     whose partial results are merged by the last unit to finish. The last CTA to finish resets
+//     the counter; no CTA ever waits for another.
 //   * 8 warps; tile i of a unit is 128 keys = 8 pages and warp w owns page w of every tile. Each
 //     warp streams its own pages with tiled TMA (cp.async.bulk.tensor, 128-byte swizzle, no
 //     multicast) into a private 3-deep ring of shared-memory slots, each slot guarded by an
@@ -38,6 +40,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "kopt.h"
 
@@ -53,7 +56,8 @@ constexpr int kStages = 3;
 constexpr int kThreads = kNW * 32;
 constexpr int kMaxB = 256;
 constexpr int kBoxBytes = kPage * kHalf * 2;   // 2 KiB: one TMA box
-constexpr int kChunkPages = 32;                // dynamic scheduling granule: 512 keys of one pair
+constexpr int kChunkPages = 32;                // dynamic chunk: 512 keys of the page line
+constexpr int kDefaultStaticPct = 100;         // share of the page line split statically
 constexpr unsigned long long kTimeoutNs = 1000000000ull;  // 1 s per mbarrier wait
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegBig = -1.0e30f;     // running-max seed (finite, as fused.py:164)
@@ -82,6 +86,7 @@ struct Params {
   int* ws_err;           // error word; ws_err[1] = next dynamic chunk, ws_err[2] = CTAs done
   int bt_stride, num_pages, cap, rope_len;
   int B, T, nkv;
+  int static_pct;        // share of the page line cut into one static piece per CTA
   float scale_log2, eps;
 };
 
@@ -90,22 +95,28 @@ struct Params {
 struct __align__(1024) Smem {
   bf16 k[kStages][kNW][2][kPage * kHalf];
   bf16 v[kStages][kNW][2][kPage * kHalf];
-  union {
-    bf16 q[kGroup][kD];                 // unit prologue: roped q rows (bf16, the reference's q)
-    float o[kNW][kGroup][kD];           // unit epilogue: per-warp partial outputs
-  } u;
+  alignas(16) bf16 q[kGroup][kD];       // roped q rows of the current unit (the reference's q)
+  float o[kNW][kGroup][kD + 4];         // unit epilogue: per-warp partial outputs (padded rows)
+  alignas(16) bf16 rows[8][kD];         // next unit's prologue inputs, staged by cp.async:
+                                        // q heads 0-3, k head, v head, cos row, sin row
+  alignas(16) bf16 wq[kD];              // q_norm weight
+  alignas(16) bf16 wk[kD];              // k_norm weight
   float red_m[kNW][kGroup];
   float red_l[kNW][kGroup];
   bf16 knew[kD];
   bf16 vnew[kD];
-  int cstart[kMaxB + 1];                // first chunk of pair (b, kv head 0)
+  int pstart[kMaxB + 1];                // first page of pair (b, kv head 0) on the page line
   int npages[kMaxB];                    // pages streamed per (b, kv head)
   int lens[kMaxB];                      // keys attended by sequence b
   int ring[4];                          // the CTA's k-th claimed chunk in ring[k % 4] (-1: none)
   unsigned long long full[kStages][kNW];   // per-warp ring: slot filled by this warp's TMA
-  int total_chunks;
+  int total_pages;
+  int static_pages;                     // P: pages of the line split into one piece per CTA
+  int total_chunks;                     // grid static pieces + dynamic chunks
   volatile int nclaimed;                // ring entries 0 .. nclaimed-1 are valid
-  int last_flag;
+  int merge_go, mq, mc0, mn, mb, mkvh;  // a pair whose partials this CTA merges now
+  int unext[12];                        // the look-ahead unit, parked across the tile loop
+  int have_next;
   volatile int abort;
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + slack to align the base to 1 KiB
@@ -172,6 +183,16 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
       "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar), "l"(policy)
       : "memory");
+}
+// 16-byte global -> shared copy through L2 only, tracked per thread by cp.async groups.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 __device__ __forceinline__ uint64_t evict_first_policy() {
   uint64_t pol;
@@ -260,10 +281,11 @@ __device__ __forceinline__ void store4_bf16(bf16* dst, const float y[4]) {
 // ---------------------------------------------------------------------------- device plan
 __device__ __forceinline__ int ceil_div_i(int a, int b) { return (a + b - 1) / b; }
 
-// Warp 0 derives the chunk list from pos[]: sequence b streams Ls_b keys from the cache (all L_b
+// Warp 0 lays out the page line from pos[]: sequence b streams Ls_b keys from the cache (all L_b
 // keys, or L_b - 1 when the fused prologue appends the last one itself) = max(1, ceil(Ls_b/16))
-// pages per kv head, cut into ceil(pages / 32) chunks; pair (b, kvh) owns chunks
-// [cstart[b] + kvh * nch_b, + nch_b).
+// pages per kv head; pair (b, kvh) owns pages [pstart[b] + kvh * npages[b], + npages[b]).
+// Chunks: k < grid is CTA k's static piece [k*piece, (k+1)*piece); k >= grid is dynamic chunk
+// k - grid covering [grid*piece + (k-grid)*32, ...) up to the end of the line.
 template <bool FUSED>
 __device__ void compute_plan(const Params& p, Smem& s, int lane) {
   int err = 0;
@@ -282,60 +304,93 @@ __device__ void compute_plan(const Params& p, Smem& s, int lane) {
   int carry = 0;
   for (int base = 0; base < p.B; base += 32) {
     const int b = base + lane;
-    const int n = b < p.B ? ceil_div_i(s.npages[b], kChunkPages) * p.nkv : 0;
+    const int n = b < p.B ? s.npages[b] * p.nkv : 0;
     int incl = n;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const int t = __shfl_up_sync(0xffffffffu, incl, off);
       if (lane >= off) incl += t;
     }
-    if (b < p.B) s.cstart[b + 1] = carry + incl;
+    if (b < p.B) s.pstart[b + 1] = carry + incl;
     carry += __shfl_sync(0xffffffffu, incl, 31);
   }
   if (lane == 0) {
-    s.cstart[0] = 0;
-    s.total_chunks = carry;
+    const int G = gridDim.x;
+    int P = static_cast<int>(static_cast<long long>(carry) * p.static_pct / 100);
+    if (P < G) P = 0;   // too few pages for one per CTA: everything is dynamic
+    s.pstart[0] = 0;
+    s.total_pages = carry;
+    s.static_pages = P;
+    s.total_chunks = G + ceil_div_i(carry - P, kChunkPages);
   }
+}
+
+// Chunk k's page range on the line: k < grid is CTA k's static piece [k P / G, (k+1) P / G) of the
+// first P pages (P >= G, so no piece is empty, or P = 0); k >= grid is dynamic chunk k - grid, 32
+// pages from P + 32 (k - grid), clipped to the end of the line.
+__device__ __forceinline__ void chunk_range(const Smem& s, int k, int& x0, int& x1) {
+  const int G = gridDim.x;
+  const long long P = s.static_pages;
+  if (k < G) {
+    x0 = static_cast<int>(k * P / G);
+    x1 = static_cast<int>((k + 1) * P / G);
+  } else {
+    x0 = static_cast<int>(P) + (k - G) * kChunkPages;
+    x1 = min(x0 + kChunkPages, s.total_pages);
+  }
+}
+// The chunk holding page y.
+__device__ __forceinline__ int chunk_of(const Smem& s, int y) {
+  const long long G = gridDim.x;
+  const long long P = s.static_pages;
+  return y < P ? static_cast<int>(((y + 1) * G - 1) / P)
+               : static_cast<int>(G) + (y - static_cast<int>(P)) / kChunkPages;
 }
 
 struct Unit {
   int b, kvh, q;      // sequence, kv head, pair index b * nkv + kvh
   int t0, t1;         // keys streamed from the cache: [t0, t1)
   int L;              // keys attended by the sequence
-  int g;              // chunk index = workspace slot of this unit's partial result
-  int c0, n;          // the pair's chunks: c0 .. c0 + n - 1
-  bool last;          // last chunk of the pair (owns the appended token in the fused path)
+  int slot;           // workspace slot of this unit's partial result: chunk + q
+  int c0, n;          // chunks holding the pair: c0 .. c0 + n - 1 (slots c + q)
+  bool last;          // this unit ends the pair (owns the appended token in the fused path)
 };
 
+// The unit starting at page x of chunk k (x is advanced past it, up to x1).
 template <bool FUSED>
-__device__ __forceinline__ Unit chunk_unit(const Params& p, const Smem& s, int g) {
-  int lo = 0, hi = p.B;   // largest b with cstart[b] <= g
+__device__ __forceinline__ Unit unit_at(const Params& p, const Smem& s, int k, int& x, int x1) {
+  int lo = 0, hi = p.B;   // largest b with pstart[b] <= x
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (s.cstart[mid] <= g) lo = mid; else hi = mid;
+    if (s.pstart[mid] <= x) lo = mid; else hi = mid;
   }
   Unit U;
-  const int b = lo, np = s.npages[b], nch = ceil_div_i(np, kChunkPages);
-  const int r = g - s.cstart[b];
-  const int kvh = r / nch, j = r % nch;
+  const int b = lo, np = s.npages[b];
+  const int off = x - s.pstart[b];
+  const int kvh = off / np, pg = off % np;
+  const int pair0 = s.pstart[b] + kvh * np, pair1 = pair0 + np;
+  const int ux1 = min(x1, pair1);
   U.b = b;
   U.kvh = kvh;
   U.q = b * p.nkv + kvh;
   U.L = s.lens[b];
   const int Ls = FUSED ? U.L - 1 : U.L;
-  U.t0 = j * kChunkPages * kPage;
-  U.t1 = max(U.t0, min((j + 1) * kChunkPages * kPage, Ls));
-  U.g = g;
-  U.c0 = s.cstart[b] + kvh * nch;
-  U.n = nch;
-  U.last = j == nch - 1;
+  U.t0 = pg * kPage;
+  U.t1 = max(U.t0, min((ux1 - pair0) * kPage, Ls));
+  U.slot = k + U.q;
+  U.c0 = chunk_of(s, pair0);
+  U.n = chunk_of(s, pair1 - 1) - U.c0 + 1;
+  U.last = ux1 == pair1;
+  x = ux1;
   return U;
 }
 
-// Claim the next chunk for this CTA (thread 0 only): chunk index or -1 when none are left.
-__device__ __forceinline__ int claim_chunk(const Params& p, int total) {
-  const int g = static_cast<int>(gridDim.x) + atomicAdd(p.ws_err + 1, 1);
-  return g < total ? g : -1;
+// Claim the next dynamic chunk (thread 0 only). claim_issue returns the raw counter value so that
+// the atomic's latency is only paid where claim_chunk turns it into a chunk index (or -1).
+__device__ __forceinline__ int claim_issue(const Params& p) { return atomicAdd(p.ws_err + 1, 1); }
+__device__ __forceinline__ int claim_chunk(int raw, int total) {
+  const int k = static_cast<int>(gridDim.x) + raw;
+  return k < total ? k : -1;
 }
 
 // Element offset of token t's row of (b, kvh) in the cache, or -1 for a page id out of range.
@@ -444,7 +499,7 @@ __device__ __forceinline__ void inject_token(const Smem& s, float scale_log2, Wa
   float dot[kGroup];
 #pragma unroll
   for (int r = 0; r < kGroup; ++r) {
-    const uint2 qr = *reinterpret_cast<const uint2*>(&s.u.q[r][4 * lane]);
+    const uint2 qr = *reinterpret_cast<const uint2*>(&s.q[r][4 * lane]);
     const float2 q01 = bf2f(qr.x), q23 = bf2f(qr.y);
     dot[r] = q01.x * k01.x + q01.y * k01.y + q23.x * k23.x + q23.y * k23.y;
   }
@@ -473,6 +528,7 @@ __device__ __forceinline__ void inject_token(const Smem& s, float scale_log2, Wa
 template <bool PAGED, bool FUSED>
 struct Issuer {
   int k;              // next ring index to open
+  int chunk, x, x1;   // current chunk and the unopened part of its page range [x, x1)
   Unit U;
   int ti, ntiles;     // current tile within U
   int npg;            // pages streamed by U
@@ -491,12 +547,17 @@ struct Issuer {
     while (true) {
       ++ti;
       while (ti >= ntiles) {
-        if (k >= s.nclaimed) return 0;
-        __threadfence_block();   // pairs with the fence between the ring write and nclaimed
-        const int g = const_cast<const volatile int*>(s.ring)[k & 3];
-        if (g < 0) return -1;
-        ++k;
-        U = chunk_unit<FUSED>(p, s, g);
+        if (x >= x1) {   // chunk exhausted: open the next claimed one
+          if (k >= s.nclaimed) return 0;
+          __threadfence_block();   // pairs with the fence between the ring write and nclaimed
+          const int c = const_cast<const volatile int*>(s.ring)[k & 3];
+          if (c < 0 || c >= s.total_chunks) return -1;
+          ++k;
+          chunk = c;
+          chunk_range(s, c, x, x1);
+          continue;
+        }
+        U = unit_at<FUSED>(p, s, chunk, x, x1);
         ntiles = ceil_div_i(U.t1 - U.t0, kTile);
         npg = ceil_div_i(U.t1 - U.t0, kPage);
         ti = 0;
@@ -573,20 +634,143 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
     asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmk) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmv) : "memory");
   }
+  if (FUSED && (warp == 2 || warp == 3)) {   // q_norm / k_norm weights, once per CTA
+    const bf16* w = warp == 2 ? p.qw : p.kw;
+    bf16* dstw = warp == 2 ? s.wq : s.wk;
+    *reinterpret_cast<uint2*>(dstw + 4 * lane) = *reinterpret_cast<const uint2*>(w + 4 * lane);
+  }
   __syncwarp();
-  if (threadIdx.x == 0) {   // first chunk static, the next one claimed
-    const int total = s.total_chunks;
-    const int g0 = static_cast<int>(blockIdx.x) < total ? static_cast<int>(blockIdx.x) : -1;
-    s.ring[0] = g0;
-    s.ring[1] = g0 >= 0 ? claim_chunk(p, total) : -1;
-    s.nclaimed = 2;
+  if (threadIdx.x == 0) {   // the static piece; dynamic chunks are claimed from the prologues
+    s.ring[0] = blockIdx.x;
+    s.ring[1] = s.ring[2] = s.ring[3] = -1;
+    s.nclaimed = 1;
+    if (s.total_chunks == static_cast<int>(gridDim.x)) {   // no dynamic chunks: piece, then end
+      s.nclaimed = 2;
+    } else if (s.static_pages == 0) {   // no pieces: the first dynamic chunk must be known up front
+      // (with P = 0 every chunk is dynamic, so total_chunks > grid whenever there is work)
+      s.ring[1] = claim_chunk(claim_issue(p), s.total_chunks);
+      s.nclaimed = 2;
+    }
   }
   __syncthreads();
   const uint64_t pol = evict_first_policy();
 
+  const int ctid = threadIdx.x;
+  // Consume cursor: ring index kc to open next, current chunk and its unvisited pages [cx, cx1).
+  int kc = 0, chunk = -1, cx = 0, cx1 = 0;
+  int pend_claim = -2;   // thread 0: raw claim in flight for ring index kc (published at a prologue)
+  // Next unit along the cursor; opening a chunk claims the one after it.
+  auto advance = [&](Unit& V) -> bool {
+    while (cx >= cx1) {
+      if (kc >= s.nclaimed) {   // never read a ring entry before it is published
+        if (ctid == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_PLAN);
+        return false;
+      }
+      const int c = const_cast<const volatile int*>(s.ring)[kc & 3];
+      if (c < 0) return false;
+      if (c >= s.total_chunks) {
+        if (ctid == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_PLAN);
+        return false;
+      }
+      chunk = c;
+      chunk_range(s, c, cx, cx1);
+      ++kc;
+      // claim the chunk after this one, unless the piece was empty (then it was claimed up front)
+      if (ctid == 0 && cx < cx1 && s.total_chunks > static_cast<int>(gridDim.x))
+        pend_claim = claim_issue(p);
+    }
+    V = unit_at<FUSED>(p, s, chunk, cx, cx1);
+    return true;
+  };
+  // Stage unit V's prologue inputs: warp w < 4 its q head row, warp 4 the k row, warp 5 the v row,
+  // warps 6/7 the RoPE rows (16 lanes x 16 B each).
+  auto stage = [&](const Unit& V) {
+    const bf16* src = nullptr;
+    if (warp < kGroup) {
+      const int h = V.kvh * kGroup + warp;
+      src = FUSED ? p.qkv + static_cast<long long>(V.b) * (nq + 2 * p.nkv) * kD + h * kD
+                  : p.q + static_cast<long long>(V.b) * p.T * nq * kD + h * kD;
+    } else if (FUSED) {
+      const bf16* row = p.qkv + static_cast<long long>(V.b) * (nq + 2 * p.nkv) * kD;
+      int rp = V.L - 1;
+      if (rp >= p.rope_len) {
+        if (lane == 0 && warp == 6) atomicOr(p.ws_err, KOPT_DEV_ERR_ROPE);
+        rp = p.rope_len - 1;
+      }
+      if (warp == 4) src = row + (nq + V.kvh) * kD;
+      else if (warp == 5) src = row + (nq + p.nkv + V.kvh) * kD;
+      else if (warp == 6) src = p.cos + static_cast<long long>(rp) * kD;
+      else src = p.sin + static_cast<long long>(rp) * kD;
+    }
+    if (src != nullptr && lane < 16) cp_async16(smem_u32(&s.rows[warp][8 * lane]), src + 8 * lane);
+    cp_async_commit();
+  };
+  // Merge every partial of pair (q, b, kvh) held in slots c + q, c in c0 .. c0+n-1: online
+  // log-sum-exp over the splits, loads issued four splits at a time.
+  auto merge_pair = [&](int q, int c0, int n, int b, int kvh) {
+    const int r = ctid >> 6, d = 2 * (ctid & 63);
+    float M = kNegBig, L = 0.f;
+    float2 O = make_float2(0.f, 0.f);
+    for (int c = c0; c < c0 + n; c += 4) {
+      float2 ml[4], oj[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (c + j < c0 + n) {
+          const long long sl = static_cast<long long>(c + j) + q;
+          ml[j] = __ldcg(&p.ws_ml[sl * kGroup + r]);
+          oj[j] = __ldcg(reinterpret_cast<const float2*>(&p.ws_o[(sl * kGroup + r) * kD + d]));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (c + j < c0 + n) {
+          const float mn = fmaxf(M, ml[j].x);
+          const float a = exp2f(M - mn), f = exp2f(ml[j].x - mn);
+          L = L * a + ml[j].y * f;
+          O.x = O.x * a + oj[j].x * f;
+          O.y = O.y * a + oj[j].y * f;
+          M = mn;
+        }
+      }
+    }
+    const float inv = 1.0f / L;
+    bf16* dst = p.out + static_cast<long long>(b) * p.T * nq * kD + (kvh * kGroup + r) * kD + d;
+    *reinterpret_cast<uint32_t*>(dst) = pack_bf16(O.x * inv, O.y * inv);
+    if (ctid == 0) atomicExch(&p.ws_cnt[q], 0);
+  };
+  // thread 0: a partial written but not yet released (fence + counter), and a pair whose
+  // last-unit test is in flight (atomic result checked at the next epilogue or at the end)
+  bool pm_release = false, pm_valid = false;
+  int pm_prev = 0, pm_q = 0, pm_c0 = 0, pm_n = 0, pm_b = 0, pm_kvh = 0;
+  // The release waits for this CTA's partial stores to be acknowledged (microseconds under full
+  // HBM load), so it runs off the critical path: after warp 0's first tile of the next unit.
+  auto release = [&]() {
+    __threadfence();
+    pm_prev = atomicAdd(&p.ws_cnt[pm_q], 1);
+    pm_valid = true;
+    pm_release = false;
+  };
+  auto resolve_pending = [&]() {   // thread 0 only: publish whether this CTA merges that pair
+    s.merge_go = 0;
+    if (pm_valid) {
+      if (pm_prev == pm_n - 1) {
+        __threadfence();   // acquire the other units' partials
+        s.merge_go = 1;
+        s.mq = pm_q; s.mc0 = pm_c0; s.mn = pm_n; s.mb = pm_b; s.mkvh = pm_kvh;
+      }
+      pm_valid = false;
+    }
+  };
+
+  Unit U;
+  bool have = advance(U);
+  if (have) stage(U);   // the first unit's prologue inputs travel while the rings fill
+
   // This warp's ring: `state` tells whether the issue cursor stands on an unissued tile.
   Issuer<PAGED, FUSED> iss;
   iss.k = 0;
+  iss.chunk = 0;
+  iss.x = iss.x1 = 0;
   iss.ti = 0;
   iss.ntiles = 0;
   iss.npg = 0;
@@ -605,71 +789,57 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
   };
   pump();
 
-  const int ctid = threadIdx.x;
-  for (int kc = 0;; ++kc) {
-    const int g = const_cast<const volatile int*>(s.ring)[kc & 3];
-    if (g < 0) break;
-    // keep one chunk claimed ahead (thread 0; published by the prologue barrier below)
-    if (ctid == 0 && kc >= 1 && s.ring[kc & 3] >= 0) {
-      s.ring[(kc + 1) & 3] = claim_chunk(p, s.total_chunks);
-      __threadfence_block();
-      s.nclaimed = kc + 2;
-    }
-    const Unit U = chunk_unit<FUSED>(p, s, g);
+  while (have) {
     const bool inject = FUSED && U.last;
     const int se = U.t1;                          // keys streamed from the cache end here
     const int ntiles = ceil_div_i(se - U.t0, kTile);
-    const int qh = U.kvh * kGroup + (warp & 3);  // query head computed by warps 0-3
 
-    // ---- prologue: q rows (and the new K/V for the CTA owning position L-1)
+    // ---- prologue from the staged rows: q rows, and the new K/V for the unit ending the pair
+    cp_async_wait_all();
+    if (ctid == 0 && pend_claim != -2) {
+      s.ring[kc & 3] = claim_chunk(pend_claim, s.total_chunks);
+      __threadfence_block();
+      s.nclaimed = kc + 1;
+      pend_claim = -2;
+    }
+    named_bar(1, kNW * 32);
+    pump();   // a chunk claimed in the previous unit is visible now
     if (FUSED) {
-      const int rowlen = (nq + 2 * p.nkv) * kD;
-      const bf16* src = p.qkv + static_cast<long long>(U.b) * rowlen;
-      int rp = U.L - 1;
-      if (rp >= p.rope_len) {
-        if (lane == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_ROPE);
-        rp = p.rope_len - 1;
-      }
-      const bf16* cs = p.cos + static_cast<long long>(rp) * kD;
-      const bf16* sn = p.sin + static_cast<long long>(rp) * kD;
       float y[4];
       if (warp < kGroup) {
-        norm_rope_head(src + qh * kD, p.qw, cs, sn, p.eps, lane, y);
-        store4_bf16(&s.u.q[warp][4 * lane], y);
+        norm_rope_head(s.rows[warp], s.wq, s.rows[6], s.rows[7], p.eps, lane, y);
+        store4_bf16(&s.q[warp][4 * lane], y);
         if (p.q_out != nullptr && U.t0 == 0)
-          store4_bf16(p.q_out + static_cast<long long>(U.b) * nq * kD + qh * kD + 4 * lane, y);
+          store4_bf16(p.q_out + static_cast<long long>(U.b) * nq * kD +
+                          (U.kvh * kGroup + warp) * kD + 4 * lane, y);
       } else if (inject && warp < kGroup + 2) {
         const long long off = row_offset(p, U.b, U.kvh, U.L - 1);
         if (warp == kGroup) {
-          norm_rope_head(src + (nq + U.kvh) * kD, p.kw, cs, sn, p.eps, lane, y);
+          norm_rope_head(s.rows[4], s.wk, s.rows[6], s.rows[7], p.eps, lane, y);
           store4_bf16(&s.knew[4 * lane], y);
           if (off >= 0) store4_bf16(p.kc + off + 4 * lane, y);
         } else {
-          const uint2 raw =
-              *reinterpret_cast<const uint2*>(src + (nq + p.nkv + U.kvh) * kD + 4 * lane);
+          const uint2 raw = *reinterpret_cast<const uint2*>(&s.rows[5][4 * lane]);
           *reinterpret_cast<uint2*>(&s.vnew[4 * lane]) = raw;
           if (off >= 0) *reinterpret_cast<uint2*>(p.vc + off + 4 * lane) = raw;
         }
         if (off < 0 && lane == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_PAGE);
       }
     } else if (warp < kGroup) {
-      const bf16* src = p.q + static_cast<long long>(U.b) * p.T * nq * kD + qh * kD;
-      *reinterpret_cast<uint2*>(&s.u.q[warp][4 * lane]) =
-          *reinterpret_cast<const uint2*>(src + 4 * lane);
+      *reinterpret_cast<uint2*>(&s.q[warp][4 * lane]) =
+          *reinterpret_cast<const uint2*>(&s.rows[warp][4 * lane]);
     }
     named_bar(1, kNW * 32);
-    pump();   // the chunk claimed above is visible now
     // A fragments of Q (rows 0-3 live on lanes 0-15): a0 = Q[r][16ks + 2(l%4) + {0,1}], a2 = +8
     uint32_t qa[8][2];
     {
       const int r = lane >> 2, c = 2 * (lane & 3);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        qa[ks][0] = lane < 16 ? *reinterpret_cast<const uint32_t*>(&s.u.q[r & 3][16 * ks + c]) : 0u;
-        qa[ks][1] = lane < 16 ? *reinterpret_cast<const uint32_t*>(&s.u.q[r & 3][16 * ks + 8 + c]) : 0u;
+        qa[ks][0] = lane < 16 ? *reinterpret_cast<const uint32_t*>(&s.q[r & 3][16 * ks + c]) : 0u;
+        qa[ks][1] = lane < 16 ? *reinterpret_cast<const uint32_t*>(&s.q[r & 3][16 * ks + 8 + c]) : 0u;
       }
     }
-    named_bar(1, kNW * 32);
 
     WarpState st;
     st.m = kNegBig;
@@ -677,6 +847,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
 #pragma unroll
     for (int j = 0; j < 16; ++j) st.o[j][0] = st.o[j][1] = 0.f;
 
+    // Look one unit ahead and stage its inputs while this unit streams; done after this warp's
+    // first tile so that it does not delay the start of the unit.
+    bool looked = false;
+    auto look_ahead = [&]() {
+      Unit Un;
+      const bool hn = advance(Un);
+      if (hn) stage(Un);
+      if (ctid == 0) {
+        static_assert(sizeof(Unit) <= sizeof(s.unext), "look-ahead unit does not fit");
+        *reinterpret_cast<Unit*>(s.unext) = Un;
+        s.have_next = hn;
+      }
+      looked = true;
+    };
     for (int i = 0; i < ntiles; ++i) {
       const int ntok = min(max(se - (U.t0 + i * kTile + warp * kPage), 0), kPage);
       if (ntok == 0) continue;          // no page of this warp in this tile
@@ -688,19 +872,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
       ++consumed;
       __syncwarp();
       pump();                           // refill the slot just consumed
+      if (!looked) look_ahead();
+      if (ctid == 0 && pm_release) release();
     }
+    if (!looked) look_ahead();          // this warp had no tile in this unit
     if (inject && warp == 0) inject_token(s, p.scale_log2, st, lane);
 
-    // ---- epilogue: merge the 4 warps, then the splits of this (b, kvh)
+    // ---- epilogue: merge the 8 warps, then the splits of this (b, kvh)
+    if (ctid == 0) {
+      if (pm_release) release();   // warp 0 had no tile in this unit
+      resolve_pending();
+    }
     float l = st.l;
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
-    named_bar(1, kNW * 32);   // every warp is done reading s.u.q
     if (lane < 16) {
       const int r = lane >> 2, c = 2 * (lane & 3);
 #pragma unroll
       for (int j = 0; j < 16; ++j)
-        *reinterpret_cast<float2*>(&s.u.o[warp][r][8 * j + c]) = make_float2(st.o[j][0], st.o[j][1]);
+        *reinterpret_cast<float2*>(&s.o[warp][r][8 * j + c]) = make_float2(st.o[j][0], st.o[j][1]);
       if ((lane & 3) == 0) {
         s.red_m[warp][r] = st.m;
         s.red_l[warp][r] = l;
@@ -718,50 +908,36 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
     for (int w = 0; w < kNW; ++w) {
       const float f = exp2f(s.red_m[w][r] - M);
       Lsum += f * s.red_l[w][r];
-      const float2 ow = *reinterpret_cast<const float2*>(&s.u.o[w][r][d]);
+      const float2 ow = *reinterpret_cast<const float2*>(&s.o[w][r][d]);
       O.x += f * ow.x;
       O.y += f * ow.y;
     }
-    bf16* dst = p.out + static_cast<long long>(U.b) * p.T * nq * kD + (U.kvh * kGroup + r) * kD + d;
     if (U.n == 1) {
+      bf16* dst = p.out + static_cast<long long>(U.b) * p.T * nq * kD + (U.kvh * kGroup + r) * kD + d;
       const float inv = 1.0f / Lsum;
       *reinterpret_cast<uint32_t*>(dst) = pack_bf16(O.x * inv, O.y * inv);
     } else {
-      const long long slot = U.g;
+      const long long slot = U.slot;
       *reinterpret_cast<float2*>(&p.ws_o[(slot * kGroup + r) * kD + d]) = O;
       if ((ctid & 63) == 0) p.ws_ml[slot * kGroup + r] = make_float2(M, Lsum);
-      __threadfence();
-      named_bar(1, kNW * 32);
-      if (ctid == 0) {
-        const int prev = atomicAdd(&p.ws_cnt[U.q], 1);
-        s.last_flag = prev == U.n - 1;
-      }
-      named_bar(1, kNW * 32);
-      if (s.last_flag) {
-        __threadfence();
-        float Mt = kNegBig;
-        for (int c = U.c0; c < U.c0 + U.n; ++c) {
-          const long long sl = c;
-          Mt = fmaxf(Mt, __ldcg(&p.ws_ml[sl * kGroup + r]).x);
-        }
-        float Lt = 0.f;
-        float2 Ot = make_float2(0.f, 0.f);
-        for (int c = U.c0; c < U.c0 + U.n; ++c) {
-          const long long sl = c;
-          const float2 ml = __ldcg(&p.ws_ml[sl * kGroup + r]);
-          const float f = exp2f(ml.x - Mt);
-          Lt += f * ml.y;
-          const float2 oj = __ldcg(reinterpret_cast<const float2*>(&p.ws_o[(sl * kGroup + r) * kD + d]));
-          Ot.x += f * oj.x;
-          Ot.y += f * oj.y;
-        }
-        const float inv = 1.0f / Lt;
-        *reinterpret_cast<uint32_t*>(dst) = pack_bf16(Ot.x * inv, Ot.y * inv);
-        if (ctid == 0) atomicExch(&p.ws_cnt[U.q], 0);
-      }
     }
+    if (s.merge_go) merge_pair(s.mq, s.mc0, s.mn, s.mb, s.mkvh);
     named_bar(1, kNW * 32);
+    if (U.n > 1 && ctid == 0) {   // released later (see release)
+      pm_release = true;
+      pm_q = U.q; pm_c0 = U.c0; pm_n = U.n; pm_b = U.b; pm_kvh = U.kvh;
+    }
+    named_bar(1, kNW * 32);   // parked look-ahead unit visible
+    have = s.have_next != 0;
+    U = *reinterpret_cast<const Unit*>(s.unext);
   }
+  // the last pending release and split test of this CTA
+  if (ctid == 0) {
+    if (pm_release) release();
+    resolve_pending();
+  }
+  named_bar(1, kNW * 32);
+  if (s.merge_go) merge_pair(s.mq, s.mc0, s.mn, s.mb, s.mkvh);
   // Drain: after an abort, copies issued into this warp's ring may still be in flight. The last
   // phase issued to each slot is the newest one on its barrier, so waiting on it is exact.
   if (lane == 0) {
@@ -1009,19 +1185,26 @@ int kopt_decode_attn_plan(int device, int B, int T, int nq, int nkv, int d, int 
   rc = attn_occupancy<false, false>(device, nullptr);
   if (rc) return rc;
   if (occ < 1) return KOPT_ERR_CUDA;
-  const long long pages = (static_cast<long long>(max_len) + kPage - 1) / kPage;
-  const long long units = static_cast<long long>(B) * nkv * ((pages + kChunkPages - 1) / kChunkPages);
-  if (units > (1ll << 30)) return KOPT_ERR_ARG;
+  // slot = chunk + pair < grid + ceil(T / 32) + B * nkv, T = total pages at max_len
+  const int grid = target_ctas > 0 ? target_ctas : sms * occ;
+  const long long pages = static_cast<long long>(B) * nkv * ((static_cast<long long>(max_len) + kPage - 1) / kPage);
+  if (pages >= (1ll << 31)) return KOPT_ERR_ARG;
+  const long long units = grid + (pages + kChunkPages - 1) / kChunkPages + static_cast<long long>(B) * nkv;
   plan->B = B;
   plan->T = T;
   plan->nkv = nkv;
-  plan->grid = target_ctas > 0 ? target_ctas : sms * occ;
+  plan->grid = grid;
   plan->ctas_per_sm = occ;
   plan->tile_tokens = kTile;
   plan->max_units = static_cast<int32_t>(units);
   plan->device = device;
   plan->max_len = max_len;
   plan->chunk_tokens = kChunkPages * kPage;
+  plan->static_pct = kDefaultStaticPct;
+  if (const char* e = getenv("KOPT_STATIC_PCT")) {
+    const int v = atoi(e);
+    if (v >= 0 && v <= 100) plan->static_pct = v;
+  }
   plan->ws_bytes = ws_layout(B, nkv, plan->max_units).total;
   return KOPT_OK;
 }
@@ -1071,6 +1254,7 @@ int kopt_decode_attn(const kopt_plan* plan, const void* q, const kopt_kv_cache* 
   p.B = plan->B;
   p.T = plan->T;
   p.nkv = plan->nkv;
+  p.static_pct = plan->static_pct;
   p.scale_log2 = scale * kLog2e;
   rc = set_device(plan->device);
   if (rc) return rc;
@@ -1108,6 +1292,7 @@ int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, const void* q
   p.B = plan->B;
   p.T = plan->T;
   p.nkv = plan->nkv;
+  p.static_pct = plan->static_pct;
   p.scale_log2 = scale * kLog2e;
   p.eps = eps;
   rc = set_device(plan->device);

@@ -1,17 +1,18 @@
 """Host mirror of the device-side work split of the decode-attention kernel.
 
-The kernel (csrc/decode_attn.cu, compute_plan / chunk_unit / claim_chunk) decides on the device,
-at every call, how the keys are divided between CTAs, from the live lengths pos[b] + T. This module
-restates that arithmetic in Python so the split can be inspected and property-tested without a GPU:
+The kernel (csrc/decode_attn.cu: compute_plan, chunk_range, chunk_of, unit_at, claim_chunk) decides
+on the device, at every call, how the keys are divided between CTAs, from the live lengths
+pos[b] + T. This module restates that arithmetic so the split can be inspected and property-tested
+without a GPU:
 
 * sequence b streams Ls_b keys from the cache (L_b, or L_b - 1 when the fused prologue appends the
   last key itself) = max(1, ceil(Ls_b / 16)) pages for each kv head;
-* the pages of each pair (b, kvh), pair index q = b * nkv + kvh, are cut into chunks of 32 pages
-  (512 keys); chunks are numbered pair after pair, b-major;
-* CTA c processes chunk c first, then chunks it claims from a global counter (grid + 0, 1, 2 ...);
-  which CTA gets which dynamic chunk depends on timing, not on this plan;
-* chunk g's partial result goes to workspace slot g; the last of the pair's n chunks to finish
-  merges slots c0 .. c0 + n - 1 (a pair with a single chunk writes its output directly).
+* the pages of all pairs (b, kvh), pair index q = b * nkv + kvh, are laid end to end: T pages;
+* with P = floor(pct T / 100) (0 when P < grid), chunk k < grid is CTA k's static piece
+  [k P / grid, (k+1) P / grid); chunk k >= grid is the dynamic chunk [P + 32 (k - grid), ...)
+  clipped to T, claimed at run time;
+* a unit is a chunk's intersection with one pair; its partial result goes to workspace slot k + q,
+  and the last of the pair's n units to finish merges slots c + q for c in c0 .. c0 + n - 1.
 """
 
 from __future__ import annotations
@@ -20,57 +21,98 @@ from dataclasses import dataclass
 
 PAGE = 16
 CHUNK_PAGES = 32
-CHUNK_TOKENS = PAGE * CHUNK_PAGES
+STATIC_PCT = 100
 
 
 @dataclass(frozen=True)
-class Chunk:
-    g: int       # chunk index = workspace slot
+class Unit:
+    chunk: int
     b: int
     kvh: int
     q: int
     t0: int      # first key streamed from the cache
     t1: int      # one past the last key streamed from the cache
-    c0: int      # first chunk of the pair
-    n: int       # chunks of the pair
-    last: bool   # last chunk of the pair (owns the appended key in the fused path)
+    c0: int      # first chunk holding the pair
+    n: int       # chunks holding the pair
+    last: bool   # this unit ends the pair (owns the appended key in the fused path)
+
+    @property
+    def slot(self) -> int:
+        return self.chunk + self.q
 
 
-def chunks(lengths, nkv: int, fused: bool) -> list[Chunk]:
-    """Every chunk of one call, in index order."""
+@dataclass(frozen=True)
+class Plan:
+    npages: list
+    pstart: list
+    total_pages: int
+    static_pages: int
+    total_chunks: int
+    grid: int
+
+    def chunk_range(self, k: int):
+        G, P = self.grid, self.static_pages
+        if k < G:
+            return k * P // G, (k + 1) * P // G
+        x0 = P + (k - G) * CHUNK_PAGES
+        return x0, min(x0 + CHUNK_PAGES, self.total_pages)
+
+    def chunk_of(self, y: int) -> int:
+        G, P = self.grid, self.static_pages
+        return ((y + 1) * G - 1) // P if y < P else G + (y - P) // CHUNK_PAGES
+
+
+def plan(lengths, nkv: int, grid: int, fused: bool, static_pct: int = STATIC_PCT) -> Plan:
+    npages = [max(1, -(-((L - 1) if fused else L) // PAGE)) for L in lengths]
+    pstart = [0]
+    for n in npages:
+        pstart.append(pstart[-1] + n * nkv)
+    T = pstart[-1]
+    P = T * static_pct // 100
+    if P < grid:
+        P = 0
+    return Plan(npages, pstart, T, P, grid + -(-(T - P) // CHUNK_PAGES), grid)
+
+
+def units_of_chunk(pl: Plan, lengths, nkv: int, fused: bool, k: int) -> list[Unit]:
+    x, x1 = pl.chunk_range(k)
     out = []
-    g = 0
-    for b, L in enumerate(lengths):
-        ls = L - 1 if fused else L
-        np_ = max(1, -(-ls // PAGE))
-        nch = -(-np_ // CHUNK_PAGES)
-        for kvh in range(nkv):
-            c0 = g
-            for j in range(nch):
-                t0 = j * CHUNK_TOKENS
-                t1 = max(t0, min((j + 1) * CHUNK_TOKENS, ls))
-                out.append(Chunk(g, b, kvh, b * nkv + kvh, t0, t1, c0, nch, j == nch - 1))
-                g += 1
+    while x < x1:
+        b = max(i for i in range(len(lengths)) if pl.pstart[i] <= x)
+        np_ = pl.npages[b]
+        kvh, pg = divmod(x - pl.pstart[b], np_)
+        pair0 = pl.pstart[b] + kvh * np_
+        pair1 = pair0 + np_
+        ux1 = min(x1, pair1)
+        ls = lengths[b] - 1 if fused else lengths[b]
+        t0 = pg * PAGE
+        c0 = pl.chunk_of(pair0)
+        out.append(Unit(k, b, kvh, b * nkv + kvh, t0, max(t0, min((ux1 - pair0) * PAGE, ls)),
+                        c0, pl.chunk_of(pair1 - 1) - c0 + 1, ux1 == pair1))
+        x = ux1
     return out
 
 
-def max_units(B: int, nkv: int, max_len: int) -> int:
-    """Workspace slots a plan for caches of up to max_len keys needs (the host plan's max_units)."""
-    pages = -(-max_len // PAGE)
-    return B * nkv * (-(-pages // CHUNK_PAGES))
+def all_units(lengths, nkv: int, grid: int, fused: bool, static_pct: int = STATIC_PCT) -> list[Unit]:
+    pl = plan(lengths, nkv, grid, fused, static_pct)
+    return [u for k in range(pl.total_chunks) for u in units_of_chunk(pl, lengths, nkv, fused, k)]
+
+
+def max_units(B: int, nkv: int, max_len: int, grid: int) -> int:
+    """Workspace slots of the host plan: grid + ceil(T_max / 32) + B * nkv."""
+    pages = B * nkv * (-(-max_len // PAGE))
+    return grid + -(-pages // CHUNK_PAGES) + B * nkv
 
 
 def schedule(n_chunks: int, grid: int, speeds) -> list[list[int]]:
-    """Simulate the claiming: CTA c starts with chunk c; whenever a CTA starts a chunk it claims
-    the next one (one ahead). `speeds[c]` is CTA c's time per chunk. Returns the chunks each CTA
-    processed, to check that every chunk is taken exactly once."""
+    """Simulate the claiming: CTA c starts with piece c and claims one dynamic chunk ahead; a CTA
+    that finishes a chunk starts its claimed one and claims the next. speeds[c] is CTA c's time
+    per chunk. Returns the chunks each CTA processed."""
     import heapq
     nxt = grid
-    taken = [[] for _ in range(grid)]
-    heap = []
-    for c in range(min(grid, n_chunks)):
-        taken[c].append(c)
-        heapq.heappush(heap, (speeds[c], c))
+    taken = [[c] for c in range(grid)]
+    heap = [(speeds[c], c) for c in range(grid)]
+    heapq.heapify(heap)
     while heap:
         t, c = heapq.heappop(heap)
         if nxt < n_chunks:

@@ -5,55 +5,66 @@ from collections import defaultdict
 
 import pytest
 
-from kernel_optim_b200.plan import CHUNK_TOKENS, PAGE, chunks, max_units, schedule
+from kernel_optim_b200.plan import PAGE, all_units, max_units, plan, schedule
 
 
-def check_plan(lengths, nkv, fused, max_len=None):
-    cs = chunks(lengths, nkv, fused)
+def check_plan(lengths, nkv, grid, fused, max_len=None, static_pct=100):
+    us = all_units(lengths, nkv, grid, fused, static_pct)
     B = len(lengths)
-    assert [c.g for c in cs] == list(range(len(cs)))
-    assert len(cs) <= max_units(B, nkv, max_len or max(lengths))
+    pl = plan(lengths, nkv, grid, fused, static_pct)
+    limit = max_units(B, nkv, max_len or max(lengths), grid)
+    slots = [u.slot for u in us]
+    assert len(slots) == len(set(slots)), "two units share a workspace slot"
+    assert all(0 <= x < limit for x in slots)
+    # every chunk is non-empty, except that all pieces are empty when P = 0
+    for k in range(pl.total_chunks):
+        x0, x1 = pl.chunk_range(k)
+        assert x1 > x0 or (k < grid and pl.static_pages == 0)
     by_pair = defaultdict(list)
-    for c in cs:
-        by_pair[c.q].append(c)
-    assert set(by_pair) == set(range(B * nkv)), "a (sequence, kv head) pair has no chunk"
+    for u in us:
+        by_pair[u.q].append(u)
+    assert set(by_pair) == set(range(B * nkv)), "a (sequence, kv head) pair has no unit"
     for q, lst in by_pair.items():
         b = q // nkv
         ls = lengths[b] - 1 if fused else lengths[b]
         pos = 0
-        for c in lst:   # keys [0, Ls) covered exactly once, in order, on page boundaries
-            assert c.t0 == pos and c.t0 % PAGE == 0 and c.t1 - c.t0 <= CHUNK_TOKENS
-            pos = c.t1
+        for u in lst:   # keys [0, Ls) covered exactly once, in order, on page boundaries
+            assert u.t0 == pos and u.t0 % PAGE == 0
+            pos = u.t1
         assert pos == ls
-        assert [c.g for c in lst] == list(range(lst[0].c0, lst[0].c0 + lst[0].n))
-        assert [c.last for c in lst] == [False] * (len(lst) - 1) + [True]
-    return cs
+        # the units of a pair sit in consecutive chunks and agree on the split count
+        assert [u.chunk for u in lst] == list(range(lst[0].c0, lst[0].c0 + lst[0].n))
+        assert all(u.n == len(lst) for u in lst)
+        assert [u.last for u in lst] == [False] * (len(lst) - 1) + [True]
+    return pl, us
 
 
 @pytest.mark.parametrize("fused", [False, True])
 def test_baseline_configs(fused):
-    c2 = check_plan([4097] * 16, 8, fused)
-    assert len(c2) == 16 * 8 * (8 if fused else 9)   # 4096 or 4097 streamed keys per pair
-    check_plan([131072] * 4, 8, fused)
-    check_plan([1] * 3, 8, fused)              # only the appended key
-    check_plan([5, 130, 77], 8, fused, 136)
+    pl, _ = check_plan([4097] * 16, 8, 148, fused)
+    assert pl.static_pages == pl.total_pages and pl.total_chunks == 148   # one piece per CTA
+    pl, _ = check_plan([4097] * 16, 8, 148, fused, static_pct=90)
+    assert 0 < pl.static_pages < pl.total_pages and pl.total_chunks > 148
+    check_plan([131072] * 4, 8, 148, fused)
+    check_plan([1] * 3, 8, 148, fused)              # fewer pages than CTAs: no static pieces
+    check_plan([5, 130, 77], 8, 148, fused, 136)
 
 
-def test_random_lengths_and_heads():
+def test_random_lengths_grids_and_heads():
     rng = random.Random(0)
     for _ in range(300):
         B = rng.randint(1, 40)
         nkv = rng.choice([1, 2, 4, 8])
+        grid = rng.choice([1, 2, 7, 37, 148, 296, 1000])
         lengths = [rng.choice([1, 2, 15, 16, 17, 512, 513, rng.randint(1, 20000)]) for _ in range(B)]
-        check_plan(lengths, nkv, rng.random() < 0.5)
+        check_plan(lengths, nkv, grid, rng.random() < 0.5, static_pct=rng.choice([0, 60, 90, 100]))
 
 
 def test_dynamic_claims_take_every_chunk_once():
     rng = random.Random(1)
     for _ in range(50):
-        n = rng.randint(1, 3000)
         grid = rng.choice([1, 7, 148, 296])
+        n = grid + rng.randint(0, 3000)
         speeds = [rng.uniform(0.7, 1.3) for _ in range(grid)]
         taken = schedule(n, grid, speeds)
-        flat = sorted(g for t in taken for g in t)
-        assert flat == list(range(n))
+        assert sorted(g for t in taken for g in t) == list(range(n))
