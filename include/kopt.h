@@ -36,6 +36,7 @@ extern "C" {
 #define KOPT_ERR_ARG 1         /* bad shape, unsupported head_dim/group, bad pointer alignment */
 #define KOPT_ERR_CUDA 2        /* a CUDA runtime call failed (launch, attribute, device query) */
 #define KOPT_ERR_WORKSPACE 3   /* workspace too small for the plan */
+#define KOPT_ERR_SCRATCH 4     /* plan needs more scratch than kopt_decode_attn_fused_noalloc has */
 
 /* Bits of the device-side error word (read back with kopt_read_error). The kernels never trap:
  * a bad page id or length is recorded here and the access is skipped or clamped. */
@@ -132,6 +133,27 @@ KOPT_API int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, cons
                            const void* k_norm_w, const void* cos, const void* sin, int rope_len,
                            const kopt_kv_cache* cache, const int32_t* pos, void* out, void* q_out,
                            void* ws, float scale, float eps, void* stream);
+
+/* kopt_decode_attn_fused without a workspace argument, for callers that cannot allocate device
+ * memory for it (an engine that owns the whole memory budget and hands out only fixed buffers, a
+ * process whose allocator must not grow after start-up, a plugin host without a device allocator
+ * at the call site). This entry point has no counterpart in the reference, which always allocates
+ * its scratch (DecodeAttention.__init__). It allocates nothing: the split scratch is an 8 MiB
+ * buffer built into this library, present on every GPU that loads it until the process exits.
+ *   - Plans whose ws_bytes exceed 8 MiB are rejected with KOPT_ERR_SCRATCH (for example B = 16
+ *     sequences of up to 4097 keys need 2.7 MiB; 4 sequences of 131072 keys do not fit).
+ *   - The first call on a device resolves the buffer's device address (cudaGetSymbolAddress) with
+ *     that device current; make that first call before any stream capture.
+ *   - Every call clears the buffer's error word and split counters on `stream` before the launch.
+ *     All calls share the one buffer, so calls whose executions overlap on the GPU (other streams,
+ *     other threads) race and corrupt each other's results: serialise them.
+ *   - dev_err (device int, may be NULL) receives the KOPT_DEV_ERR_* bits of this call. */
+KOPT_API int kopt_decode_attn_fused_noalloc(const kopt_plan* plan, const void* qkv,
+                                            const void* q_norm_w, const void* k_norm_w,
+                                            const void* cos, const void* sin, int rope_len,
+                                            const kopt_kv_cache* cache, const int32_t* pos,
+                                            void* out, void* q_out, float scale, float eps,
+                                            int* dev_err, void* stream);
 
 /* Human-readable text for a KOPT_* status. */
 KOPT_API const char* kopt_strerror(int status);

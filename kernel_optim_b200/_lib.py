@@ -16,6 +16,7 @@ KOPT_OK = 0
 KOPT_ERR_ARG = 1
 KOPT_ERR_CUDA = 2
 KOPT_ERR_WORKSPACE = 3
+KOPT_ERR_SCRATCH = 4
 
 DEV_ERR_PAGE = 1
 DEV_ERR_LEN = 2
@@ -33,6 +34,7 @@ EXPORTED = (
     "kopt_decode_attn",
     "kopt_qk_norm_rope",
     "kopt_decode_attn_fused",
+    "kopt_decode_attn_fused_noalloc",
 )
 
 
@@ -93,6 +95,9 @@ _SIGS = {
                                  _i32, _i32, _i32, _i32, _i32, _f32, _vp, _i32, _vp]),
     "kopt_decode_attn_fused": (_i32, [ctypes.POINTER(Plan), _vp, _vp, _vp, _vp, _vp, _i32,
                                       ctypes.POINTER(KvCache), _vp, _vp, _vp, _vp, _f32, _f32, _vp]),
+    "kopt_decode_attn_fused_noalloc": (_i32, [ctypes.POINTER(Plan), _vp, _vp, _vp, _vp, _vp, _i32,
+                                              ctypes.POINTER(KvCache), _vp, _vp, _vp, _f32, _f32,
+                                              _vp, _vp]),
 }
 
 

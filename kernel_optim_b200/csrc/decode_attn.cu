@@ -42,6 +42,8 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <mutex>
+
 #include "kopt.h"
 
 namespace kopt {
@@ -1161,6 +1163,9 @@ const char* kopt_strerror(int status) {
     case KOPT_ERR_ARG: return "invalid argument (shape, head_dim, group, alignment or pointer)";
     case KOPT_ERR_CUDA: return "CUDA runtime call failed";
     case KOPT_ERR_WORKSPACE: return "workspace missing, misaligned or sized for another plan";
+    case KOPT_ERR_SCRATCH:
+      return "plan needs more split scratch than the 8 MiB built into the library (use "
+             "kopt_decode_attn_fused with a caller-owned workspace)";
     default: return "unknown kopt status";
   }
 }
@@ -1339,3 +1344,58 @@ int kopt_qk_norm_rope(const void* qkv, const void* q_norm_w, const void* k_norm_
 }
 
 }  // extern "C"
+
+// ====================================================================== allocation-free variant
+// Some callers cannot allocate device memory for the split scratch: an engine that owns the whole
+// memory budget and hands out only fixed buffers, a process whose allocator must not grow after
+// start-up, or a plugin host whose memory calls are not reachable from the attention call site.
+// For them the scratch of kopt_decode_attn_fused lives in a buffer built into this library.
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;   // 8 MiB, held by every GPU using the library
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_scratch_mutex;
+void* g_static_scratch_ptr[64] = {};   // device address of g_static_scratch, per device
+
+// Device address of the built-in scratch on the current device (resolved once per device).
+int static_scratch(int device, void** out) {
+  if (device < 0 || device >= 64) return KOPT_ERR_ARG;
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (g_static_scratch_ptr[device] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_static_scratch) != cudaSuccess || ptr == nullptr)
+      return KOPT_ERR_CUDA;
+    g_static_scratch_ptr[device] = ptr;
+  }
+  *out = g_static_scratch_ptr[device];
+  return KOPT_OK;
+}
+
+}  // namespace
+
+extern "C" int kopt_decode_attn_fused_noalloc(
+    const kopt_plan* plan, const void* qkv, const void* q_norm_w, const void* k_norm_w,
+    const void* cos, const void* sin, int rope_len, const kopt_kv_cache* cache,
+    const int32_t* pos, void* out, void* q_out, float scale, float eps, int* dev_err,
+    void* stream) {
+  if (plan == nullptr) return KOPT_ERR_ARG;
+  if (plan->ws_bytes > static_cast<int64_t>(kStaticScratchBytes)) return KOPT_ERR_SCRATCH;
+  int rc = set_device(plan->device);
+  if (rc) return rc;
+  void* ws = nullptr;
+  rc = static_scratch(plan->device, &ws);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The buffer keeps the previous call's contents: the error word and the split counters must
+  // start at zero (the partial-result slots need no initial value).
+  const WsLayout w = ws_layout(plan->B, plan->nkv, plan->max_units);
+  if (cudaMemsetAsync(ws, 0, static_cast<size_t>(w.ml), st) != cudaSuccess) return KOPT_ERR_CUDA;
+  rc = kopt_decode_attn_fused(plan, qkv, q_norm_w, k_norm_w, cos, sin, rope_len, cache, pos, out,
+                              q_out, ws, scale, eps, stream);
+  if (rc) return rc;
+  if (dev_err != nullptr &&
+      cudaMemcpyAsync(dev_err, ws, sizeof(int), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+    return KOPT_ERR_CUDA;
+  return KOPT_OK;
+}
