@@ -199,7 +199,7 @@ def run_ours(args):
     def step(i):
         launch(i)
         if dist is not None:
-            dist.all_gather_into_tensor(gathered, out)
+            dist.all_gather_into_tensor(gathered.view(-1, gathered.shape[-1]), out)
 
     for i in range(args.warmup):
         step(i)
@@ -311,7 +311,7 @@ def run_e2e(args, case, attn, launch, out, gathered, dist, bytes_job):
         dev_in.copy_(host_in, non_blocking=True)
         e2e_launch(i)
         if dist is not None:
-            dist.all_gather_into_tensor(gathered, out)
+            dist.all_gather_into_tensor(gathered.view(-1, gathered.shape[-1]), out)
         out_h.copy_(res, non_blocking=True)
 
     for i in range(args.warmup):

@@ -1,0 +1,191 @@
+"""Qwen3 decode engine on the B200 decode-attention step.
+
+Keeps the reference engine's surface (GodRishUniverse/kernel_optim engine/engine.py):
+
+* ``Engine(model_path)`` (engine.py:119-161) loads the checkpoint with Transformers
+  (bf16, attn_implementation="sdpa", local_files_only) and concatenates each layer's q/k/v weights
+  into one QKV weight (engine.py:148).
+* ``generate(input_ids, max_new_tokens)`` (engine.py:418-523) yields ``max_new_tokens`` lists of B
+  token ids, greedy, never stopping at EOS.
+
+What changes is the decode step (engine.py:313-341, 388-401): the per-layer ``qk_norm_rope`` +
+``attn1`` pair becomes one ``PagedDecodeAttention`` launch over a paged KV cache, and the whole step
+is captured once per shape in a CUDA graph and replayed, pipelined one step ahead of the host as in
+engine.py:509-533. Projections, norms, the MLP and the LM head run as the loaded Transformers
+modules (cuBLAS), exactly the native path's arithmetic. Prefill is the native Transformers forward
+with its DynamicCache, whose K/V are copied into the pages (prefill is not the optimised path).
+
+Multi-GPU (``group`` = a torch.distributed process group of G ranks, one GPU each): rank r keeps kv
+heads [r*nkv/G, (r+1)*nkv/G) — their QKV weight rows and their pages — runs attention for them and
+all-gathers the head outputs over NCCL before o_proj; everything after attention is replicated.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from ._lib import KoptError
+from .paged import PAGE, PagedDecodeAttention, PagedKVCache
+from .shard import gather_heads, head_range, shard_qkv_weight
+
+
+class Engine:
+    def __init__(self, model_path: str, device: str = "cuda:0", group=None):
+        from transformers import AutoModelForCausalLM
+        model = AutoModelForCausalLM.from_pretrained(
+            model_path, dtype=torch.bfloat16, attn_implementation="sdpa", local_files_only=True)
+        self._init(model.eval().to(device), device, group)
+
+    @classmethod
+    def from_model(cls, model, device: str = "cuda:0", group=None) -> "Engine":
+        """Wrap an already loaded Qwen3ForCausalLM (bf16, sdpa) instead of reading a checkpoint."""
+        self = cls.__new__(cls)
+        self._init(model.eval().to(device), device, group)
+        return self
+
+    # ------------------------------------------------------------------ construction
+    def _init(self, model, device, group):
+        torch.backends.cuda.matmul.allow_tf32 = False
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise KoptError("Engine needs a CUDA device (the decode step has no CPU path)")
+        cfg = model.config
+        self.nq, self.nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        self.d = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.nq
+        if self.d != 128 or self.nq != 4 * self.nkv:
+            raise KoptError("the decode-attention kernel needs head_dim 128 and 4 query heads per kv head")
+        self.eps = cfg.rms_norm_eps
+        self.n_layers = cfg.num_hidden_layers
+        self.model = model
+        self.group = group
+        self.world = 1 if group is None else torch.distributed.get_world_size(group)
+        self.rank = 0 if group is None else torch.distributed.get_rank(group)
+        h0, _ = head_range(self.nkv, self.rank, self.world)
+        self.nkv_l = self.nkv // self.world
+        self.nq_l = 4 * self.nkv_l
+        self.h0 = h0
+        base = model.model
+        self.embed = base.embed_tokens.weight
+        self.layers = []
+        with torch.no_grad():
+            for layer in base.layers:
+                a = layer.self_attn
+                self.layers.append(dict(
+                    mod=layer,
+                    # this rank's q/k/v rows in one weight, as engine.py:148 fuses them
+                    qkv=shard_qkv_weight(a.q_proj.weight, a.k_proj.weight, a.v_proj.weight,
+                                         self.nkv, self.rank, self.world, self.d),
+                    q_norm=a.q_norm.weight.contiguous(),
+                    k_norm=a.k_norm.weight.contiguous(),
+                ))
+        self._shape = None
+        self.graph = None
+
+    def _rope(self, n):
+        pos = torch.arange(n, device=self.device).unsqueeze(0)
+        dummy = torch.empty(1, dtype=torch.bfloat16, device=self.device)
+        cos, sin = self.model.model.rotary_emb(dummy, pos)   # exactly the native tables
+        return cos[0].contiguous(), sin[0].contiguous()
+
+    def _setup(self, B, S, N):
+        if self._shape == (B, S, N):
+            return
+        self.graph = None
+        self._shape = None
+        cap = S + N + 1
+        self.cos, self.sin = self._rope(cap)
+        pages = B * ((cap + PAGE - 1) // PAGE)
+        self.cache = PagedKVCache(self.n_layers, pages, self.nkv_l, self.d, B, cap, self.device)
+        self.cache.assign_sequential([cap] * B)
+        self.attn = PagedDecodeAttention(B, self.nq_l, self.nkv_l, self.d, self.device,
+                                         self.cache.capacity, eps=self.eps)
+        self.B, self.S, self.cap = B, S, cap
+        dev, bf = self.device, torch.bfloat16
+        self.ids = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.attn_out = torch.zeros(B, self.nq_l * self.d, dtype=bf, device=dev)
+        self.gathered = (torch.zeros(self.world, B, self.nq_l * self.d, dtype=bf, device=dev)
+                         if self.world > 1 else None)
+        self.pin_ids = torch.empty(N + 1, B, dtype=torch.int64, pin_memory=True)
+        self.events = [torch.cuda.Event() for _ in range(N + 1)]
+        self.graph = self._capture(self._step)
+        self._shape = (B, S, N)
+
+    def _capture(self, fn):
+        # warm up on a side stream (cuBLAS handles, kernel attributes), then capture once
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.pos.fill_(1)
+                fn()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        self.pos.fill_(1)
+        with torch.cuda.graph(g):
+            fn()
+        torch.cuda.synchronize(self.device)
+        return g
+
+    # ----------------------------------------------------------------------- forward
+    def _attention_out(self):
+        if self.world == 1:
+            return self.attn_out
+        return gather_heads(self.attn_out, self.gathered, self.group)
+
+    def _step(self):
+        """One decode step at positions pos[b]; argmax feeds ids, positions advance."""
+        x = F.embedding(self.ids, self.embed)
+        for i, lw in enumerate(self.layers):
+            layer = lw["mod"]
+            h = layer.input_layernorm(x)
+            qkv = torch.mm(h, lw["qkv"].t())
+            self.attn(qkv, lw["q_norm"], lw["k_norm"], self.cos, self.sin, self.cache, i, self.pos,
+                      self.attn_out)
+            x = x + layer.self_attn.o_proj(self._attention_out())
+            x = x + layer.mlp(layer.post_attention_layernorm(x))
+        logits = self.model.lm_head(self.model.model.norm(x))
+        torch.argmax(logits, dim=-1, out=self.ids)
+        self.pos.add_(1)
+
+    def _prefill(self, prompt):
+        """The native forward over the prompt; its K/V (this rank's heads) go into the pages."""
+        out = self.model(input_ids=prompt, use_cache=True)
+        self.ids.copy_(out.logits[:, -1, :].argmax(dim=-1))
+        h0 = self.h0
+        for i, layer in enumerate(out.past_key_values.layers):
+            self.cache.write_prefix(i, layer.keys[:, h0:h0 + self.nkv_l],
+                                    layer.values[:, h0:h0 + self.nkv_l])
+        self.pos.fill_(prompt.shape[1])
+
+    # ---------------------------------------------------------------------- generate
+    @torch.inference_mode()
+    def generate(self, input_ids: list[list[int]], max_new_tokens: int):
+        N = max_new_tokens
+        if N <= 0:
+            return
+        B, S = len(input_ids), len(input_ids[0])
+        if any(len(r) != S for r in input_ids):
+            raise KoptError("prompts must have equal length")
+        self._setup(B, S, N)
+        stream = torch.cuda.current_stream(self.device)
+        prompt = torch.tensor(input_ids, dtype=torch.int64).pin_memory().to(self.device, non_blocking=True)
+        self._prefill(prompt)
+        ids_h, ev = self.pin_ids, self.events
+        ids_h[0].copy_(self.ids, non_blocking=True)
+        ev[0].record(stream)
+        # queue the next step before waiting on the current one (engine.py:509-533)
+        for j in range(1, N):
+            self.graph.replay()
+            ids_h[j].copy_(self.ids, non_blocking=True)
+            ev[j].record(stream)
+            ev[j - 1].synchronize()
+            yield ids_h[j - 1].tolist()
+        ev[N - 1].synchronize()
+        yield ids_h[N - 1].tolist()
+
+    def read_error(self) -> int:
+        """Device error bits of the attention kernel since the last read (synchronises)."""
+        return self.attn.read_error()

@@ -1,0 +1,62 @@
+"""GPU: the engine end to end on a random-init Qwen3 (head_dim 128, 32 query / 8 kv heads).
+
+Judged the way the reference's judge judges (QWEN_ENGINE_CONTRACT.md, "The quality rule"): the
+emitted tokens are replayed through native Transformers Qwen3 (sdpa), teacher-forced, and every
+emitted token must be the native argmax at its position or within 2.0 logits of it.
+"""
+
+import pytest
+import torch
+
+from kernel_optim_b200.checkpoint import random_qwen3
+from kernel_optim_b200.engine import Engine
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+TIE_MARGIN = 2.0
+
+
+def replay_margins(model, prompts, generated):
+    """Teacher-forced native replay: (max logit - logit of the emitted token) per output step, and
+    whether the emitted token is the native argmax."""
+    seq = torch.cat([prompts, generated[:, :-1]], 1).to(DEV)
+    with torch.no_grad():
+        logits = model(input_ids=seq).logits.float()
+    S = prompts.shape[1]
+    lg = logits[:, S - 1:]                                   # positions that produced each output
+    chosen = lg.gather(-1, generated.to(DEV).unsqueeze(-1)).squeeze(-1)
+    return (lg.max(-1).values - chosen).cpu(), (lg.argmax(-1).cpu() == generated)
+
+
+@pytest.fixture(scope="module")
+def small_model(tmp_path_factory):
+    path = tmp_path_factory.mktemp("qwen3_small")
+    random_qwen3(path, layers=3, hidden=512, intermediate=1024, vocab=4096, seed=0)
+    return path
+
+
+def test_generate_passes_the_reference_quality_rule(small_model):
+    eng = Engine(str(small_model), DEV)
+    g = torch.Generator().manual_seed(1)
+    B, S, N = 4, 96, 64
+    prompts = torch.randint(0, 4096, (B, S), generator=g)
+    steps = list(eng.generate(prompts.tolist(), N))
+    assert len(steps) == N and all(len(s) == B for s in steps)
+    assert eng.read_error() == 0
+    generated = torch.tensor(steps).t()                      # [B, N]
+    margins, exact = replay_margins(eng.model, prompts, generated)
+    assert float(margins.max()) <= TIE_MARGIN, f"max margin {float(margins.max()):.3f}"
+    assert float(exact.float().mean()) >= 0.9, f"argmax agreement {float(exact.float().mean()):.3f}"
+
+
+def test_two_generations_do_not_share_state(small_model):
+    """Two consecutive generate calls with different prompts (OPTIMIZATION_GUIDE.md: reset
+    prompt-dependent state); the second must equal a fresh engine's output."""
+    g = torch.Generator().manual_seed(2)
+    p1 = torch.randint(0, 4096, (2, 40), generator=g).tolist()
+    p2 = torch.randint(0, 4096, (2, 40), generator=g).tolist()
+    eng = Engine(str(small_model), DEV)
+    list(eng.generate(p1, 16))
+    second = list(eng.generate(p2, 16))
+    fresh = list(Engine(str(small_model), DEV).generate(p2, 16))
+    assert second == fresh
