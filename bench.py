@@ -7,7 +7,10 @@ A step is one decode-attention call of the engine (the fused QK-norm/RoPE/KV-app
 split-K GQA attention over the paged cache) for one batch. The default workload is BASELINE config
 c2 (B=16, 4096 cached keys + 1 appended, 32 query / 8 kv heads, d=128) per GPU. For N > 1 the kv
 heads are sharded 8/N per GPU and the batch grows to 16N (weak scaling: per-GPU work fixed), and
-each step all-gathers the head outputs over NCCL, as the engine does before o_proj.
+each step all-gathers the head outputs, as the engine does before o_proj: by default inside the
+attention kernel, which stores its rows into every rank's buffer over NVLink and ends with a
+bounded wait for the peers' flags (kernel_optim_b200/gather.py); `--gather nccl` uses an NCCL
+all-gather after the kernel instead.
 
 value: whole-job algorithmic bytes / device time (TB/s), inputs resident in HBM, back-to-back
 launches timed with CUDA events on the launching stream, max over ranks. Each step reads a different
@@ -52,6 +55,8 @@ def parse_args():
                     help="c2-c4: one decode-attention call per step; c5: the engine end to end")
     ap.add_argument("--layers", type=int, default=8, help="layer caches rotated across steps")
     ap.add_argument("--layout", choices=["paged", "contiguous"], default="paged")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: all-gather fused into the attention kernel (NVLink stores) or NCCL")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--soak-ms", type=float, default=600.0,
@@ -152,10 +157,18 @@ class ClockSampler:
 class StepLauncher:
     """Prebuilt C-ABI arguments for every layer, so a step costs one ctypes call."""
 
-    def __init__(self, case, attn, layers, out, qkv=None, pos=None):
+    def __init__(self, case, attn, layers, out, qkv=None, pos=None, gather=None):
         from kernel_optim_b200 import _lib
         from kernel_optim_b200.fused import _ptr, contiguous_cache
-        self.fn = _lib.lib().kopt_decode_attn_fused
+        L = _lib.lib()
+        self.gather = gather
+        self.slot = 0
+        if gather is None:
+            self.fn = L.kopt_decode_attn_fused
+            self.dst = [_ptr(out)] * 2
+        else:
+            self.fn = L.kopt_decode_attn_fused_gather
+            self.dst = [ctypes.byref(gather.descriptor(s)) for s in range(2)]
         self.check = _lib.check
         t = case.tensors
         qkv = t["qkv"] if qkv is None else qkv
@@ -166,13 +179,20 @@ class StepLauncher:
             self.descs = [contiguous_cache(t["k_cache"][i], t["v_cache"][i]) for i in range(layers)]
         self.common = (ctypes.byref(attn.plan), _ptr(qkv), _ptr(t["q_norm_w"]),
                        _ptr(t["k_norm_w"]), _ptr(t["cos"]), _ptr(t["sin"]), t["cos"].shape[0])
-        self.tail = (_ptr(pos), _ptr(out), None, _ptr(attn.ws), ctypes.c_float(attn.scale),
-                     ctypes.c_float(attn.eps))
+        self.pos = _ptr(pos)
+        self.tail = (None, _ptr(attn.ws), ctypes.c_float(attn.scale), ctypes.c_float(attn.eps))
         self.stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         self.layers = layers
 
+    def result(self, out):
+        """The buffer holding the last step's (gathered) output."""
+        return out if self.gather is None else self.gather.out[self.slot]
+
     def __call__(self, step: int):
-        rc = self.fn(*self.common, ctypes.byref(self.descs[step % self.layers]), *self.tail, self.stream)
+        if self.gather is not None:
+            self.slot = self.gather.next_slot()
+        rc = self.fn(*self.common, ctypes.byref(self.descs[step % self.layers]), self.pos,
+                     self.dst[self.slot], *self.tail, self.stream)
         if rc:
             self.check(rc, "kopt_decode_attn_fused")
 
@@ -192,14 +212,21 @@ def run_ours(args):
     cap = t["cache"].capacity if "cache" in t else t["k_cache"].shape[3]
     attn = PagedDecodeAttention(B, case.nq, case.nkv, 128, dev, cap)
     out = torch.empty(B, case.nq * 128, dtype=torch.bfloat16, device=dev)
-    gathered = torch.empty(n, B, case.nq * 128, dtype=torch.bfloat16, device=dev) if n > 1 else None
-    launch = StepLauncher(case, attn, args.layers, out)
+    fused_gather = n > 1 and args.gather == "fused"
+    nccl_gather = n > 1 and not fused_gather
+    gathered = torch.empty(n, B, case.nq * 128, dtype=torch.bfloat16, device=dev) if nccl_gather else None
+    pg = None
+    if fused_gather:
+        from kernel_optim_b200.gather import PeerGather
+        pg = PeerGather(B, n * case.nq * 128, dev)
+    launch = StepLauncher(case, attn, args.layers, out)          # attention alone (roofline)
+    step_launch = StepLauncher(case, attn, args.layers, out, gather=pg) if pg else launch
     bytes_rank = case.algorithmic_bytes()
     bytes_job = bytes_rank * n
 
     def step(i):
-        launch(i)
-        if dist is not None:
+        step_launch(i)
+        if nccl_gather:
             dist.all_gather_into_tensor(gathered.view(-1, gathered.shape[-1]), out)
 
     for i in range(args.warmup):
@@ -258,7 +285,7 @@ def run_ours(args):
                 "kernel": "decode_attn_kernel<PAGED=1,FUSED=1>", "kernel_us": round(kern_ms * 1e3, 2),
                 "algorithmic_bytes_per_launch": bytes_rank}
 
-    e2e = None if args.no_e2e else run_e2e(args, case, attn, launch, out, gathered, dist, bytes_job)
+    e2e = None if args.no_e2e else run_e2e(args, case, attn, out, gathered, pg, dist, bytes_job)
     cpu = None
     if n == 1 and rank == 0 and not args.no_cpu_baseline and args.layout == "paged":
         cpu = cpu_baseline(case, bytes_rank)
@@ -275,7 +302,9 @@ def run_ours(args):
             "B": B, "keys_per_seq": (max(case.keys) if len(set(case.keys)) == 1 else "ragged"),
             "q_heads_per_gpu": case.nq, "kv_heads_per_gpu": case.nkv, "head_dim": 128,
             "paged": args.layout == "paged", "page_size": 16, "layers_rotated": args.layers,
-            "parallelism": f"kv-head shard x{n} + NCCL all-gather" if n > 1 else "single GPU",
+            "parallelism": (f"kv-head shard x{n} + all-gather fused into the kernel (NVLink stores)"
+                            if fused_gather else f"kv-head shard x{n} + NCCL all-gather"
+                            if n > 1 else "single GPU"),
             "l2": f"inputs larger than L2: {args.layers} layer caches of "
                   f"{bytes_rank / 1e6:.0f} MB read in rotation, one per step",
             "launch": "back-to-back C-ABI calls on one stream",
@@ -288,12 +317,14 @@ def run_ours(args):
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def run_e2e(args, case, attn, launch, out, gathered, dist, bytes_job):
+def run_e2e(args, case, attn, out, gathered, pg, dist, bytes_job):
     """Same steps through host buffers: one pinned H2D copy of the new token's qkv and positions,
     the step, and a D2H copy of the (gathered) output."""
     t = case.tensors
@@ -304,16 +335,16 @@ def run_e2e(args, case, attn, launch, out, gathered, dist, bytes_job):
     dev_in = torch.empty_like(host_in, device=out.device)
     qkv_d = dev_in[:qkv_b].view(torch.bfloat16).view(t["qkv"].shape)
     pos_d = dev_in[qkv_b:].view(torch.int32)
-    e2e_launch = StepLauncher(case, attn, args.layers, out, qkv=qkv_d, pos=pos_d)
-    res = gathered if gathered is not None else out
+    e2e_launch = StepLauncher(case, attn, args.layers, out, qkv=qkv_d, pos=pos_d, gather=pg)
+    res = gathered if gathered is not None else pg.out[0] if pg is not None else out
     out_h = torch.empty(res.shape, dtype=res.dtype, pin_memory=True)
 
     def step(i):
         dev_in.copy_(host_in, non_blocking=True)
         e2e_launch(i)
-        if dist is not None:
+        if gathered is not None:
             dist.all_gather_into_tensor(gathered.view(-1, gathered.shape[-1]), out)
-        out_h.copy_(res, non_blocking=True)
+        out_h.copy_(gathered if gathered is not None else e2e_launch.result(out), non_blocking=True)
 
     for i in range(args.warmup):
         step(i)
@@ -446,16 +477,17 @@ def run_engine(args):
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init Qwen3-4B (std 0.02, seed 0), uniform random prompt ids",
         "config": {"workload": "c5 engine generate", "B": B, "prompt": S, "new_tokens": N,
-                   "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU"},
+                   "parallelism": (f"kv-head shard x{world}, all-gather fused into the attention "
+                                   "kernel (NVLink stores)" if world > 1 else "single GPU")},
         "decode_tokens_s": round(B / (step_ms * 1e-3), 1), "decode_step_ms": round(step_ms, 4),
         "wall_s_per_generate": round(wall, 3), "device_error_bits": err,
         "gpu_launches": None, "tokens_sample": toks[0][:4],
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    eng.close()
     if dist is not None:
         dist.barrier()
-        del eng
         dist.destroy_process_group()
 
 

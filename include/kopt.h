@@ -134,6 +134,44 @@ KOPT_API int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, cons
                            const kopt_kv_cache* cache, const int32_t* pos, void* out, void* q_out,
                            void* ws, float scale, float eps, void* stream);
 
+/* ---- multi-GPU: KV-head sharding with the all-gather fused into the attention kernel --------
+ * Rank r of G (one GPU each, one node) owns kv heads [r*nkv/G, (r+1)*nkv/G) and runs
+ * kopt_decode_attn_fused_gather with a plan for its nkv/G heads. Its CTAs store each finished
+ * output row straight into every rank's gathered buffer (plain stores over NVLink through CUDA IPC
+ * mappings), at column offset r * nq_local * 128. When all its CTAs are done, the last one raises
+ * flags[w][r] = epoch + 1 on every rank w, then waits until every rank's flag in its own array has
+ * reached epoch + 1 (bounded, 1 s; KOPT_DEV_ERR_TIMEOUT in the workspace error word on expiry) and
+ * advances the epoch: once the call completes on a stream, the gathered rows of all ranks are in
+ * this rank's buffer. Every rank must make the same calls in the same order. This takes the place
+ * of a separate all-gather (NCCL) of the head outputs between attention and o_proj, which the
+ * reference does not have (it runs on one GPU); the attention itself is fused.py:209-219 as for
+ * kopt_decode_attn_fused. */
+#define KOPT_IPC_HANDLE_BYTES 64
+#define KOPT_MAX_RANKS 8
+typedef struct kopt_gather {
+  void* out[KOPT_MAX_RANKS];   /* out[w]: rank w's gathered buffer [B, row_elems] bf16 */
+  int* flags[KOPT_MAX_RANKS];  /* flags[w]: rank w's flag array [world] int32, zeroed once */
+  int* epoch;                  /* this rank's call counter (device int32, zeroed once) */
+  int32_t rank;
+  int32_t world;               /* 1 .. KOPT_MAX_RANKS */
+  int64_t row_elems;           /* elements per gathered row: nq_total * 128 */
+} kopt_gather;
+
+/* kopt_decode_attn_fused whose output goes to every rank's gathered buffer (see above); plan->T 1. */
+KOPT_API int kopt_decode_attn_fused_gather(const kopt_plan* plan, const void* qkv,
+                                           const void* q_norm_w, const void* k_norm_w,
+                                           const void* cos, const void* sin, int rope_len,
+                                           const kopt_kv_cache* cache, const int32_t* pos,
+                                           const kopt_gather* gather, void* q_out, void* ws,
+                                           float scale, float eps, void* stream);
+
+/* Device buffers shared between the ranks' processes (CUDA IPC). alloc zero-fills. */
+KOPT_API int kopt_ipc_alloc(int device, int64_t bytes, void** ptr);
+KOPT_API int kopt_ipc_free(int device, void* ptr);
+KOPT_API int kopt_ipc_get_handle(const void* ptr, void* handle /* KOPT_IPC_HANDLE_BYTES */);
+KOPT_API int kopt_ipc_open(int device, const void* handle, void** peer_ptr);
+KOPT_API int kopt_ipc_close(int device, void* peer_ptr);
+
 /* kopt_decode_attn_fused without a workspace argument, for callers that cannot allocate device
  * memory for it (an engine that owns the whole memory budget and hands out only fixed buffers, a
  * process whose allocator must not grow after start-up, a plugin host without a device allocator

@@ -35,7 +35,16 @@ EXPORTED = (
     "kopt_qk_norm_rope",
     "kopt_decode_attn_fused",
     "kopt_decode_attn_fused_noalloc",
+    "kopt_decode_attn_fused_gather",
+    "kopt_ipc_alloc",
+    "kopt_ipc_free",
+    "kopt_ipc_get_handle",
+    "kopt_ipc_open",
+    "kopt_ipc_close",
 )
+
+IPC_HANDLE_BYTES = 64
+MAX_RANKS = 8
 
 
 class KoptError(RuntimeError):
@@ -78,6 +87,19 @@ class Plan(ctypes.Structure):
     ]
 
 
+class Gather(ctypes.Structure):
+    """Mirror of struct kopt_gather."""
+
+    _fields_ = [
+        ("out", ctypes.c_void_p * MAX_RANKS),
+        ("flags", ctypes.c_void_p * MAX_RANKS),
+        ("epoch", ctypes.c_void_p),
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("row_elems", ctypes.c_int64),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -98,6 +120,14 @@ _SIGS = {
     "kopt_decode_attn_fused_noalloc": (_i32, [ctypes.POINTER(Plan), _vp, _vp, _vp, _vp, _vp, _i32,
                                               ctypes.POINTER(KvCache), _vp, _vp, _vp, _f32, _f32,
                                               _vp, _vp]),
+    "kopt_decode_attn_fused_gather": (_i32, [ctypes.POINTER(Plan), _vp, _vp, _vp, _vp, _vp, _i32,
+                                             ctypes.POINTER(KvCache), _vp, ctypes.POINTER(Gather),
+                                             _vp, _vp, _f32, _f32, _vp]),
+    "kopt_ipc_alloc": (_i32, [_i32, _i64, ctypes.POINTER(_vp)]),
+    "kopt_ipc_free": (_i32, [_i32, _vp]),
+    "kopt_ipc_get_handle": (_i32, [_vp, _vp]),
+    "kopt_ipc_open": (_i32, [_i32, _vp, ctypes.POINTER(_vp)]),
+    "kopt_ipc_close": (_i32, [_i32, _vp]),
 }
 
 

@@ -41,6 +41,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include <mutex>
 
@@ -57,6 +58,7 @@ constexpr int kTile = kPage * kNW;      // tokens per pipeline stage
 constexpr int kStages = 3;
 constexpr int kThreads = kNW * 32;
 constexpr int kMaxB = 256;
+constexpr int kMaxRanks = KOPT_MAX_RANKS;   // fused gather: ranks of one node
 constexpr int kBoxBytes = kPage * kHalf * 2;   // 2 KiB: one TMA box
 constexpr int kChunkPages = 32;                // dynamic chunk: 512 keys of the page line
 constexpr int kDefaultStaticPct = 100;         // share of the page line split statically
@@ -81,7 +83,15 @@ struct Params {
   long long sb, sh;      // contiguous strides (elements)
   const int* bt;         // block table or nullptr
   const int* pos;        // [B]
-  bf16* out;             // [B*T, nq*128]
+  bf16* out;             // [B*T, nq*128] (when world == 0)
+  // fused all-gather (world > 0): row b, head h of this rank go to out_peer[w] + b*out_row +
+  // out_col + h*128 on every rank w; then flag_peer[w][rank] = epoch + 1
+  bf16* out_peer[kMaxRanks];
+  int* flag_peer[kMaxRanks];
+  int* epoch;            // this rank's call counter, advanced by the last CTA
+  long long out_row;     // elements per output row
+  int out_col;           // this rank's first column
+  int rank, world;       // world == 0: no gather, write `out`
   float* ws_o;           // [max_units, 4, 128]
   float2* ws_ml;         // [max_units, 4]
   int* ws_cnt;           // [B * nkv]
@@ -404,6 +414,46 @@ __device__ __forceinline__ long long row_offset(const Params& p, int b, int kvh,
   }
   return static_cast<long long>(b) * p.sb + static_cast<long long>(kvh) * p.sh +
          static_cast<long long>(t) * kD;
+}
+
+// Fused gather, run by the last CTA of this rank once every CTA's rows are out: raise this rank's
+// flag on every rank (release at system scope, after a system fence covering the rows that the
+// other CTAs ordered before their counter increment), then wait until every rank's flag for this
+// call is up here (acquire; bounded at 1 s, KOPT_DEV_ERR_TIMEOUT on expiry), so that this
+// kernel's completion means the whole gathered row block has landed in local memory. The peers are
+// other GPUs running the same kernel; nothing here waits on work of this GPU.
+__device__ __noinline__ void gather_signal_and_wait(const Params& p) {
+  __threadfence_system();
+  const int e = *p.epoch + 1;
+  for (int w = 0; w < p.world; ++w)
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p.flag_peer[w] + p.rank), "r"(e)
+                 : "memory");
+  const int* mine = p.flag_peer[p.rank];
+  const unsigned long long t0 = globaltimer();
+  for (int w = 0; w < p.world; ++w) {
+    while (true) {
+      int f;
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(f) : "l"(mine + w) : "memory");
+      if (f >= e) break;
+      if (globaltimer() - t0 > kTimeoutNs) {
+        atomicOr(p.ws_err, KOPT_DEV_ERR_TIMEOUT);
+        break;
+      }
+    }
+  }
+  *p.epoch = e;
+}
+
+// Final output of (sequence b, query head h, dims d, d+1): to `out`, or, for the fused gather, to
+// this rank's columns of every rank's gathered buffer (plain stores; peers over NVLink).
+__device__ __forceinline__ void store_out(const Params& p, int b, int h, int d, float x, float y) {
+  const uint32_t v = pack_bf16(x, y);
+  const long long off = static_cast<long long>(b) * p.out_row + p.out_col + h * kD + d;
+  if (p.world == 0) {
+    *reinterpret_cast<uint32_t*>(p.out + off) = v;
+  } else {
+    for (int w = 0; w < p.world; ++w) *reinterpret_cast<uint32_t*>(p.out_peer[w] + off) = v;
+  }
 }
 
 // ---------------------------------------------------------------- consumer: one 16-token page
@@ -736,8 +786,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
       }
     }
     const float inv = 1.0f / L;
-    bf16* dst = p.out + static_cast<long long>(b) * p.T * nq * kD + (kvh * kGroup + r) * kD + d;
-    *reinterpret_cast<uint32_t*>(dst) = pack_bf16(O.x * inv, O.y * inv);
+    store_out(p, b, kvh * kGroup + r, d, O.x * inv, O.y * inv);
     if (ctid == 0) atomicExch(&p.ws_cnt[q], 0);
   };
   // thread 0: a partial written but not yet released (fence + counter), and a pair whose
@@ -915,9 +964,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
       O.y += f * ow.y;
     }
     if (U.n == 1) {
-      bf16* dst = p.out + static_cast<long long>(U.b) * p.T * nq * kD + (U.kvh * kGroup + r) * kD + d;
       const float inv = 1.0f / Lsum;
-      *reinterpret_cast<uint32_t*>(dst) = pack_bf16(O.x * inv, O.y * inv);
+      store_out(p, U.b, U.kvh * kGroup + r, d, O.x * inv, O.y * inv);
     } else {
       const long long slot = U.slot;
       *reinterpret_cast<float2*>(&p.ws_o[(slot * kGroup + r) * kD + d]) = O;
@@ -946,12 +994,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
     for (int k = issued > kStages ? issued - kStages : 0; k < issued; ++k)
       mbar_wait(smem_u32(&s.full[k % kStages][warp]), (k / kStages) & 1, s, p.ws_err, false);
   }
-  // The last CTA to finish (all claims made) resets the chunk counter for the next call.
+  // The last CTA to finish (all claims made) resets the chunk counter for the next call; with the
+  // fused gather it also tells every rank that all of this rank's rows have landed there.
+  if (p.world > 0) named_bar(1, kNW * 32);   // every output store of this CTA is issued
   if (threadIdx.x == 0) {
-    __threadfence();
+    if (p.world > 0) __threadfence_system();   // this CTA's rows visible to the peers
+    else __threadfence();
     if (atomicAdd(p.ws_err + 2, 1) == static_cast<int>(gridDim.x) - 1) {
       atomicExch(p.ws_err + 1, 0);
       atomicExch(p.ws_err + 2, 0);
+      if (p.world > 0) gather_signal_and_wait(p);
     }
   }
 }
@@ -1256,6 +1308,9 @@ int kopt_decode_attn(const kopt_plan* plan, const void* q, const kopt_kv_cache* 
   p.q = static_cast<const bf16*>(q);
   p.pos = pos;
   p.out = static_cast<bf16*>(out);
+  p.out_row = static_cast<long long>(plan->T) * plan->nkv * kGroup * kD;
+  p.out_col = 0;
+  p.world = 0;
   p.B = plan->B;
   p.T = plan->T;
   p.nkv = plan->nkv;
@@ -1268,15 +1323,20 @@ int kopt_decode_attn(const kopt_plan* plan, const void* q, const kopt_kv_cache* 
   return p.bt ? launch_attn<true, false>(plan, p, stream) : launch_attn<false, false>(plan, p, stream);
 }
 
-int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, const void* q_norm_w,
-                           const void* k_norm_w, const void* cos, const void* sin, int rope_len,
-                           const kopt_kv_cache* cache, const int32_t* pos, void* out, void* q_out,
-                           void* ws, float scale, float eps, void* stream) {
+}  // extern "C"
+
+namespace {
+// Shared by kopt_decode_attn_fused (g == nullptr: write `out`) and kopt_decode_attn_fused_gather.
+int fused_launch(const kopt_plan* plan, const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                 const void* cos, const void* sin, int rope_len, const kopt_kv_cache* cache,
+                 const int32_t* pos, void* out, const kopt_gather* g, void* q_out, void* ws,
+                 float scale, float eps, void* stream) {
   if (plan == nullptr || qkv == nullptr || q_norm_w == nullptr || k_norm_w == nullptr ||
-      cos == nullptr || sin == nullptr || pos == nullptr || out == nullptr || rope_len < 1)
+      cos == nullptr || sin == nullptr || pos == nullptr || (g == nullptr && out == nullptr) ||
+      rope_len < 1)
     return KOPT_ERR_ARG;
-  if (!aligned16(qkv) || !aligned16(out) || (q_out && !aligned16(q_out)) || !aligned16(cos) ||
-      !aligned16(sin) || (reinterpret_cast<uintptr_t>(q_norm_w) & 7) ||
+  if (!aligned16(qkv) || (out && !aligned16(out)) || (q_out && !aligned16(q_out)) ||
+      !aligned16(cos) || !aligned16(sin) || (reinterpret_cast<uintptr_t>(q_norm_w) & 7) ||
       (reinterpret_cast<uintptr_t>(k_norm_w) & 7))
     return KOPT_ERR_ARG;
   Params p{};
@@ -1293,7 +1353,30 @@ int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, const void* q
   p.rope_len = rope_len;
   p.q_out = static_cast<bf16*>(q_out);
   p.pos = pos;
-  p.out = static_cast<bf16*>(out);
+  const long long heads = static_cast<long long>(plan->nkv) * kGroup * kD;   // this rank's columns
+  if (g == nullptr) {
+    p.out = static_cast<bf16*>(out);
+    p.out_row = static_cast<long long>(plan->T) * heads;
+    p.out_col = 0;
+    p.world = 0;
+  } else {
+    if (g->world < 1 || g->world > kMaxRanks || g->rank < 0 || g->rank >= g->world ||
+        g->epoch == nullptr || g->row_elems < (g->rank + 1) * heads || g->row_elems % 8 != 0 ||
+        plan->T != 1)
+      return KOPT_ERR_ARG;
+    for (int w = 0; w < g->world; ++w) {
+      if (g->out[w] == nullptr || g->flags[w] == nullptr || !aligned16(g->out[w]))
+        return KOPT_ERR_ARG;
+      p.out_peer[w] = static_cast<bf16*>(g->out[w]);
+      p.flag_peer[w] = g->flags[w];
+    }
+    p.out = nullptr;
+    p.epoch = g->epoch;
+    p.rank = g->rank;
+    p.world = g->world;
+    p.out_row = g->row_elems;
+    p.out_col = static_cast<int>(g->rank * heads);
+  }
   p.B = plan->B;
   p.T = plan->T;
   p.nkv = plan->nkv;
@@ -1305,6 +1388,70 @@ int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, const void* q
   rc = encode_kv_maps(p, plan->B, plan->nkv);
   if (rc) return rc;
   return p.bt ? launch_attn<true, true>(plan, p, stream) : launch_attn<false, true>(plan, p, stream);
+}
+}  // namespace
+
+extern "C" {
+
+int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, const void* q_norm_w,
+                           const void* k_norm_w, const void* cos, const void* sin, int rope_len,
+                           const kopt_kv_cache* cache, const int32_t* pos, void* out, void* q_out,
+                           void* ws, float scale, float eps, void* stream) {
+  return fused_launch(plan, qkv, q_norm_w, k_norm_w, cos, sin, rope_len, cache, pos, out, nullptr,
+                      q_out, ws, scale, eps, stream);
+}
+
+int kopt_decode_attn_fused_gather(const kopt_plan* plan, const void* qkv, const void* q_norm_w,
+                                  const void* k_norm_w, const void* cos, const void* sin,
+                                  int rope_len, const kopt_kv_cache* cache, const int32_t* pos,
+                                  const kopt_gather* gather, void* q_out, void* ws, float scale,
+                                  float eps, void* stream) {
+  if (gather == nullptr) return KOPT_ERR_ARG;
+  return fused_launch(plan, qkv, q_norm_w, k_norm_w, cos, sin, rope_len, cache, pos, nullptr,
+                      gather, q_out, ws, scale, eps, stream);
+}
+
+int kopt_ipc_alloc(int device, int64_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes <= 0) return KOPT_ERR_ARG;
+  int rc = set_device(device);
+  if (rc) return rc;
+  if (cudaMalloc(ptr, static_cast<size_t>(bytes)) != cudaSuccess) return KOPT_ERR_CUDA;
+  if (cudaMemset(*ptr, 0, static_cast<size_t>(bytes)) != cudaSuccess) return KOPT_ERR_CUDA;
+  return cudaDeviceSynchronize() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+}
+
+int kopt_ipc_free(int device, void* ptr) {
+  if (ptr == nullptr) return KOPT_ERR_ARG;
+  int rc = set_device(device);
+  if (rc) return rc;
+  return cudaFree(ptr) == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+}
+
+int kopt_ipc_get_handle(const void* ptr, void* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == KOPT_IPC_HANDLE_BYTES, "IPC handle size");
+  if (ptr == nullptr || handle == nullptr) return KOPT_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)) != cudaSuccess) return KOPT_ERR_CUDA;
+  memcpy(handle, &h, sizeof(h));
+  return KOPT_OK;
+}
+
+int kopt_ipc_open(int device, const void* handle, void** peer_ptr) {
+  if (handle == nullptr || peer_ptr == nullptr) return KOPT_ERR_ARG;
+  int rc = set_device(device);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  if (cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return KOPT_ERR_CUDA;
+  return KOPT_OK;
+}
+
+int kopt_ipc_close(int device, void* peer_ptr) {
+  if (peer_ptr == nullptr) return KOPT_ERR_ARG;
+  int rc = set_device(device);
+  if (rc) return rc;
+  return cudaIpcCloseMemHandle(peer_ptr) == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
 }
 
 int kopt_qk_norm_rope(const void* qkv, const void* q_norm_w, const void* k_norm_w,

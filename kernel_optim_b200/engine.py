@@ -15,9 +15,11 @@ engine.py:509-533. Projections, norms, the MLP and the LM head run as the loaded
 modules (cuBLAS), exactly the native path's arithmetic. Prefill is the native Transformers forward
 with its DynamicCache, whose K/V are copied into the pages (prefill is not the optimised path).
 
-Multi-GPU (``group`` = a torch.distributed process group of G ranks, one GPU each): rank r keeps kv
-heads [r*nkv/G, (r+1)*nkv/G) — their QKV weight rows and their pages — runs attention for them and
-all-gathers the head outputs over NCCL before o_proj; everything after attention is replicated.
+Multi-GPU (``group`` = a torch.distributed process group of G ranks, one GPU each, one node): rank r
+keeps kv heads [r*nkv/G, (r+1)*nkv/G) — their QKV weight rows and their pages — and runs attention
+for them with the all-gather fused into the kernel (kernel_optim_b200/gather.py): every rank's rows
+land in every rank's [B, nq*128] buffer over NVLink, which feeds o_proj directly; everything after
+attention is replicated, so every rank emits the same tokens.
 """
 
 from __future__ import annotations
@@ -27,7 +29,8 @@ import torch.nn.functional as F
 
 from ._lib import KoptError
 from .paged import PAGE, PagedDecodeAttention, PagedKVCache
-from .shard import gather_heads, head_range, shard_qkv_weight
+from .gather import PeerGather, slot_of
+from .shard import head_range, shard_qkv_weight
 
 
 class Engine:
@@ -81,6 +84,7 @@ class Engine:
                 ))
         self._shape = None
         self.graph = None
+        self.pg = None
 
     def _rope(self, n):
         pos = torch.arange(n, device=self.device).unsqueeze(0)
@@ -105,8 +109,11 @@ class Engine:
         self.ids = torch.zeros(B, dtype=torch.int64, device=dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
         self.attn_out = torch.zeros(B, self.nq_l * self.d, dtype=bf, device=dev)
-        self.gathered = (torch.zeros(self.world, B, self.nq_l * self.d, dtype=bf, device=dev)
-                         if self.world > 1 else None)
+        if self.pg is not None:
+            self.pg.close()
+            self.pg = None
+        if self.world > 1:
+            self.pg = PeerGather(B, self.nq * self.d, dev, self.group)
         self.pin_ids = torch.empty(N + 1, B, dtype=torch.int64, pin_memory=True)
         self.events = [torch.cuda.Event() for _ in range(N + 1)]
         self.graph = self._capture(self._step)
@@ -130,10 +137,14 @@ class Engine:
         return g
 
     # ----------------------------------------------------------------------- forward
-    def _attention_out(self):
-        if self.world == 1:
+    def _attention(self, i, lw, qkv):
+        """Attention of layer i; returns [B, nq*128] (all heads, gathered when sharded)."""
+        if self.pg is None:
+            self.attn(qkv, lw["q_norm"], lw["k_norm"], self.cos, self.sin, self.cache, i, self.pos,
+                      self.attn_out)
             return self.attn_out
-        return gather_heads(self.attn_out, self.gathered, self.group)
+        return self.pg.attend(self.attn, qkv, lw["q_norm"], lw["k_norm"], self.cos, self.sin,
+                              self.cache, i, self.pos, slot_of(i, self.n_layers))
 
     def _step(self):
         """One decode step at positions pos[b]; argmax feeds ids, positions advance."""
@@ -142,9 +153,7 @@ class Engine:
             layer = lw["mod"]
             h = layer.input_layernorm(x)
             qkv = torch.mm(h, lw["qkv"].t())
-            self.attn(qkv, lw["q_norm"], lw["k_norm"], self.cos, self.sin, self.cache, i, self.pos,
-                      self.attn_out)
-            x = x + layer.self_attn.o_proj(self._attention_out())
+            x = x + layer.self_attn.o_proj(self._attention(i, lw, qkv))
             x = x + layer.mlp(layer.post_attention_layernorm(x))
         logits = self.model.lm_head(self.model.model.norm(x))
         torch.argmax(logits, dim=-1, out=self.ids)
@@ -189,3 +198,11 @@ class Engine:
     def read_error(self) -> int:
         """Device error bits of the attention kernel since the last read (synchronises)."""
         return self.attn.read_error()
+
+    def close(self) -> None:
+        """Release the cross-rank gather buffers (collective when sharded)."""
+        self.graph = None
+        self._shape = None
+        if self.pg is not None:
+            self.pg.close()
+            self.pg = None

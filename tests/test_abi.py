@@ -44,6 +44,8 @@ def test_struct_layouts_match_header():
     # kopt_kv_cache: 2 pointers, 2 int64, 2 int32, pointer, 2 int32 -> 56 bytes on LP64
     assert ctypes.sizeof(_lib.KvCache) == 56
     assert ctypes.sizeof(_lib.Plan) == 56
+    # kopt_gather: 8 + 8 pointers, pointer, 2 int32, int64 -> 152 bytes
+    assert ctypes.sizeof(_lib.Gather) == 152
 
 
 @pytest.mark.parametrize("args", [

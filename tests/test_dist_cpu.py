@@ -52,7 +52,7 @@ def _worker(rank, world, port, q):
         assert torch.allclose(qkv[:, nq_l * D:(nq_l + (h1 - h0)) * D], (x @ wk.t())[:, h0 * D:h1 * D])
         local = decode_attn_fp32(qh, k[:, h0:h1], v[:, h0:h1], lens).reshape(B, -1)
         out = gather_heads(local, torch.empty(world, B, local.shape[1]))
-        q.put((rank, out))
+        q.put((rank, out.numpy()))   # by value: a queued tensor's shared memory dies with its sender
     finally:
         dist.destroy_process_group()
 
@@ -66,7 +66,7 @@ def test_kv_head_shard_and_gather_reproduce_unsharded_attention():
     for p in procs:
         p.start()
     try:
-        results = dict(q.get(timeout=120) for _ in range(world))
+        results = {r: torch.from_numpy(a) for r, a in (q.get(timeout=120) for _ in range(world))}
     finally:
         for p in procs:
             p.join(timeout=60)

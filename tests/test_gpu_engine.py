@@ -60,3 +60,61 @@ def test_two_generations_do_not_share_state(small_model):
     second = list(eng.generate(p2, 16))
     fresh = list(Engine(str(small_model), DEV).generate(p2, 16))
     assert second == fresh
+
+
+def _engine_worker(rank, world, port, path, prompts, n, q):
+    import os
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        eng = Engine(path, f"cuda:{rank}", group=dist.group.WORLD)
+        steps = list(eng.generate(prompts, n))
+        err = eng.read_error()
+        eng.close()
+        q.put((rank, (steps, err)))
+    except Exception as e:  # surfaced by the parent
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_kv_head_sharded_engine_on_two_gpus(small_model):
+    """Two ranks, 4 kv heads each, attention with the fused NVLink all-gather: both ranks emit the
+    same tokens, and they pass the quality rule against the native model."""
+    import socket
+
+    import torch.multiprocessing as mp
+    from transformers import AutoModelForCausalLM
+    g = torch.Generator().manual_seed(3)
+    B, S, N = 4, 64, 32
+    prompts = torch.randint(0, 4096, (B, S), generator=g)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_engine_worker, args=(r, 2, port, str(small_model), prompts.tolist(),
+                                                      N, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        res = dict(q.get(timeout=300) for _ in range(2))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(2):
+        assert not isinstance(res[r], str), f"rank {r}: {res[r]}"
+        assert res[r][1] == 0, f"rank {r}: device error bits {res[r][1]}"
+    assert res[0][0] == res[1][0]
+    model = AutoModelForCausalLM.from_pretrained(str(small_model), dtype=torch.bfloat16,
+                                                 attn_implementation="sdpa").to(DEV).eval()
+    generated = torch.tensor(res[0][0]).t()
+    margins, exact = replay_margins(model, prompts, generated)
+    assert float(margins.max()) <= TIE_MARGIN, f"max margin {float(margins.max()):.3f}"
+    assert float(exact.float().mean()) >= 0.9, f"argmax agreement {float(exact.float().mean()):.3f}"
