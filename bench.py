@@ -57,6 +57,9 @@ def parse_args():
     ap.add_argument("--layout", choices=["paged", "contiguous"], default="paged")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="N > 1: all-gather fused into the attention kernel (NVLink stores) or NCCL")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="launch without programmatic dependent launch (each call waits for the "
+                         "previous kernel before it starts)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--soak-ms", type=float, default=600.0,
@@ -210,7 +213,8 @@ def run_ours(args):
     t = case.tensors
     B = case.B
     cap = t["cache"].capacity if "cache" in t else t["k_cache"].shape[3]
-    attn = PagedDecodeAttention(B, case.nq, case.nkv, 128, dev, cap)
+    # consecutive calls read different layers' caches, so each may overlap the previous one
+    attn = PagedDecodeAttention(B, case.nq, case.nkv, 128, dev, cap, overlap_prev=not args.no_overlap)
     out = torch.empty(B, case.nq * 128, dtype=torch.bfloat16, device=dev)
     fused_gather = n > 1 and args.gather == "fused"
     nccl_gather = n > 1 and not fused_gather
@@ -307,7 +311,9 @@ def run_ours(args):
                             if n > 1 else "single GPU"),
             "l2": f"inputs larger than L2: {args.layers} layer caches of "
                   f"{bytes_rank / 1e6:.0f} MB read in rotation, one per step",
-            "launch": "back-to-back C-ABI calls on one stream",
+            "launch": "back-to-back C-ABI calls on one stream" + (
+                "" if args.no_overlap else ", programmatic dependent launch (each call's split "
+                "and first page copies overlap the previous call's end)"),
         },
         "roofline": roofline,
         "cpu_baseline": cpu,
@@ -325,42 +331,80 @@ def run_ours(args):
 
 
 def run_e2e(args, case, attn, out, gathered, pg, dist, bytes_job):
-    """Same steps through host buffers: one pinned H2D copy of the new token's qkv and positions,
-    the step, and a D2H copy of the (gathered) output."""
+    """Same steps through host buffers, pipelined the way a server runs them: each step's qkv and
+    positions are copied from pinned host memory on an H2D stream while the step before computes,
+    and each step's (gathered) output is copied back on a D2H stream while the step after
+    computes. Two device buffers of each, ordered by events; every step's copies are inside the
+    timed region."""
     t = case.tensors
+    dev = out.device
     qkv_b = t["qkv"].numel() * 2
     host_in = torch.empty(qkv_b + t["pos"].numel() * 4, dtype=torch.uint8, pin_memory=True)
     host_in[:qkv_b].view(torch.bfloat16).copy_(t["qkv"].reshape(-1).cpu())
     host_in[qkv_b:].view(torch.int32).copy_(t["pos"].cpu())
-    dev_in = torch.empty_like(host_in, device=out.device)
-    qkv_d = dev_in[:qkv_b].view(torch.bfloat16).view(t["qkv"].shape)
-    pos_d = dev_in[qkv_b:].view(torch.int32)
-    e2e_launch = StepLauncher(case, attn, args.layers, out, qkv=qkv_d, pos=pos_d, gather=pg)
-    res = gathered if gathered is not None else pg.out[0] if pg is not None else out
-    out_h = torch.empty(res.shape, dtype=res.dtype, pin_memory=True)
+    dev_in = [torch.empty_like(host_in, device=dev) for _ in range(2)]
+    outs = [out, torch.empty_like(out)]
+    gath = [gathered, torch.empty_like(gathered)] if gathered is not None else None
+    launchers = [StepLauncher(case, attn, args.layers, outs[j],
+                              qkv=dev_in[j][:qkv_b].view(torch.bfloat16).view(t["qkv"].shape),
+                              pos=dev_in[j][qkv_b:].view(torch.int32), gather=pg)
+                 for j in range(2)]
+    res0 = gath[0] if gath is not None else pg.out[0] if pg is not None else out
+    out_h = [torch.empty(res0.shape, dtype=res0.dtype, pin_memory=True) for _ in range(2)]
+    compute = torch.cuda.current_stream(dev)
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]      # step's kernel(s) finished with its buffers
+    out_free = [torch.cuda.Event() for _ in range(2)]  # step's output copied to the host
+    used = [False, False]
 
     def step(i):
-        dev_in.copy_(host_in, non_blocking=True)
-        e2e_launch(i)
-        if gathered is not None:
-            dist.all_gather_into_tensor(gathered.view(-1, gathered.shape[-1]), out)
-        out_h.copy_(gathered if gathered is not None else e2e_launch.result(out), non_blocking=True)
+        j = i % 2
+        with torch.cuda.stream(h2d):
+            if used[j]:
+                h2d.wait_event(done[j])
+            dev_in[j].copy_(host_in, non_blocking=True)
+            in_ready[j].record(h2d)
+        compute.wait_event(in_ready[j])
+        if used[j]:
+            compute.wait_event(out_free[j])
+        if pg is not None and used[1 - j]:
+            # peers write the next step's rows into this rank's other slot: its copy must be out
+            compute.wait_event(out_free[1 - j])
+        launchers[j](i)
+        if gath is not None:
+            dist.all_gather_into_tensor(gath[j].view(-1, gath[j].shape[-1]), outs[j])
+        res = gath[j] if gath is not None else launchers[j].result(outs[j])
+        done[j].record(compute)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(done[j])
+            out_h[j].copy_(res, non_blocking=True)
+            out_free[j].record(d2h)
+        used[j] = True
+
+    def drain():
+        compute.wait_stream(h2d)
+        compute.wait_stream(d2h)
 
     for i in range(args.warmup):
         step(i)
+    drain()
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    e0.record(compute)
+    h2d.wait_event(e0)                                  # no copy starts before the clock
     for i in range(args.steps):
         step(i)
-    e1.record()
+    drain()
+    e1.record(compute)
     torch.cuda.synchronize()
     ms = max_over_ranks(dist, e0.elapsed_time(e1)) / args.steps
     return {"value": round(bytes_job / (ms * 1e-3) / 1e12, 4), "unit": "TB/s",
             "us_per_call": round(ms * 1e3, 2),
-            "h2d_bytes_per_step": host_in.numel(), "d2h_bytes_per_step": out_h.numel() * 2}
+            "h2d_bytes_per_step": host_in.numel(), "d2h_bytes_per_step": out_h[0].numel() * 2,
+            "pipeline": "H2D of step i+1 and D2H of step i-1 overlap step i (two streams, events)"}
 
 
 # --------------------------------------------------------------------------- CPU reference
@@ -441,7 +485,8 @@ def run_engine(args):
     B, S, N = 32, 1024, 256
     model = random_model(QWEN3_4B["layers"], QWEN3_4B["hidden"], QWEN3_4B["intermediate"],
                          QWEN3_4B["vocab"], seed=0, device=dev)
-    eng = Engine.from_model(model, dev, group=dist.group.WORLD if dist is not None else None)
+    eng = Engine.from_model(model, dev, group=dist.group.WORLD if dist is not None else None,
+                            overlap=not args.no_overlap)
     g = torch.Generator().manual_seed(5)
     prompts = torch.randint(0, QWEN3_4B["vocab"], (B, S), generator=g).tolist()
     for _ in range(max(1, args.warmup)):
@@ -477,6 +522,7 @@ def run_engine(args):
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init Qwen3-4B (std 0.02, seed 0), uniform random prompt ids",
         "config": {"workload": "c5 engine generate", "B": B, "prompt": S, "new_tokens": N,
+                   "overlap_prev": not args.no_overlap,
                    "parallelism": (f"kv-head shard x{world}, all-gather fused into the attention "
                                    "kernel (NVLink stores)" if world > 1 else "single GPU")},
         "decode_tokens_s": round(B / (step_ms * 1e-3), 1), "decode_step_ms": round(step_ms, 4),

@@ -85,9 +85,19 @@ typedef struct kopt_plan {
   int32_t chunk_tokens;      /* keys per dynamically scheduled chunk */
   int32_t static_pct;        /* share of the page line split statically, one piece per CTA
                                 (environment KOPT_STATIC_PCT overrides the default at plan time) */
-  int32_t reserved;
+  int32_t flags;             /* KOPT_PLAN_* bits: 0 from kopt_decode_attn_plan, set by the caller */
   int64_t ws_bytes;          /* workspace bytes the caller must provide (zeroed once) */
 } kopt_plan;
+
+/* plan->flags bit: launch the attention kernel with programmatic dependent launch, so that its
+ * CTAs take the SMs that the kernel before it on the stream leaves, and lay out the work split and
+ * issue the first K/V page copies before waiting for that kernel to complete. Set it only when the
+ * kernel right before the call on its stream writes none of pos, the block table and the cache
+ * rows [0, pos[b]) of this call (the fused entry points; the unfused one waits before reading
+ * anything): e.g. the QKV projection GEMM of a decode step, or another decode-attention call for a
+ * different layer. qkv, the norm weights, the RoPE tables, the workspace and the outputs are only
+ * touched after the wait. */
+#define KOPT_PLAN_OVERLAP_PREV 1
 
 /* Plan a decode-attention launch: B sequences of at most max_len keys, T query tokens each
  * (T == 1), nq = 4 * nkv query heads of dim d == 128. target_ctas <= 0 launches one CTA per

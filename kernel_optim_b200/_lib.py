@@ -18,6 +18,8 @@ KOPT_ERR_CUDA = 2
 KOPT_ERR_WORKSPACE = 3
 KOPT_ERR_SCRATCH = 4
 
+PLAN_OVERLAP_PREV = 1
+
 DEV_ERR_PAGE = 1
 DEV_ERR_LEN = 2
 DEV_ERR_TIMEOUT = 4
@@ -82,7 +84,7 @@ class Plan(ctypes.Structure):
         ("max_len", ctypes.c_int32),
         ("chunk_tokens", ctypes.c_int32),
         ("static_pct", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
         ("ws_bytes", ctypes.c_int64),
     ]
 

@@ -129,6 +129,7 @@ struct __align__(1024) Smem {
   int merge_go, mq, mc0, mn, mb, mkvh;  // a pair whose partials this CTA merges now
   int unext[12];                        // the look-ahead unit, parked across the tile loop
   int have_next;
+  int err_bits;                         // errors found before the wait (reported at the end)
   volatile int abort;
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + slack to align the base to 1 KiB
@@ -210,6 +211,15 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   return pol;
+}
+
+// Programmatic dependent launch. wait: block until the kernels this launch may overlap have
+// completed and their writes are visible (a no-op for a launch without the attribute).
+// launch_dependents: let the next kernel on the stream, if launched with the attribute, start
+// placing its CTAs (they run on SMs as this kernel's CTAs leave them).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -311,7 +321,8 @@ __device__ void compute_plan(const Params& p, Smem& s, int lane) {
     const int Ls = FUSED ? L - 1 : L;
     s.npages[b] = Ls > 0 ? ceil_div_i(Ls, kPage) : 1;
   }
-  if (err && blockIdx.x == 0) atomicOr(p.ws_err, err);
+  err = __reduce_or_sync(0xffffffffu, err);
+  if (lane == 0) s.err_bits = err;
   __syncwarp();
   int carry = 0;
   for (int base = 0; base < p.B; base += 32) {
@@ -643,7 +654,7 @@ struct Issuer {
     if (lane == 0) {
       const uint32_t fb = smem_u32(&s.full[slot][warp]);
       if (!ok) {
-        atomicOr(p.ws_err, KOPT_DEV_ERR_PAGE);
+        atomicOr(&s.err_bits, KOPT_DEV_ERR_PAGE);
         mbar_arrive_expect_tx(fb, 0);   // completes the phase without data
         return;
       }
@@ -675,6 +686,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = p.nkv * kGroup;
 
+  // Launched with programmatic dependent launch (KOPT_PLAN_OVERLAP_PREV), this CTA may start while
+  // the previous kernel on the stream is still running. Before griddep_wait it reads only pos, the
+  // block table and cache rows below pos (which that kernel must not write) and writes nothing
+  // outside shared memory. The unfused variant reads the row at pos, which the standalone
+  // prologue kernel before it writes, so it waits first.
+  if (!FUSED) griddep_wait();
   if (warp == 0) compute_plan<FUSED>(p, s, lane);
   if (threadIdx.x == 32) {
     for (int i = 0; i < kStages; ++i)
@@ -686,26 +703,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
     asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmk) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmv) : "memory");
   }
-  if (FUSED && (warp == 2 || warp == 3)) {   // q_norm / k_norm weights, once per CTA
-    const bf16* w = warp == 2 ? p.qw : p.kw;
-    bf16* dstw = warp == 2 ? s.wq : s.wk;
-    *reinterpret_cast<uint2*>(dstw + 4 * lane) = *reinterpret_cast<const uint2*>(w + 4 * lane);
-  }
   __syncwarp();
   if (threadIdx.x == 0) {   // the static piece; dynamic chunks are claimed from the prologues
     s.ring[0] = blockIdx.x;
     s.ring[1] = s.ring[2] = s.ring[3] = -1;
     s.nclaimed = 1;
-    if (s.total_chunks == static_cast<int>(gridDim.x)) {   // no dynamic chunks: piece, then end
-      s.nclaimed = 2;
-    } else if (s.static_pages == 0) {   // no pieces: the first dynamic chunk must be known up front
-      // (with P = 0 every chunk is dynamic, so total_chunks > grid whenever there is work)
-      s.ring[1] = claim_chunk(claim_issue(p), s.total_chunks);
-      s.nclaimed = 2;
-    }
+    if (s.total_chunks == static_cast<int>(gridDim.x)) s.nclaimed = 2;   // piece, then end
   }
   __syncthreads();
   const uint64_t pol = evict_first_policy();
+  // With no dynamic chunks nothing of the first unit touches the workspace, so its split and its
+  // first page copies go out before the wait; otherwise all of it waits.
+  const bool early = s.total_chunks == static_cast<int>(gridDim.x);
 
   const int ctid = threadIdx.x;
   // Consume cursor: ring index kc to open next, current chunk and its unvisited pages [cx, cx1).
@@ -814,9 +823,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
   };
 
   Unit U;
-  bool have = advance(U);
-  if (have) stage(U);   // the first unit's prologue inputs travel while the rings fill
-
+  bool have = false;
   // This warp's ring: `state` tells whether the issue cursor stands on an unissued tile.
   Issuer<PAGED, FUSED> iss;
   iss.k = 0;
@@ -827,7 +834,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
   iss.npg = 0;
   iss.bt_row = nullptr;
   iss.win = iss.win_next = iss.win_base = 0;
-  int state = iss.next(p, s, warp, lane);
+  int state = 0;
   int issued = 0, consumed = 0;
   auto pump = [&]() {
     while (issued - consumed < kStages && !s.abort) {
@@ -838,7 +845,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
       state = iss.next(p, s, warp, lane);
     }
   };
-  pump();
+  if (early) {
+    have = advance(U);
+    state = iss.next(p, s, warp, lane);
+    pump();
+  }
+  if (FUSED) griddep_wait();
+  griddep_launch_dependents();
+  if (FUSED && (warp == 2 || warp == 3)) {   // q_norm / k_norm weights, once per CTA
+    const bf16* w = warp == 2 ? p.qw : p.kw;
+    bf16* dstw = warp == 2 ? s.wq : s.wk;
+    *reinterpret_cast<uint2*>(dstw + 4 * lane) = *reinterpret_cast<const uint2*>(w + 4 * lane);
+  }
+  if (!early) {
+    if (threadIdx.x == 0 && s.static_pages == 0) {
+      // no pieces: the first dynamic chunk must be known up front (with P = 0 every chunk is
+      // dynamic, so total_chunks > grid whenever there is work)
+      s.ring[1] = claim_chunk(claim_issue(p), s.total_chunks);
+      s.nclaimed = 2;
+    }
+    __syncthreads();
+    have = advance(U);
+    state = iss.next(p, s, warp, lane);
+    pump();
+  }
+  if (have) stage(U);   // the first unit's prologue inputs travel while the rings fill
 
   while (have) {
     const bool inject = FUSED && U.last;
@@ -998,6 +1029,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
   // fused gather it also tells every rank that all of this rank's rows have landed there.
   if (p.world > 0) named_bar(1, kNW * 32);   // every output store of this CTA is issued
   if (threadIdx.x == 0) {
+    if (s.err_bits) atomicOr(p.ws_err, s.err_bits);
     if (p.world > 0) __threadfence_system();   // this CTA's rows visible to the peers
     else __threadfence();
     if (atomicAdd(p.ws_err + 2, 1) == static_cast<int>(gridDim.x) - 1) {
@@ -1195,9 +1227,22 @@ int launch_attn(const kopt_plan* plan, Params& p, void* stream) {
   if (rc) return rc;
   rc = attn_occupancy<PAGED, FUSED>(plan->device, nullptr);
   if (rc) return rc;
-  decode_attn_kernel<PAGED, FUSED><<<plan->grid, kThreads, kSmemBytes,
-                                     static_cast<cudaStream_t>(stream)>>>(p);
-  return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+  if (plan->flags & ~KOPT_PLAN_OVERLAP_PREV) return KOPT_ERR_ARG;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan->grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (plan->flags & KOPT_PLAN_OVERLAP_PREV) ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, decode_attn_kernel<PAGED, FUSED>, p) != cudaSuccess) {
+    cudaGetLastError();
+    return KOPT_ERR_CUDA;
+  }
+  return KOPT_OK;
 }
 
 }  // namespace kopt
@@ -1258,6 +1303,7 @@ int kopt_decode_attn_plan(int device, int B, int T, int nq, int nkv, int d, int 
   plan->max_len = max_len;
   plan->chunk_tokens = kChunkPages * kPage;
   plan->static_pct = kDefaultStaticPct;
+  plan->flags = 0;
   if (const char* e = getenv("KOPT_STATIC_PCT")) {
     const int v = atoi(e);
     if (v >= 0 && v <= 100) plan->static_pct = v;

@@ -34,21 +34,22 @@ from .shard import head_range, shard_qkv_weight
 
 
 class Engine:
-    def __init__(self, model_path: str, device: str = "cuda:0", group=None):
+    def __init__(self, model_path: str, device: str = "cuda:0", group=None, overlap: bool = True):
         from transformers import AutoModelForCausalLM
         model = AutoModelForCausalLM.from_pretrained(
             model_path, dtype=torch.bfloat16, attn_implementation="sdpa", local_files_only=True)
-        self._init(model.eval().to(device), device, group)
+        self._init(model.eval().to(device), device, group, overlap)
 
     @classmethod
-    def from_model(cls, model, device: str = "cuda:0", group=None) -> "Engine":
+    def from_model(cls, model, device: str = "cuda:0", group=None,
+                   overlap: bool = True) -> "Engine":
         """Wrap an already loaded Qwen3ForCausalLM (bf16, sdpa) instead of reading a checkpoint."""
         self = cls.__new__(cls)
-        self._init(model.eval().to(device), device, group)
+        self._init(model.eval().to(device), device, group, overlap)
         return self
 
     # ------------------------------------------------------------------ construction
-    def _init(self, model, device, group):
+    def _init(self, model, device, group, overlap=True):
         torch.backends.cuda.matmul.allow_tf32 = False
         self.device = torch.device(device)
         if self.device.type != "cuda":
@@ -62,6 +63,7 @@ class Engine:
         self.n_layers = cfg.num_hidden_layers
         self.model = model
         self.group = group
+        self.overlap = overlap
         self.world = 1 if group is None else torch.distributed.get_world_size(group)
         self.rank = 0 if group is None else torch.distributed.get_rank(group)
         h0, _ = head_range(self.nkv, self.rank, self.world)
@@ -102,8 +104,11 @@ class Engine:
         pages = B * ((cap + PAGE - 1) // PAGE)
         self.cache = PagedKVCache(self.n_layers, pages, self.nkv_l, self.d, B, cap, self.device)
         self.cache.assign_sequential([cap] * B)
+        # the kernel before each attention call is the QKV projection GEMM, which writes neither
+        # positions, block table nor cache: the call may start while it finishes
         self.attn = PagedDecodeAttention(B, self.nq_l, self.nkv_l, self.d, self.device,
-                                         self.cache.capacity, eps=self.eps)
+                                         self.cache.capacity, eps=self.eps,
+                                         overlap_prev=self.overlap)
         self.B, self.S, self.cap = B, S, cap
         dev, bf = self.device, torch.bfloat16
         self.ids = torch.zeros(B, dtype=torch.int64, device=dev)

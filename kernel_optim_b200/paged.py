@@ -124,8 +124,13 @@ class PagedDecodeAttention:
     token's K/V appended at pos[b], and split-K attention over keys 0..pos[b].
     """
 
-    def __init__(self, B, nq, nkv, d, device, max_len, target_ctas=None, eps=1e-6):
-        """max_len: the largest cache capacity (keys per sequence) any call will pass."""
+    def __init__(self, B, nq, nkv, d, device, max_len, target_ctas=None, eps=1e-6,
+                 overlap_prev=False):
+        """max_len: the largest cache capacity (keys per sequence) any call will pass.
+        overlap_prev: launch with programmatic dependent launch (KOPT_PLAN_OVERLAP_PREV), so that
+        each call's work split and first page copies overlap the end of the kernel before it on
+        the stream. Only valid when that kernel writes neither pos, the block table, nor the cache
+        rows below pos of the call: a QKV projection GEMM, or an attention call of another layer."""
         self.B, self.nq, self.nkv, self.d, self.eps = B, nq, nkv, d, eps
         self.max_len = max_len
         self.device = torch.device(device)
@@ -137,6 +142,8 @@ class PagedDecodeAttention:
         check(_lib.lib().kopt_decode_attn_plan(self.device.index, B, 1, nq, nkv, d, max_len,
                                                int(target_ctas or 0), ctypes.byref(self.plan)),
               "kopt_decode_attn_plan")
+        if overlap_prev:
+            self.plan.flags |= _lib.PLAN_OVERLAP_PREV
         self.ws = torch.empty(self.plan.ws_bytes, dtype=torch.uint8, device=self.device)
         check(_lib.lib().kopt_workspace_init(ctypes.byref(self.plan), _ptr(self.ws),
                                              _stream(self.device)), "kopt_workspace_init")
