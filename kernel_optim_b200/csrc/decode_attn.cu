@@ -61,6 +61,7 @@ constexpr int kMaxB = 256;
 constexpr int kMaxRanks = KOPT_MAX_RANKS;   // fused gather: ranks of one node
 constexpr int kBoxBytes = kPage * kHalf * 2;   // 2 KiB: one TMA box
 constexpr int kChunkPages = 32;                // dynamic chunk: 512 keys of the page line
+constexpr int kMaxPend = 8;                    // partial units a CTA holds before releasing them
 constexpr int kDefaultStaticPct = 100;         // share of the page line split statically
 constexpr unsigned long long kTimeoutNs = 1000000000ull;  // 1 s per mbarrier wait
 constexpr float kLog2e = 1.4426950408889634f;
@@ -126,7 +127,10 @@ struct __align__(1024) Smem {
   int static_pages;                     // P: pages of the line split into one piece per CTA
   int total_chunks;                     // grid static pieces + dynamic chunks
   volatile int nclaimed;                // ring entries 0 .. nclaimed-1 are valid
-  int merge_go, mq, mc0, mn, mb, mkvh;  // a pair whose partials this CTA merges now
+  int npend;                            // partial units written, not yet released
+  int pend[kMaxPend][5];                // their (pair, first chunk, chunks, sequence, kv head)
+  int nmerge;                           // pending entries whose pair this CTA merges
+  int merge[kMaxPend];
   int unext[12];                        // the look-ahead unit, parked across the tile loop
   int have_next;
   int err_bits;                         // errors found before the wait (reported at the end)
@@ -697,6 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
     for (int i = 0; i < kStages; ++i)
       for (int w = 0; w < kNW; ++w) mbar_init(smem_u32(&s.full[i][w]), 1);
     s.abort = 0;
+    s.npend = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (threadIdx.x == 64) {
@@ -798,28 +803,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
     store_out(p, b, kvh * kGroup + r, d, O.x * inv, O.y * inv);
     if (ctid == 0) atomicExch(&p.ws_cnt[q], 0);
   };
-  // thread 0: a partial written but not yet released (fence + counter), and a pair whose
-  // last-unit test is in flight (atomic result checked at the next epilogue or at the end)
-  bool pm_release = false, pm_valid = false;
-  int pm_prev = 0, pm_q = 0, pm_c0 = 0, pm_n = 0, pm_b = 0, pm_kvh = 0;
-  // The release waits for this CTA's partial stores to be acknowledged (microseconds under full
-  // HBM load), so it runs off the critical path: after warp 0's first tile of the next unit.
-  auto release = [&]() {
-    __threadfence();
-    pm_prev = atomicAdd(&p.ws_cnt[pm_q], 1);
-    pm_valid = true;
-    pm_release = false;
-  };
-  auto resolve_pending = [&]() {   // thread 0 only: publish whether this CTA merges that pair
-    s.merge_go = 0;
-    if (pm_valid) {
-      if (pm_prev == pm_n - 1) {
-        __threadfence();   // acquire the other units' partials
-        s.merge_go = 1;
-        s.mq = pm_q; s.mc0 = pm_c0; s.mn = pm_n; s.mb = pm_b; s.mkvh = pm_kvh;
+  // Releasing a partial (fence, then the pair's counter) waits until this CTA's partial stores are
+  // acknowledged, microseconds under full HBM load, and would stall the warp doing it and with it
+  // the whole unit. So partial units are only recorded as they finish, and released together
+  // once, when the CTA has streamed all its pages (or when the record is full); whoever releases
+  // a pair's last partial merges it then. Collective: every thread calls flush.
+  auto flush = [&]() {
+    if (ctid == 0) {
+      const int np = s.npend;
+      int nm = 0;
+      if (np > 0) {
+        __threadfence();
+        int prev[kMaxPend];
+#pragma unroll
+        for (int i = 0; i < kMaxPend; ++i) prev[i] = i < np ? atomicAdd(&p.ws_cnt[s.pend[i][0]], 1) : 0;
+#pragma unroll
+        for (int i = 0; i < kMaxPend; ++i)
+          if (i < np && prev[i] == s.pend[i][2] - 1) s.merge[nm++] = i;
+        if (nm > 0) __threadfence();   // acquire the other units' partials
       }
-      pm_valid = false;
+      s.nmerge = nm;
     }
+    named_bar(1, kNW * 32);
+    for (int i = 0; i < s.nmerge; ++i) {
+      const int* e = s.pend[s.merge[i]];
+      merge_pair(e[0], e[1], e[2], e[3], e[4]);
+    }
+    named_bar(1, kNW * 32);
+    if (ctid == 0) s.npend = 0;
   };
 
   Unit U;
@@ -955,16 +966,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
       __syncwarp();
       pump();                           // refill the slot just consumed
       if (!looked) look_ahead();
-      if (ctid == 0 && pm_release) release();
     }
     if (!looked) look_ahead();          // this warp had no tile in this unit
     if (inject && warp == 0) inject_token(s, p.scale_log2, st, lane);
 
-    // ---- epilogue: merge the 8 warps, then the splits of this (b, kvh)
-    if (ctid == 0) {
-      if (pm_release) release();   // warp 0 had no tile in this unit
-      resolve_pending();
-    }
+    // ---- epilogue: merge the 8 warps; a split pair's partial goes to the workspace
     float l = st.l;
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
@@ -1002,23 +1008,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
       *reinterpret_cast<float2*>(&p.ws_o[(slot * kGroup + r) * kD + d]) = O;
       if ((ctid & 63) == 0) p.ws_ml[slot * kGroup + r] = make_float2(M, Lsum);
     }
-    if (s.merge_go) merge_pair(s.mq, s.mc0, s.mn, s.mb, s.mkvh);
     named_bar(1, kNW * 32);
-    if (U.n > 1 && ctid == 0) {   // released later (see release)
-      pm_release = true;
-      pm_q = U.q; pm_c0 = U.c0; pm_n = U.n; pm_b = U.b; pm_kvh = U.kvh;
+    if (U.n > 1 && ctid == 0) {   // released by flush
+      int* e = s.pend[s.npend++];
+      e[0] = U.q; e[1] = U.c0; e[2] = U.n; e[3] = U.b; e[4] = U.kvh;
     }
     named_bar(1, kNW * 32);   // parked look-ahead unit visible
+    if (s.npend == kMaxPend) flush();
     have = s.have_next != 0;
     U = *reinterpret_cast<const Unit*>(s.unext);
   }
-  // the last pending release and split test of this CTA
-  if (ctid == 0) {
-    if (pm_release) release();
-    resolve_pending();
-  }
-  named_bar(1, kNW * 32);
-  if (s.merge_go) merge_pair(s.mq, s.mc0, s.mn, s.mb, s.mkvh);
+  flush();   // release this CTA's partials; merge the pairs it completes
   // Drain: after an abort, copies issued into this warp's ring may still be in flight. The last
   // phase issued to each slot is the newest one on its barrier, so waiting on it is exact.
   if (lane == 0) {
