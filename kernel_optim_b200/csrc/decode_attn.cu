@@ -591,7 +591,7 @@ __device__ __forceinline__ void inject_token(const Smem& s, float scale_log2, Wa
 
 // ------------------------------------------------------------------------------- main kernel
 // Issue side of a warp's private pipeline: walks the CTA's claimed chunks in order and yields the
-// tiles in which this warp owns a page (page w of tile i = keys t0 + 128 i + 16 w ...).
+// tiles in which this warp owns a page (page jw of tile i = keys t0 + 128 i + 16 jw ...).
 template <bool PAGED, bool FUSED>
 struct Issuer {
   int k;              // next ring index to open
@@ -599,12 +599,14 @@ struct Issuer {
   Unit U;
   int ti, ntiles;     // current tile within U
   int npg;            // pages streamed by U
+  int rot;            // pages the CTA streamed before U, mod 8
+  int jw;             // this warp's page in each tile of U: (warp - rot) mod 8
   const int* bt_row;  // block-table row of U, from U's first page
   int win, win_next, win_base;  // page ids of this warp's pages of tiles win_base + lane
 
-  __device__ __forceinline__ void open_window(int warp, int lane, int base) {
+  __device__ __forceinline__ void open_window(int lane, int base) {
     win_base = base;
-    const int a = 8 * (base + lane) + warp, b = 8 * (base + 32 + lane) + warp;
+    const int a = 8 * (base + lane) + jw, b = 8 * (base + 32 + lane) + jw;
     win = a < npg ? bt_row[a] : 0;
     win_next = b < npg ? bt_row[b] : 0;
   }
@@ -625,15 +627,17 @@ struct Issuer {
           continue;
         }
         U = unit_at<FUSED>(p, s, chunk, x, x1);
+        rot = (rot + npg) & 7;
+        jw = (warp - rot) & 7;
         ntiles = ceil_div_i(U.t1 - U.t0, kTile);
         npg = ceil_div_i(U.t1 - U.t0, kPage);
         ti = 0;
         if (PAGED && ntiles > 0) {
           bt_row = p.bt + static_cast<long long>(U.b) * p.bt_stride + U.t0 / kPage;
-          open_window(warp, lane, 0);
+          open_window(lane, 0);
         }
       }
-      if (U.t0 + ti * kTile + warp * kPage < U.t1) return 1;
+      if (U.t0 + ti * kTile + jw * kPage < U.t1) return 1;
     }
   }
   // TMA of this warp's page of the current tile into ring slot `slot` (lane 0 issues).
@@ -645,7 +649,7 @@ struct Issuer {
       if (ti >= win_base + 32) {   // window exhausted: move on, prefetch the one after
         win = win_next;
         win_base += 32;
-        const int b = 8 * (win_base + 32 + lane) + warp;
+        const int b = 8 * (win_base + 32 + lane) + jw;
         win_next = b < npg ? bt_row[b] : 0;
       }
       const int pid = __shfl_sync(0xffffffffu, win, ti - win_base);
@@ -665,7 +669,7 @@ struct Issuer {
       // order this warp's earlier generic reads/writes of the slot before the async-proxy refill
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive_expect_tx(fb, 4u * kBoxBytes);
-      const int tq = U.t0 + ti * kTile + warp * kPage;
+      const int tq = U.t0 + ti * kTile + jw * kPage;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const uint32_t dk = smem_u32(&s.k[slot][warp][h][0]);
@@ -843,6 +847,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
   iss.ti = 0;
   iss.ntiles = 0;
   iss.npg = 0;
+  iss.rot = 0;
+  iss.jw = warp;
   iss.bt_row = nullptr;
   iss.win = iss.win_next = iss.win_base = 0;
   int state = 0;
@@ -882,10 +888,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
   }
   if (have) stage(U);   // the first unit's prologue inputs travel while the rings fill
 
+  int cbase = 0;   // pages streamed by the units before U, mod 8
   while (have) {
     const bool inject = FUSED && U.last;
     const int se = U.t1;                          // keys streamed from the cache end here
     const int ntiles = ceil_div_i(se - U.t0, kTile);
+    // Pages go to the warps round-robin along the CTA's whole piece, not unit by unit, so that
+    // the short last tiles of successive units do not all land on the same warps.
+    const int jw = (warp - cbase) & 7;
+    cbase = (cbase + ceil_div_i(se - U.t0, kPage)) & 7;
 
     // ---- prologue from the staged rows: q rows, and the new K/V for the unit ending the pair
     cp_async_wait_all();
@@ -955,7 +966,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
       looked = true;
     };
     for (int i = 0; i < ntiles; ++i) {
-      const int ntok = min(max(se - (U.t0 + i * kTile + warp * kPage), 0), kPage);
+      const int ntok = min(max(se - (U.t0 + i * kTile + jw * kPage), 0), kPage);
       if (ntok == 0) continue;          // no page of this warp in this tile
       if (issued == consumed) pump();   // this tile's copy must be in flight before waiting
       const int slot = consumed % kStages;
