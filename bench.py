@@ -240,14 +240,21 @@ def run_ours(args):
     if err:
         raise RuntimeError(f"device error word {err} after warm-up")
 
+    # soak: untimed launches so the clock samples see the GPU under this load. Every rank runs the
+    # same number of steps (each step is a collective), sized from a short timed probe.
+    n_soak = 0
+    if args.soak_ms > 0:
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record()
+        for i in range(8):
+            step(i)
+        p1.record()
+        torch.cuda.synchronize()
+        n_soak = int(max_over_ranks(dist, args.soak_ms / max(p0.elapsed_time(p1) / 8, 1e-3)))
     sampler = ClockSampler(local)
-    # soak: untimed launches so the clock samples see the GPU under this load
-    t_end = time.perf_counter() + args.soak_ms / 1e3
-    i = 0
-    while time.perf_counter() < t_end:
+    for i in range(n_soak):
         step(i)
-        i += 1
-        if i % 64 == 0:
+        if i % 64 == 63:
             torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
