@@ -100,6 +100,7 @@ struct Params {
   int bt_stride, num_pages, cap, rope_len;
   int B, T, nkv;
   int static_pct;        // share of the page line cut into one static piece per CTA
+  int nsplit, tblocks;   // verify kernel (T > 1): key splits, blocks of 4 query tokens
   float scale_log2, eps;
 };
 
@@ -170,7 +171,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait. With use_abort, returns false at once when another thread already gave up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, Smem& s, int* err,
+template <class S>
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, S& s, int* err,
                                           bool use_abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
@@ -854,7 +856,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
   int state = 0;
   int issued = 0, consumed = 0;
   auto pump = [&]() {
-    while (issued - consumed < kStages && !s.abort) {
+    while (issued - consumed < kStages && !__shfl_sync(0xffffffffu, s.abort, 0)) {
       if (state == 0) state = iss.next(p, s, warp, lane);
       if (state != 1) break;
       iss.issue(p, s, issued % kStages, warp, lane, pol);
@@ -1091,6 +1093,334 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(const __grid_constant
   }
 }
 
+// ======================================================== verify attention (T > 1 query tokens)
+// T query tokens per sequence at positions pos[b] .. pos[b] + T - 1, causal among themselves: the
+// query at pos[b] + t sees keys 0 .. pos[b] + t (fused.py:130-185 with T > 1, the verify step of
+// engine.py:403-415). Their K/V are already in the cache (qk_norm_rope appends all T). One CTA
+// takes one (pair, block of up to 4 tokens, split of the keys): the block's 16 query rows (4 tokens
+// x the 4 heads of the GQA group) fill one m16 MMA tile; 4 warps stream the split's pages
+// round-robin through private 2-deep TMA rings; the split that finishes last merges the partials.
+// Tokens 5..8 are a second block, so T > 4 reads the keys twice.
+constexpr int kVW = 4;                       // warps per verify CTA
+constexpr int kVThreads = kVW * 32;
+constexpr int kVStages = 2;
+constexpr int kVTok = 4;                     // query tokens per CTA (16 rows)
+constexpr int kVRows = kVTok * kGroup;
+constexpr int kVMaxT = 8;
+
+struct __align__(1024) VSmem {
+  bf16 k[kVStages][kVW][2][kPage * kHalf];   // per warp and stage: one page, two 64-dim boxes
+  bf16 v[kVStages][kVW][2][kPage * kHalf];
+  alignas(16) bf16 q[kVRows][kD + 8];        // query rows (padded rows: no ldmatrix conflicts)
+  float red_m[kVW][kVRows];
+  float red_l[kVW][kVRows];
+  unsigned long long full[kVStages][kVW];
+  int last;                                  // this CTA merges the splits of its block
+  volatile int abort;
+};
+constexpr size_t kVSmemBytes = sizeof(VSmem) + 1024;
+// the warps' partial outputs reuse the rings once every page is consumed
+static_assert(sizeof(float) * kVW * kVRows * (kD + 4) <= sizeof(bf16) * 2 * kVStages * kVW * 2 * kPage * kHalf,
+              "verify partials do not fit in the rings");
+
+// D += A B, m16n8k16, all 16 rows live (4 accumulators).
+__device__ __forceinline__ void mma16816_full(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                              uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <bool PAGED>
+__global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_constant__ Params p) {
+  extern __shared__ unsigned char smem_raw[];
+  VSmem& s = *reinterpret_cast<VSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                       ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = p.nkv * kGroup;
+  int idx = blockIdx.x;
+  const int split = idx % p.nsplit;
+  idx /= p.nsplit;
+  const int tb = idx % p.tblocks;
+  const int pair = idx / p.tblocks;
+  const int b = pair / p.nkv, kvh = pair % p.nkv;
+  const int t0 = tb * kVTok;
+  const int nt = min(kVTok, p.T - t0);                  // tokens of this block, >= 1
+  int p0 = p.pos[b];
+  if (p0 < 0 || p0 + p.T > p.cap) {
+    if (threadIdx.x == 0 && split == 0 && tb == 0 && kvh == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_LEN);
+    p0 = min(max(p0, 0), p.cap - p.T);
+  }
+  const int Lb = p0 + t0 + nt;                          // keys the block's last query sees
+  const int per = ceil_div_i(ceil_div_i(Lb, p.nsplit), kPage) * kPage;
+  const int s0 = split * per, s1 = min(Lb, s0 + per);   // this split's keys (s0 on a page edge)
+  const int pg0 = s0 / kPage;
+  const int npg = s1 > s0 ? ceil_div_i(s1, kPage) - pg0 : 0;
+  const int mine = npg > warp ? ceil_div_i(npg - warp, kVW) : 0;   // pages of this warp
+
+  // query rows r = 4 j + g: token t0 + j, head kvh * 4 + g (rows of tokens past T are zero)
+  for (int i = threadIdx.x; i < kVRows * (kD / 8); i += kVThreads) {
+    const int r = i / (kD / 8), c = i % (kD / 8);
+    const int j = r / kGroup, g = r % kGroup;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (j < nt)
+      v = *reinterpret_cast<const uint4*>(
+          p.q + (static_cast<long long>(b) * p.T + t0 + j) * nq * kD + (kvh * kGroup + g) * kD + c * 8);
+    *reinterpret_cast<uint4*>(&s.q[r][c * 8]) = v;
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kVStages; ++i)
+      for (int w = 0; w < kVW; ++w) mbar_init(smem_u32(&s.full[i][w]), 1);
+    s.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const uint64_t pol = evict_first_policy();
+
+  // page ids of this warp's pages k = base + lane, 32 at a time
+  const int* bt_row = PAGED ? p.bt + static_cast<long long>(b) * p.bt_stride : nullptr;
+  int win = 0, win_base = -32;
+  auto issue = [&](int k) {
+    const int pg = pg0 + warp + k * kVW;
+    int row = 0;
+    bool ok = true;
+    if (PAGED) {
+      if (k >= win_base + 32) {
+        win_base = k - (k & 31);
+        const int kk = win_base + lane;
+        win = kk < mine ? bt_row[pg0 + warp + kk * kVW] : 0;
+      }
+      const int pid = __shfl_sync(0xffffffffu, win, k - win_base);
+      if (pid < 0 || pid >= p.num_pages) ok = false;
+      else row = (pid * p.nkv + kvh) * kPage;
+    }
+    if (lane == 0) {
+      const int slot = k % kVStages;
+      const uint32_t fb = smem_u32(&s.full[slot][warp]);
+      if (!ok) {
+        atomicOr(p.ws_err, KOPT_DEV_ERR_PAGE);
+        mbar_arrive_expect_tx(fb, 0);
+        return;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive_expect_tx(fb, 4u * kBoxBytes);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t dk = smem_u32(&s.k[slot][warp][h][0]);
+        const uint32_t dv = smem_u32(&s.v[slot][warp][h][0]);
+        if (PAGED) {
+          tma_load_2d(dk, &p.tmk, h * kHalf, row, fb, pol);
+          tma_load_2d(dv, &p.tmv, h * kHalf, row, fb, pol);
+        } else {
+          tma_load_4d(dk, &p.tmk, h * kHalf, pg * kPage, kvh, b, fb, pol);
+          tma_load_4d(dv, &p.tmv, h * kHalf, pg * kPage, kvh, b, fb, pol);
+        }
+      }
+    }
+  };
+  int issued = 0;
+  for (; issued < min(mine, kVStages) && !__shfl_sync(0xffffffffu, s.abort, 0); ++issued) issue(issued);
+
+  // lane: rows r = lane / 4 and r + 8, columns 2 (lane % 4) + {0, 1} of each n-block
+  const int rA = lane >> 2, rB = rA + 8;
+  const int limA = p0 + t0 + rA / kGroup, limB = p0 + t0 + rB / kGroup;   // last key each row sees
+  const bool liveA = rA / kGroup < nt, liveB = rB / kGroup < nt;
+  float mA = kNegBig, mB = kNegBig, lA = 0.f, lB = 0.f;
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  const int mi = lane >> 3, ri = lane & 7;
+
+  for (int k = 0; k < mine; ++k) {
+    const int slot = k % kVStages;
+    mbar_wait(smem_u32(&s.full[slot][warp]), (k / kVStages) & 1, s, p.ws_err, true);
+    const int key0 = (pg0 + warp + k * kVW) * kPage;
+    const uint32_t kbase = smem_u32(&s.k[slot][warp][0][0]);
+    const uint32_t vbase = smem_u32(&s.v[slot][warp][0][0]);
+    // ---- S = Q K^T, 16 rows x 16 keys
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const int tok = 8 * (mi >> 1) + ri;
+      const uint32_t krow = kbase + tok * 128;
+      const uint32_t qaddr = smem_u32(&s.q[lane & 15][(lane >> 4) * 8]);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(qaddr + ks * 32, a0, a1, a2, a3);
+        const int h = ks >> 2, c = 2 * (ks & 3) + (mi & 1);
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4(krow + h * kBoxBytes + ((c ^ ri) << 4), b00, b01, b10, b11);
+        mma16816_full(c0, a0, a1, a2, a3, b00, b01);
+        mma16816_full(c1, a0, a1, a2, a3, b10, b11);
+      }
+    }
+    const int kc = key0 + 2 * (lane & 3);
+    float sv[8];   // row A: keys kc, kc+1, kc+8, kc+9; row B: the same keys
+    sv[0] = (liveA && kc < s1 && kc <= limA) ? c0[0] * p.scale_log2 : -INFINITY;
+    sv[1] = (liveA && kc + 1 < s1 && kc + 1 <= limA) ? c0[1] * p.scale_log2 : -INFINITY;
+    sv[2] = (liveA && kc + 8 < s1 && kc + 8 <= limA) ? c1[0] * p.scale_log2 : -INFINITY;
+    sv[3] = (liveA && kc + 9 < s1 && kc + 9 <= limA) ? c1[1] * p.scale_log2 : -INFINITY;
+    sv[4] = (liveB && kc < s1 && kc <= limB) ? c0[2] * p.scale_log2 : -INFINITY;
+    sv[5] = (liveB && kc + 1 < s1 && kc + 1 <= limB) ? c0[3] * p.scale_log2 : -INFINITY;
+    sv[6] = (liveB && kc + 8 < s1 && kc + 8 <= limB) ? c1[2] * p.scale_log2 : -INFINITY;
+    sv[7] = (liveB && kc + 9 < s1 && kc + 9 <= limB) ? c1[3] * p.scale_log2 : -INFINITY;
+    // ---- online softmax, rows A and B (4 lanes share a row)
+    float xA = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+    float xB = fmaxf(fmaxf(sv[4], sv[5]), fmaxf(sv[6], sv[7]));
+    xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 1));
+    xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 2));
+    xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 1));
+    xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 2));
+    const float nA = fmaxf(mA, xA), nB = fmaxf(mB, xB);
+    const float aA = exp2f(mA - nA), aB = exp2f(mB - nB);
+    float pr[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pr[i] = exp2f(sv[i] - nA);
+#pragma unroll
+    for (int i = 4; i < 8; ++i) pr[i] = exp2f(sv[i] - nB);
+    lA = lA * aA + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
+    lB = lB * aB + ((pr[4] + pr[5]) + (pr[6] + pr[7]));
+    mA = nA;
+    mB = nB;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= aA;
+      o[j][1] *= aA;
+      o[j][2] *= aB;
+      o[j][3] *= aB;
+    }
+    // P as the A operand: a0 row A keys 0-7, a1 row B keys 0-7, a2 row A keys 8-15, a3 row B 8-15
+    const uint32_t pa0 = pack_bf16(pr[0], pr[1]), pa1 = pack_bf16(pr[4], pr[5]);
+    const uint32_t pa2 = pack_bf16(pr[2], pr[3]), pa3 = pack_bf16(pr[6], pr[7]);
+    // rows of the page past the split's keys may hold anything: zero them so 0 * V stays 0
+    const int ntok = min(s1 - key0, kPage);
+    if (ntok < kPage) {
+      for (int i = lane; i < (kPage - ntok) * 16; i += 32) {
+        const int r = ntok + (i >> 4), part = i & 15;
+        const uint32_t a = vbase + (part >> 3) * kBoxBytes + r * 128 + ((part & 7) << 4);
+        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+      }
+      __syncwarp();
+    }
+    // ---- O += P V
+    {
+      const int tok = 8 * (mi & 1) + ri;
+      const uint32_t vrow = vbase + tok * 128;
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) {
+        const int c = j + (mi >> 1);
+        uint32_t b0a, b1a, b0b, b1b;
+        ldsm_x4_t(vrow + (c >> 3) * kBoxBytes + (((c & 7) ^ ri) << 4), b0a, b1a, b0b, b1b);
+        mma16816_full(o[j], pa0, pa1, pa2, pa3, b0a, b1a);
+        mma16816_full(o[j + 1], pa0, pa1, pa2, pa3, b0b, b1b);
+      }
+    }
+    __syncwarp();
+    if (issued < mine && !__shfl_sync(0xffffffffu, s.abort, 0)) issue(issued++);
+  }
+  // every copy this warp issued has landed (waited above, or drained here after an abort)
+  if (lane == 0)
+    for (int k = max(issued - kVStages, 0); k < issued; ++k)
+      mbar_wait(smem_u32(&s.full[k % kVStages][warp]), (k / kVStages) & 1, s, p.ws_err, false);
+
+  // ---- merge the 4 warps (partials in the ring memory), then the splits of this block
+  lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+  lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+  lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+  lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+  __syncthreads();   // every warp is done with the rings
+  float* ob = reinterpret_cast<float*>(&s.k[0][0][0][0]);   // [kVW][kVRows][kD + 4]
+  {
+    const int c = 2 * (lane & 3);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      *reinterpret_cast<float2*>(&ob[(warp * kVRows + rA) * (kD + 4) + 8 * j + c]) = make_float2(o[j][0], o[j][1]);
+      *reinterpret_cast<float2*>(&ob[(warp * kVRows + rB) * (kD + 4) + 8 * j + c]) = make_float2(o[j][2], o[j][3]);
+    }
+    if ((lane & 3) == 0) {
+      s.red_m[warp][rA] = mA;
+      s.red_l[warp][rA] = lA;
+      s.red_m[warp][rB] = mB;
+      s.red_l[warp][rB] = lB;
+    }
+  }
+  __syncthreads();
+  // thread -> row r, dims d0 .. d0 + 15
+  const int r = threadIdx.x >> 3, d0 = (threadIdx.x & 7) * 16;
+  const int j = r / kGroup, g = r % kGroup;
+  float M = kNegBig;
+#pragma unroll
+  for (int w = 0; w < kVW; ++w) M = fmaxf(M, s.red_m[w][r]);
+  float Lsum = 0.f, O[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) O[e] = 0.f;
+#pragma unroll
+  for (int w = 0; w < kVW; ++w) {
+    const float f = exp2f(s.red_m[w][r] - M);
+    Lsum += f * s.red_l[w][r];
+#pragma unroll
+    for (int e = 0; e < 16; e += 4) {
+      const float4 x = *reinterpret_cast<const float4*>(&ob[(w * kVRows + r) * (kD + 4) + d0 + e]);
+      O[e] += f * x.x;
+      O[e + 1] += f * x.y;
+      O[e + 2] += f * x.z;
+      O[e + 3] += f * x.w;
+    }
+  }
+  bf16* dst = p.out + ((static_cast<long long>(b) * p.T + t0 + j) * nq + kvh * kGroup + g) * kD + d0;
+  if (p.nsplit == 1) {
+    if (j < nt) {
+      const float inv = 1.0f / Lsum;
+#pragma unroll
+      for (int e = 0; e < 16; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(O[e] * inv, O[e + 1] * inv);
+    }
+    return;
+  }
+  const long long slot = blockIdx.x;
+  float* po = p.ws_o + (slot * kVRows + r) * kD + d0;
+#pragma unroll
+  for (int e = 0; e < 16; e += 4) *reinterpret_cast<float4*>(po + e) = make_float4(O[e], O[e + 1], O[e + 2], O[e + 3]);
+  if ((threadIdx.x & 7) == 0) p.ws_ml[slot * kVRows + r] = make_float2(M, Lsum);
+  __syncthreads();
+  const int cnt = pair * p.tblocks + tb;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s.last = atomicAdd(&p.ws_cnt[cnt], 1) == p.nsplit - 1;
+    if (s.last) __threadfence();   // acquire the other splits' partials
+  }
+  __syncthreads();
+  if (!s.last) return;
+  // the last split of the block: online log-sum-exp over every split's partial
+  const long long first = blockIdx.x - split;
+  float Mm = kNegBig, Lm = 0.f;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) O[e] = 0.f;
+  for (int sp = 0; sp < p.nsplit; ++sp) {
+    const long long sl = first + sp;
+    const float2 ml = __ldcg(&p.ws_ml[sl * kVRows + r]);
+    const float mn = fmaxf(Mm, ml.x);
+    const float a = exp2f(Mm - mn), f = exp2f(ml.x - mn);
+    Lm = Lm * a + ml.y * f;
+    const float* src = p.ws_o + (sl * kVRows + r) * kD + d0;
+#pragma unroll
+    for (int e = 0; e < 16; e += 4) {
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(src + e));
+      O[e] = O[e] * a + x.x * f;
+      O[e + 1] = O[e + 1] * a + x.y * f;
+      O[e + 2] = O[e + 2] * a + x.z * f;
+      O[e + 3] = O[e + 3] * a + x.w * f;
+    }
+    Mm = mn;
+  }
+  if (j < nt) {
+    const float inv = 1.0f / Lm;
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(O[e] * inv, O[e + 1] * inv);
+  }
+  if (threadIdx.x == 0) atomicExch(&p.ws_cnt[cnt], 0);
+}
+
 // ------------------------------------------------------------------------------ host side
 constexpr int64_t kHeaderBytes = 256;
 inline int64_t align256(int64_t x) { return (x + 255) & ~static_cast<int64_t>(255); }
@@ -1098,14 +1428,20 @@ inline int64_t align256(int64_t x) { return (x + 255) & ~static_cast<int64_t>(25
 struct WsLayout {
   int64_t err, cnt, ml, o, total;
 };
-inline WsLayout ws_layout(int B, int nkv, int max_units) {
+// counters: one per (pair, token block); partials: rows per slot = 4 (T = 1) or 16 (verify)
+inline WsLayout ws_layout(int B, int nkv, int max_units, int T = 1) {
+  const int blocks = T > 1 ? (T + kVTok - 1) / kVTok : 1;
+  const int rows = T > 1 ? kVRows : kGroup;
   WsLayout w;
   w.err = 0;
   w.cnt = kHeaderBytes;
-  w.ml = w.cnt + align256(static_cast<int64_t>(B) * nkv * 4);
-  w.o = w.ml + align256(static_cast<int64_t>(max_units) * kGroup * 8);
-  w.total = w.o + static_cast<int64_t>(max_units) * kGroup * kD * 4;
+  w.ml = w.cnt + align256(static_cast<int64_t>(B) * nkv * blocks * 4);
+  w.o = w.ml + align256(static_cast<int64_t>(max_units) * rows * 8);
+  w.total = w.o + static_cast<int64_t>(max_units) * rows * kD * 4;
   return w;
+}
+inline WsLayout ws_layout(const kopt_plan* plan) {
+  return ws_layout(plan->B, plan->nkv, plan->max_units, plan->T);
 }
 
 template <bool PAGED, bool FUSED>
@@ -1222,7 +1558,7 @@ int encode_kv_maps(Params& p, int B, int nkv) {
 
 int fill_ws(Params& p, const kopt_plan* plan, void* ws) {
   if (ws == nullptr || (reinterpret_cast<uintptr_t>(ws) & 255) != 0) return KOPT_ERR_WORKSPACE;
-  const WsLayout w = ws_layout(plan->B, plan->nkv, plan->max_units);
+  const WsLayout w = ws_layout(plan);
   if (w.total != plan->ws_bytes) return KOPT_ERR_WORKSPACE;
   char* base = static_cast<char*>(ws);
   p.ws_err = reinterpret_cast<int*>(base + w.err);
@@ -1256,6 +1592,36 @@ int launch_attn(const kopt_plan* plan, Params& p, void* stream) {
   return KOPT_OK;
 }
 
+template <bool PAGED>
+int verify_occupancy(int device, int* blocks_per_sm) {
+  static int configured[64] = {0};
+  if (device < 0 || device >= 64) return KOPT_ERR_ARG;
+  auto kern = verify_attn_kernel<PAGED>;
+  if (!configured[device]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kVSmemBytes)) != cudaSuccess)
+      return KOPT_ERR_CUDA;
+    configured[device] = 1;
+  }
+  if (blocks_per_sm &&
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kern, kVThreads, kVSmemBytes) !=
+          cudaSuccess)
+    return KOPT_ERR_CUDA;
+  return KOPT_OK;
+}
+
+template <bool PAGED>
+int launch_verify(const kopt_plan* plan, Params& p, void* stream) {
+  int rc = set_device(plan->device);
+  if (rc) return rc;
+  rc = verify_occupancy<PAGED>(plan->device, nullptr);
+  if (rc) return rc;
+  p.tblocks = (plan->T + kVTok - 1) / kVTok;
+  p.nsplit = plan->grid / (plan->B * plan->nkv * p.tblocks);
+  verify_attn_kernel<PAGED><<<plan->grid, kVThreads, kVSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+}
+
 }  // namespace kopt
 
 // =================================================================================== C ABI
@@ -1281,13 +1647,42 @@ const char* kopt_strerror(int status) {
 int kopt_decode_attn_plan(int device, int B, int T, int nq, int nkv, int d, int max_len,
                           int target_ctas, kopt_plan* plan) {
   if (plan == nullptr) return KOPT_ERR_ARG;
-  if (d != kD || nkv < 1 || nq != nkv * kGroup || B < 1 || B > kMaxB || T != 1 || max_len < 1)
+  if (d != kD || nkv < 1 || nq != nkv * kGroup || B < 1 || B > kMaxB || T < 1 || T > kVMaxT ||
+      max_len < 1)
     return KOPT_ERR_ARG;
   int rc = set_device(device);
   if (rc) return rc;
   int sms = 0, occ = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
     return KOPT_ERR_CUDA;
+  if (T > 1) {   // verify: grid = pairs x token blocks x key splits, about two waves
+    if (max_len < T) return KOPT_ERR_ARG;
+    rc = verify_occupancy<true>(device, &occ);
+    if (rc) return rc;
+    rc = verify_occupancy<false>(device, nullptr);
+    if (rc) return rc;
+    if (occ < 1) return KOPT_ERR_CUDA;
+    const long long blocks = static_cast<long long>(B) * nkv * ((T + kVTok - 1) / kVTok);
+    const long long target = target_ctas > 0 ? target_ctas : 2ll * sms * occ;
+    long long nsplit = (target + blocks - 1) / blocks;
+    const long long max_split = (static_cast<long long>(max_len) + 2 * kPage - 1) / (2 * kPage);
+    nsplit = nsplit < 1 ? 1 : nsplit > max_split ? max_split : nsplit;
+    if (blocks * nsplit >= (1ll << 31)) return KOPT_ERR_ARG;
+    plan->B = B;
+    plan->T = T;
+    plan->nkv = nkv;
+    plan->grid = static_cast<int32_t>(blocks * nsplit);
+    plan->ctas_per_sm = occ;
+    plan->tile_tokens = kVW * kPage;
+    plan->max_units = plan->grid;
+    plan->device = device;
+    plan->max_len = max_len;
+    plan->chunk_tokens = static_cast<int32_t>((max_len + nsplit - 1) / nsplit);
+    plan->static_pct = 100;
+    plan->flags = 0;
+    plan->ws_bytes = ws_layout(plan).total;
+    return KOPT_OK;
+  }
   rc = attn_occupancy<true, true>(device, &occ);
   if (rc) return rc;
   // the four instantiations share block size and shared memory, so one occupancy serves all
@@ -1327,7 +1722,7 @@ int kopt_workspace_init(const kopt_plan* plan, void* ws, void* stream) {
   if (plan == nullptr || ws == nullptr) return KOPT_ERR_ARG;
   int rc = set_device(plan->device);
   if (rc) return rc;
-  const WsLayout w = ws_layout(plan->B, plan->nkv, plan->max_units);
+  const WsLayout w = ws_layout(plan);
   // error word and split counters; partials need no initial value
   if (cudaMemsetAsync(ws, 0, static_cast<size_t>(w.ml), static_cast<cudaStream_t>(stream)) !=
       cudaSuccess)
@@ -1346,7 +1741,7 @@ int kopt_read_error(const kopt_plan* plan, void* ws, int* err_out, void* stream)
   if (cudaStreamSynchronize(st) != cudaSuccess) return KOPT_ERR_CUDA;
   *err_out = host;
   if (host != 0) {
-    const WsLayout w = ws_layout(plan->B, plan->nkv, plan->max_units);
+    const WsLayout w = ws_layout(plan);
     if (cudaMemsetAsync(ws, 0, static_cast<size_t>(w.ml), st) != cudaSuccess) return KOPT_ERR_CUDA;
   }
   return KOPT_OK;
@@ -1377,6 +1772,10 @@ int kopt_decode_attn(const kopt_plan* plan, const void* q, const kopt_kv_cache* 
   if (rc) return rc;
   rc = encode_kv_maps(p, plan->B, plan->nkv);
   if (rc) return rc;
+  if (plan->T > 1) {
+    if (p.cap < plan->T) return KOPT_ERR_ARG;
+    return p.bt ? launch_verify<true>(plan, p, stream) : launch_verify<false>(plan, p, stream);
+  }
   return p.bt ? launch_attn<true, false>(plan, p, stream) : launch_attn<false, false>(plan, p, stream);
 }
 
@@ -1390,7 +1789,7 @@ int fused_launch(const kopt_plan* plan, const void* qkv, const void* q_norm_w, c
                  float scale, float eps, void* stream) {
   if (plan == nullptr || qkv == nullptr || q_norm_w == nullptr || k_norm_w == nullptr ||
       cos == nullptr || sin == nullptr || pos == nullptr || (g == nullptr && out == nullptr) ||
-      rope_len < 1)
+      rope_len < 1 || plan->T != 1)   // the fused prologue appends one token per sequence
     return KOPT_ERR_ARG;
   if (!aligned16(qkv) || (out && !aligned16(out)) || (q_out && !aligned16(q_out)) ||
       !aligned16(cos) || !aligned16(sin) || (reinterpret_cast<uintptr_t>(q_norm_w) & 7) ||

@@ -125,12 +125,14 @@ class PagedDecodeAttention:
     """
 
     def __init__(self, B, nq, nkv, d, device, max_len, target_ctas=None, eps=1e-6,
-                 overlap_prev=False):
+                 overlap_prev=False, T=1):
         """max_len: the largest cache capacity (keys per sequence) any call will pass.
         overlap_prev: launch with programmatic dependent launch (KOPT_PLAN_OVERLAP_PREV), so that
         each call's work split and first page copies overlap the end of the kernel before it on
         the stream. Only valid when that kernel writes neither pos, the block table, nor the cache
-        rows below pos of the call: a QKV projection GEMM, or an attention call of another layer."""
+        rows below pos of the call: a QKV projection GEMM, or an attention call of another layer.
+        T: query tokens per sequence; T > 1 (up to 8) is the verify step, through ``attend`` only
+        (the fused ``__call__`` appends one token per sequence)."""
         self.B, self.nq, self.nkv, self.d, self.eps = B, nq, nkv, d, eps
         self.max_len = max_len
         self.device = torch.device(device)
@@ -139,7 +141,8 @@ class PagedDecodeAttention:
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self.plan = Plan()
-        check(_lib.lib().kopt_decode_attn_plan(self.device.index, B, 1, nq, nkv, d, max_len,
+        self.T = T
+        check(_lib.lib().kopt_decode_attn_plan(self.device.index, B, T, nq, nkv, d, max_len,
                                                int(target_ctas or 0), ctypes.byref(self.plan)),
               "kopt_decode_attn_plan")
         if overlap_prev:
@@ -174,7 +177,8 @@ class PagedDecodeAttention:
             _stream(qkv.device)), "kopt_decode_attn_fused")
 
     def attend(self, q, cache, layer, pos, out):
-        """Attention only (K/V already appended at pos[b]): q/out [B, nq d]."""
+        """Attention only (K/V already appended at pos[b] .. pos[b] + T - 1): q/out
+        [B*T, nq d], rows b * T + t; query t sees keys 0 .. pos[b] + t (T > 1: verify)."""
         _require_cuda(q, "q")
         _require_cuda(out, "out")
         _require_cuda(pos, "pos", torch.int32)

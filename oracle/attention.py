@@ -39,6 +39,37 @@ def decode_attn_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lens) ->
     return out
 
 
+def verify_attn_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pos, T: int) -> torch.Tensor:
+    """T query tokens per sequence, causal among themselves (engine/kernels/fused.py:130-185 with
+    T > 1; rows laid out b * T + t as fused.py:137): query t of sequence b sees keys
+    0 .. pos[b] + t. q [B*T, nq, D] -> [B*T, nq, D] fp32, one single-token oracle call per t."""
+    B = len(pos)
+    pos = [int(x) for x in torch.as_tensor(pos).cpu().tolist()]
+    out = torch.empty(B * T, q.shape[1], D, dtype=torch.float32)
+    qv = q.view(B, T, q.shape[1], D)
+    for t in range(T):
+        out.view(B, T, q.shape[1], D)[:, t] = decode_attn_fp32(qv[:, t], k, v, [p + t + 1 for p in pos])
+    return out
+
+
+def verify_attn_masked_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pos, T: int) -> torch.Tensor:
+    """The same in one SDPA call per sequence with an explicit boolean mask (query t may attend
+    key i iff i <= pos[b] + t): an independent restatement to check verify_attn_fp32 against."""
+    B = len(pos)
+    pos = [int(x) for x in torch.as_tensor(pos).cpu().tolist()]
+    nq = q.shape[1]
+    out = torch.empty(B * T, nq, D, dtype=torch.float32)
+    for b in range(B):
+        L = pos[b] + T
+        qb = q[b * T:(b + 1) * T].float().cpu().permute(1, 0, 2).unsqueeze(0)   # [1, nq, T, D]
+        kb = k[b:b + 1, :, :L].float().cpu()
+        vb = v[b:b + 1, :, :L].float().cpu()
+        mask = torch.arange(L)[None, :] <= (pos[b] + torch.arange(T))[:, None]   # [T, L]
+        o = F.scaled_dot_product_attention(qb, kb, vb, attn_mask=mask, scale=D ** -0.5, enable_gqa=True)
+        out[b * T:(b + 1) * T] = o[0].permute(1, 0, 2)
+    return out
+
+
 def gather_pages(pool: torch.Tensor, table: torch.Tensor, b: int, L: int) -> torch.Tensor:
     """pool [num_pages, nkv, 16, D], table [B, max_pages] -> [nkv, L, D] for sequence b."""
     t = torch.arange(L)

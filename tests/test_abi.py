@@ -53,7 +53,8 @@ def test_struct_layouts_match_header():
     (0, 16, 1, 24, 8, 128, 4097, 0),    # group != 4
     (0, 0, 1, 32, 8, 128, 4097, 0),     # empty batch
     (0, 257, 1, 32, 8, 128, 4097, 0),   # batch above the plan limit
-    (0, 16, 2, 32, 8, 128, 4097, 0),    # T > 1 not built yet
+    (0, 16, 9, 32, 8, 128, 4097, 0),    # more than 8 query tokens per sequence
+    (0, 16, 0, 32, 8, 128, 4097, 0),    # no query token
     (0, 16, 1, 32, 8, 128, 0, 0),       # no capacity
 ])
 def test_plan_rejects_bad_shapes(lib, args):

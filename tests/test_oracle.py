@@ -96,3 +96,19 @@ def test_reference_plan_matches_fused_py():
     assert reference_plan(4097, 16, 8) == (3, 1408)
     assert reference_plan(131073, 4, 8) == (9, 14592)
     assert reference_plan(512, 1, 8) == (4, 128)
+
+
+def test_verify_oracle_matches_masked_restatement():
+    """The verify oracle (one single-token SDPA per query token) against one masked SDPA per
+    sequence: two independent statements of 'query t sees keys 0 .. pos + t'."""
+    from oracle.attention import verify_attn_fp32, verify_attn_masked_fp32
+    g = torch.Generator().manual_seed(11)
+    B, T, nq, nkv = 3, 5, 32, 8
+    pos = [0, 9, 40]
+    cap = max(pos) + T
+    q = torch.randn(B * T, nq, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, nkv, cap, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, nkv, cap, 128, generator=g).to(torch.bfloat16)
+    a = verify_attn_fp32(q, k, v, pos, T)
+    b = verify_attn_masked_fp32(q, k, v, pos, T)
+    assert torch.allclose(a, b, atol=1e-5, rtol=1e-5)
