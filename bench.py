@@ -51,7 +51,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "v3", "v5", "v7"], default="c2",
                     help="c2-c4: one decode-attention call per step; c5: the engine end to end")
     ap.add_argument("--layers", type=int, default=8, help="layer caches rotated across steps")
     ap.add_argument("--layout", choices=["paged", "contiguous"], default="paged")
@@ -166,7 +166,11 @@ class StepLauncher:
         L = _lib.lib()
         self.gather = gather
         self.slot = 0
-        if gather is None:
+        self.verify = not case.fused   # T query tokens (v3/v5/v7): attention only
+        if self.verify:
+            self.fn = L.kopt_decode_attn
+            self.dst = [_ptr(out)] * 2
+        elif gather is None:
             self.fn = L.kopt_decode_attn_fused
             self.dst = [_ptr(out)] * 2
         else:
@@ -174,16 +178,20 @@ class StepLauncher:
             self.dst = [ctypes.byref(gather.descriptor(s)) for s in range(2)]
         self.check = _lib.check
         t = case.tensors
-        qkv = t["qkv"] if qkv is None else qkv
         pos = t["pos"] if pos is None else pos
         if "cache" in t:
             self.descs = [t["cache"].descriptor(i) for i in range(layers)]
         else:
             self.descs = [contiguous_cache(t["k_cache"][i], t["v_cache"][i]) for i in range(layers)]
-        self.common = (ctypes.byref(attn.plan), _ptr(qkv), _ptr(t["q_norm_w"]),
-                       _ptr(t["k_norm_w"]), _ptr(t["cos"]), _ptr(t["sin"]), t["cos"].shape[0])
         self.pos = _ptr(pos)
-        self.tail = (None, _ptr(attn.ws), ctypes.c_float(attn.scale), ctypes.c_float(attn.eps))
+        if self.verify:
+            self.common = (ctypes.byref(attn.plan), _ptr(t["q"] if qkv is None else qkv))
+            self.tail = (_ptr(attn.ws), ctypes.c_float(attn.scale))
+        else:
+            qkv = t["qkv"] if qkv is None else qkv
+            self.common = (ctypes.byref(attn.plan), _ptr(qkv), _ptr(t["q_norm_w"]),
+                           _ptr(t["k_norm_w"]), _ptr(t["cos"]), _ptr(t["sin"]), t["cos"].shape[0])
+            self.tail = (None, _ptr(attn.ws), ctypes.c_float(attn.scale), ctypes.c_float(attn.eps))
         self.stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         self.layers = layers
 
@@ -214,11 +222,13 @@ def run_ours(args):
     B = case.B
     cap = t["cache"].capacity if "cache" in t else t["k_cache"].shape[3]
     # consecutive calls read different layers' caches, so each may overlap the previous one
-    attn = PagedDecodeAttention(B, case.nq, case.nkv, 128, dev, cap, overlap_prev=not args.no_overlap)
-    out = torch.empty(B, case.nq * 128, dtype=torch.bfloat16, device=dev)
-    fused_gather = n > 1 and args.gather == "fused"
+    attn = PagedDecodeAttention(B, case.nq, case.nkv, 128, dev, cap, overlap_prev=not args.no_overlap,
+                                T=case.T)
+    out = torch.empty(B * case.T, case.nq * 128, dtype=torch.bfloat16, device=dev)
+    fused_gather = n > 1 and args.gather == "fused" and case.T == 1   # the gather is T = 1 only
     nccl_gather = n > 1 and not fused_gather
-    gathered = torch.empty(n, B, case.nq * 128, dtype=torch.bfloat16, device=dev) if nccl_gather else None
+    gathered = (torch.empty(n, B * case.T, case.nq * 128, dtype=torch.bfloat16, device=dev)
+                if nccl_gather else None)
     pg = None
     if fused_gather:
         from kernel_optim_b200.gather import PeerGather
@@ -293,12 +303,14 @@ def run_ours(args):
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "frac_of_8TBs_nominal": round(achieved / 8000, 4),
                 "traffic": traffic, "peak_source": peak_src,
-                "kernel": "decode_attn_kernel<PAGED=1,FUSED=1>", "kernel_us": round(kern_ms * 1e3, 2),
+                "kernel": ("decode_attn_kernel<PAGED=1,FUSED=1>" if case.fused else
+                           f"verify_attn_kernel<PAGED=1> (T={case.T})"),
+                "kernel_us": round(kern_ms * 1e3, 2),
                 "algorithmic_bytes_per_launch": bytes_rank}
 
     e2e = None if args.no_e2e else run_e2e(args, case, attn, out, gathered, pg, dist, bytes_job)
     cpu = None
-    if n == 1 and rank == 0 and not args.no_cpu_baseline and args.layout == "paged":
+    if n == 1 and rank == 0 and not args.no_cpu_baseline and args.layout == "paged" and case.fused:
         cpu = cpu_baseline(case, bytes_rank)
 
     line = {
@@ -345,15 +357,16 @@ def run_e2e(args, case, attn, out, gathered, pg, dist, bytes_job):
     timed region."""
     t = case.tensors
     dev = out.device
-    qkv_b = t["qkv"].numel() * 2
+    src = t["qkv"] if case.fused else t["q"]   # the step's per-token input
+    qkv_b = src.numel() * 2
     host_in = torch.empty(qkv_b + t["pos"].numel() * 4, dtype=torch.uint8, pin_memory=True)
-    host_in[:qkv_b].view(torch.bfloat16).copy_(t["qkv"].reshape(-1).cpu())
+    host_in[:qkv_b].view(torch.bfloat16).copy_(src.reshape(-1).cpu())
     host_in[qkv_b:].view(torch.int32).copy_(t["pos"].cpu())
     dev_in = [torch.empty_like(host_in, device=dev) for _ in range(2)]
     outs = [out, torch.empty_like(out)]
     gath = [gathered, torch.empty_like(gathered)] if gathered is not None else None
     launchers = [StepLauncher(case, attn, args.layers, outs[j],
-                              qkv=dev_in[j][:qkv_b].view(torch.bfloat16).view(t["qkv"].shape),
+                              qkv=dev_in[j][:qkv_b].view(torch.bfloat16).view(src.shape),
                               pos=dev_in[j][qkv_b:].view(torch.int32), gather=pg)
                  for j in range(2)]
     res0 = gath[0] if gath is not None else pg.out[0] if pg is not None else out
@@ -554,6 +567,11 @@ def main():
                 "c5 runs a random-init Qwen3-4B end to end; its CPU prefill of 32 x 1024 tokens "
                 "alone is ~260 TFLOP, hours on the host cores; the reference arm times c2")}),
                 flush=True)
+    elif args.impl == "reference" and args.workload.startswith("v"):
+        if dist_env()[1] == 0:
+            print(json.dumps({"impl": "reference", "unavailable": (
+                "the reference arm times the headline decode step (c2); the verify workloads "
+                "have no separate CPU arm")}), flush=True)
     elif args.impl == "reference":
         run_reference(args)
     else:

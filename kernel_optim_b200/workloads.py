@@ -10,10 +10,13 @@ distributions, which these generators reproduce with fixed seeds:
       permutation of the pool, prologue fused.
   c4  B=4, 131071 cached + 1 appended = 131072 keys per sequence, prologue fused.
   c5  end-to-end engine (kernel_optim_b200.engine), not built here.
+  v3, v5, v7  verify (T = 3, 5, 7 query tokens per sequence, causal among themselves; the draft
+      lengths engine.py:48-56 picks for B <= 32, 16, 4): c2's shape, B=16, 4096 cached keys + the T
+      new ones already in the cache, roped q [B*T, nq*128] N(0,1).
 
 Algorithmic bytes of one call (the roofline numerator):
   sum_b keys_b * nkv * 128 * 2 B * 2 (K and V)  +  B * nq * 128 * 2 (out write)
-  + unfused: B * nq * 128 * 2 (q read)
+  + unfused: B * T * nq * 128 * 2 (q read; T query tokens per sequence, out likewise)
   + fused:   B * (nq + 2 nkv) * 128 * 2 (qkv read) + B * 2 * nkv * 128 * 2 (K/V append write)
 Page-table reads and split scratch are overhead, not counted.
 """
@@ -54,6 +57,7 @@ class Case:
     fused: bool                  # new token appended through the prologue
     nq: int = NQ
     nkv: int = NKV
+    T: int = 1                   # query tokens per sequence (verify when > 1)
     tensors: dict = field(default_factory=dict)
 
     @property
@@ -63,11 +67,11 @@ class Case:
 
     def algorithmic_bytes(self) -> int:
         kv = sum(self.keys) * self.nkv * D * 2 * 2
-        out = self.B * self.nq * D * 2
+        out = self.B * self.T * self.nq * D * 2
         if self.fused:
             extra = self.B * (self.nq + 2 * self.nkv) * D * 2 + self.B * 2 * self.nkv * D * 2
         else:
-            extra = self.B * self.nq * D * 2
+            extra = self.B * self.T * self.nq * D * 2
         return kv + out + extra
 
 
@@ -88,6 +92,10 @@ def case_shape(name: str, seed: int = 0, batch_scale: int = 1, kv_shard: int = 1
     if name == "c4":
         B = 4 * batch_scale
         return Case("c4", B, [131071] * B, True, NQ // kv_shard, nkv)
+    if name in ("v3", "v5", "v7"):
+        T = int(name[1])
+        B = 16 * batch_scale
+        return Case(name, B, [4096 + T] * B, False, NQ // kv_shard, nkv, T)
     raise ValueError(f"unknown decode-attention config {name!r}")
 
 
@@ -115,9 +123,9 @@ def build_case(name: str, device, seed: int = 0, paged: bool = True, batch_scale
         t["k_norm_w"] = torch.ones(D, dtype=bf, device=dev)
         t["cos"], t["sin"] = rope_tables(max_keys, dev)
     else:
-        full = torch.randn(B, NQ * D, generator=gen, device=dev, dtype=torch.float32).to(bf)
+        full = torch.randn(B * case.T, NQ * D, generator=gen, device=dev, dtype=torch.float32).to(bf)
         t["q"] = full[:, h0 * 4 * D:(h0 + nkv_l) * 4 * D].contiguous()
-    t["pos"] = torch.tensor([c if case.fused else c - 1 for c in case.cached], dtype=torch.int32,
+    t["pos"] = torch.tensor([c if case.fused else c - case.T for c in case.cached], dtype=torch.int32,
                             device=dev)
     if paged:
         n_pages = sum((k_ + PAGE - 1) // PAGE for k_ in case.keys)
