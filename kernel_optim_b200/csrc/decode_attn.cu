@@ -1097,31 +1097,29 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(const __grid_constant
 // T query tokens per sequence at positions pos[b] .. pos[b] + T - 1, causal among themselves: the
 // query at pos[b] + t sees keys 0 .. pos[b] + t (fused.py:130-185 with T > 1, the verify step of
 // engine.py:403-415). Their K/V are already in the cache (qk_norm_rope appends all T). One CTA
-// takes one (pair, block of up to 4 tokens, split of the keys): the block's 16 query rows (4 tokens
-// x the 4 heads of the GQA group) fill one m16 MMA tile; 4 warps stream the split's pages
-// round-robin through private 2-deep TMA rings; the split that finishes last merges the partials.
-// Tokens 5..8 are a second block, so T > 4 reads the keys twice.
+// takes one (pair, split of the keys) and all 4 T query rows of the pair (T tokens x the 4 heads
+// of the GQA group) on MT m16 MMA tiles (MT = 1 for T <= 4, 2 for T <= 8), so every key is read
+// once; 4 warps stream the split's pages round-robin through private 3-deep TMA rings, and the
+// split that finishes last merges the partials.
 constexpr int kVW = 4;                       // warps per verify CTA
 constexpr int kVThreads = kVW * 32;
-constexpr int kVStages = 2;
-constexpr int kVTok = 4;                     // query tokens per CTA (16 rows)
-constexpr int kVRows = kVTok * kGroup;
+constexpr int kVStages = 3;
 constexpr int kVMaxT = 8;
 
+template <int MT>
 struct __align__(1024) VSmem {
   bf16 k[kVStages][kVW][2][kPage * kHalf];   // per warp and stage: one page, two 64-dim boxes
   bf16 v[kVStages][kVW][2][kPage * kHalf];
-  alignas(16) bf16 q[kVRows][kD + 8];        // query rows (padded rows: no ldmatrix conflicts)
-  float red_m[kVW][kVRows];
-  float red_l[kVW][kVRows];
+  alignas(16) bf16 q[16 * MT][kD + 8];       // query rows (padded rows: no ldmatrix conflicts)
+  float red_m[kVW][16 * MT];
+  float red_l[kVW][16 * MT];
   unsigned long long full[kVStages][kVW];
-  int last;                                  // this CTA merges the splits of its block
+  int last;                                  // this CTA merges the splits of its pair
   volatile int abort;
 };
-constexpr size_t kVSmemBytes = sizeof(VSmem) + 1024;
-// the warps' partial outputs reuse the rings once every page is consumed
-static_assert(sizeof(float) * kVW * kVRows * (kD + 4) <= sizeof(bf16) * 2 * kVStages * kVW * 2 * kPage * kHalf,
-              "verify partials do not fit in the rings");
+template <int MT>
+constexpr size_t vsmem_bytes() { return sizeof(VSmem<MT>) + 1024; }
+inline int verify_tiles(int T) { return T > 4 ? 2 : 1; }
 
 // D += A B, m16n8k16, all 16 rows live (4 accumulators).
 __device__ __forceinline__ void mma16816_full(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -1132,43 +1130,33 @@ __device__ __forceinline__ void mma16816_full(float (&d)[4], uint32_t a0, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <bool PAGED>
+template <bool PAGED, int MT>
 __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_constant__ Params p) {
+  constexpr int R = 16 * MT;                 // query rows
+  // the warps' partial outputs reuse the rings once every page is consumed
+  static_assert(sizeof(float) * kVW * R * (kD + 4) <= sizeof(bf16) * 2 * kVStages * kVW * 2 * kPage * kHalf,
+                "verify partials do not fit in the rings");
   extern __shared__ unsigned char smem_raw[];
-  VSmem& s = *reinterpret_cast<VSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                       ~static_cast<uintptr_t>(1023));
+  VSmem<MT>& s = *reinterpret_cast<VSmem<MT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = p.nkv * kGroup;
-  int idx = blockIdx.x;
-  const int split = idx % p.nsplit;
-  idx /= p.nsplit;
-  const int tb = idx % p.tblocks;
-  const int pair = idx / p.tblocks;
+  const int split = blockIdx.x % p.nsplit;
+  const int pair = blockIdx.x / p.nsplit;
   const int b = pair / p.nkv, kvh = pair % p.nkv;
-  const int t0 = tb * kVTok;
-  const int nt = min(kVTok, p.T - t0);                  // tokens of this block, >= 1
+  const int T = p.T;                                    // 2 .. 4 MT
   int p0 = p.pos[b];
-  if (p0 < 0 || p0 + p.T > p.cap) {
-    if (threadIdx.x == 0 && split == 0 && tb == 0 && kvh == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_LEN);
-    p0 = min(max(p0, 0), p.cap - p.T);
+  if (p0 < 0 || p0 + T > p.cap) {
+    if (threadIdx.x == 0 && split == 0 && kvh == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_LEN);
+    p0 = min(max(p0, 0), p.cap - T);
   }
-  const int Lb = p0 + t0 + nt;                          // keys the block's last query sees
+  const int Lb = p0 + T;                                // keys the last query sees
   const int per = ceil_div_i(ceil_div_i(Lb, p.nsplit), kPage) * kPage;
   const int s0 = split * per, s1 = min(Lb, s0 + per);   // this split's keys (s0 on a page edge)
   const int pg0 = s0 / kPage;
   const int npg = s1 > s0 ? ceil_div_i(s1, kPage) - pg0 : 0;
   const int mine = npg > warp ? ceil_div_i(npg - warp, kVW) : 0;   // pages of this warp
 
-  // query rows r = 4 j + g: token t0 + j, head kvh * 4 + g (rows of tokens past T are zero)
-  for (int i = threadIdx.x; i < kVRows * (kD / 8); i += kVThreads) {
-    const int r = i / (kD / 8), c = i % (kD / 8);
-    const int j = r / kGroup, g = r % kGroup;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (j < nt)
-      v = *reinterpret_cast<const uint4*>(
-          p.q + (static_cast<long long>(b) * p.T + t0 + j) * nq * kD + (kvh * kGroup + g) * kD + c * 8);
-    *reinterpret_cast<uint4*>(&s.q[r][c * 8]) = v;
-  }
   if (threadIdx.x == 0) {
     for (int i = 0; i < kVStages; ++i)
       for (int w = 0; w < kVW; ++w) mbar_init(smem_u32(&s.full[i][w]), 1);
@@ -1219,17 +1207,39 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
       }
     }
   };
+  // the first copies go out before the query rows are read
   int issued = 0;
   for (; issued < min(mine, kVStages) && !__shfl_sync(0xffffffffu, s.abort, 0); ++issued) issue(issued);
 
-  // lane: rows r = lane / 4 and r + 8, columns 2 (lane % 4) + {0, 1} of each n-block
-  const int rA = lane >> 2, rB = rA + 8;
-  const int limA = p0 + t0 + rA / kGroup, limB = p0 + t0 + rB / kGroup;   // last key each row sees
-  const bool liveA = rA / kGroup < nt, liveB = rB / kGroup < nt;
-  float mA = kNegBig, mB = kNegBig, lA = 0.f, lB = 0.f;
-  float o[16][4];
+  // query rows r = 4 j + g: token j, head kvh * 4 + g (rows of tokens past T are zero)
+  for (int i = threadIdx.x; i < R * (kD / 8); i += kVThreads) {
+    const int r = i / (kD / 8), c = i % (kD / 8);
+    const int j = r / kGroup, g = r % kGroup;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (j < T)
+      v = *reinterpret_cast<const uint4*>(
+          p.q + (static_cast<long long>(b) * T + j) * nq * kD + (kvh * kGroup + g) * kD + c * 8);
+    *reinterpret_cast<uint4*>(&s.q[r][c * 8]) = v;
+  }
+  __syncthreads();
+
+  // lane: in tile mt, rows 16 mt + lane / 4 (h = 0) and + 8 (h = 1), columns 2 (lane % 4) + {0, 1}
+  float m[MT][2], l[MT][2];
+  int lim[MT][2];            // last key each row sees (-1: a row past the T tokens)
 #pragma unroll
-  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = 16 * mt + 8 * h + (lane >> 2);
+      m[mt][h] = kNegBig;
+      l[mt][h] = 0.f;
+      lim[mt][h] = r / kGroup < T ? p0 + r / kGroup : -1;
+    }
+  float o[MT][16][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[mt][j][0] = o[mt][j][1] = o[mt][j][2] = o[mt][j][3] = 0.f;
   const int mi = lane >> 3, ri = lane & 7;
 
   for (int k = 0; k < mine; ++k) {
@@ -1238,61 +1248,31 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
     const int key0 = (pg0 + warp + k * kVW) * kPage;
     const uint32_t kbase = smem_u32(&s.k[slot][warp][0][0]);
     const uint32_t vbase = smem_u32(&s.v[slot][warp][0][0]);
-    // ---- S = Q K^T, 16 rows x 16 keys
-    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+    // ---- S = Q K^T, R rows x 16 keys
+    float c0[MT][4], c1[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c0[mt][e] = c1[mt][e] = 0.f;
     {
       const int tok = 8 * (mi >> 1) + ri;
       const uint32_t krow = kbase + tok * 128;
       const uint32_t qaddr = smem_u32(&s.q[lane & 15][(lane >> 4) * 8]);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(qaddr + ks * 32, a0, a1, a2, a3);
         const int h = ks >> 2, c = 2 * (ks & 3) + (mi & 1);
         uint32_t b00, b01, b10, b11;
         ldsm_x4(krow + h * kBoxBytes + ((c ^ ri) << 4), b00, b01, b10, b11);
-        mma16816_full(c0, a0, a1, a2, a3, b00, b01);
-        mma16816_full(c1, a0, a1, a2, a3, b10, b11);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(qaddr + mt * 16 * (kD + 8) * 2 + ks * 32, a0, a1, a2, a3);
+          mma16816_full(c0[mt], a0, a1, a2, a3, b00, b01);
+          mma16816_full(c1[mt], a0, a1, a2, a3, b10, b11);
+        }
       }
     }
     const int kc = key0 + 2 * (lane & 3);
-    float sv[8];   // row A: keys kc, kc+1, kc+8, kc+9; row B: the same keys
-    sv[0] = (liveA && kc < s1 && kc <= limA) ? c0[0] * p.scale_log2 : -INFINITY;
-    sv[1] = (liveA && kc + 1 < s1 && kc + 1 <= limA) ? c0[1] * p.scale_log2 : -INFINITY;
-    sv[2] = (liveA && kc + 8 < s1 && kc + 8 <= limA) ? c1[0] * p.scale_log2 : -INFINITY;
-    sv[3] = (liveA && kc + 9 < s1 && kc + 9 <= limA) ? c1[1] * p.scale_log2 : -INFINITY;
-    sv[4] = (liveB && kc < s1 && kc <= limB) ? c0[2] * p.scale_log2 : -INFINITY;
-    sv[5] = (liveB && kc + 1 < s1 && kc + 1 <= limB) ? c0[3] * p.scale_log2 : -INFINITY;
-    sv[6] = (liveB && kc + 8 < s1 && kc + 8 <= limB) ? c1[2] * p.scale_log2 : -INFINITY;
-    sv[7] = (liveB && kc + 9 < s1 && kc + 9 <= limB) ? c1[3] * p.scale_log2 : -INFINITY;
-    // ---- online softmax, rows A and B (4 lanes share a row)
-    float xA = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
-    float xB = fmaxf(fmaxf(sv[4], sv[5]), fmaxf(sv[6], sv[7]));
-    xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 1));
-    xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 2));
-    xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 1));
-    xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 2));
-    const float nA = fmaxf(mA, xA), nB = fmaxf(mB, xB);
-    const float aA = exp2f(mA - nA), aB = exp2f(mB - nB);
-    float pr[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) pr[i] = exp2f(sv[i] - nA);
-#pragma unroll
-    for (int i = 4; i < 8; ++i) pr[i] = exp2f(sv[i] - nB);
-    lA = lA * aA + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
-    lB = lB * aB + ((pr[4] + pr[5]) + (pr[6] + pr[7]));
-    mA = nA;
-    mB = nB;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      o[j][0] *= aA;
-      o[j][1] *= aA;
-      o[j][2] *= aB;
-      o[j][3] *= aB;
-    }
-    // P as the A operand: a0 row A keys 0-7, a1 row B keys 0-7, a2 row A keys 8-15, a3 row B 8-15
-    const uint32_t pa0 = pack_bf16(pr[0], pr[1]), pa1 = pack_bf16(pr[4], pr[5]);
-    const uint32_t pa2 = pack_bf16(pr[2], pr[3]), pa3 = pack_bf16(pr[6], pr[7]);
     // rows of the page past the split's keys may hold anything: zero them so 0 * V stays 0
     const int ntok = min(s1 - key0, kPage);
     if (ntok < kPage) {
@@ -1303,17 +1283,50 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
       }
       __syncwarp();
     }
-    // ---- O += P V
-    {
-      const int tok = 8 * (mi & 1) + ri;
-      const uint32_t vrow = vbase + tok * 128;
+    const int tok = 8 * (mi & 1) + ri;
+    const uint32_t vrow = vbase + tok * 128;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      // ---- online softmax, rows h = 0 / 1 of this tile (4 lanes share a row)
+      uint32_t pa[4];
+      float al[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int lm = lim[mt][h];
+        float sv[4];
+        sv[0] = (kc < s1 && kc <= lm) ? c0[mt][2 * h] * p.scale_log2 : -INFINITY;
+        sv[1] = (kc + 1 < s1 && kc + 1 <= lm) ? c0[mt][2 * h + 1] * p.scale_log2 : -INFINITY;
+        sv[2] = (kc + 8 < s1 && kc + 8 <= lm) ? c1[mt][2 * h] * p.scale_log2 : -INFINITY;
+        sv[3] = (kc + 9 < s1 && kc + 9 <= lm) ? c1[mt][2 * h + 1] * p.scale_log2 : -INFINITY;
+        float x = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+        x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
+        x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+        const float mn = fmaxf(m[mt][h], x);
+        al[h] = exp2f(m[mt][h] - mn);
+        float pr[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pr[e] = exp2f(sv[e] - mn);
+        l[mt][h] = l[mt][h] * al[h] + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
+        m[mt][h] = mn;
+        // P as the A operand: a0 / a1 rows h = 0 / 1 keys 0-7, a2 / a3 keys 8-15
+        pa[h] = pack_bf16(pr[0], pr[1]);
+        pa[2 + h] = pack_bf16(pr[2], pr[3]);
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[mt][j][0] *= al[0];
+        o[mt][j][1] *= al[0];
+        o[mt][j][2] *= al[1];
+        o[mt][j][3] *= al[1];
+      }
+      // ---- O += P V
 #pragma unroll
       for (int j = 0; j < 16; j += 2) {
         const int c = j + (mi >> 1);
         uint32_t b0a, b1a, b0b, b1b;
         ldsm_x4_t(vrow + (c >> 3) * kBoxBytes + (((c & 7) ^ ri) << 4), b0a, b1a, b0b, b1b);
-        mma16816_full(o[j], pa0, pa1, pa2, pa3, b0a, b1a);
-        mma16816_full(o[j + 1], pa0, pa1, pa2, pa3, b0b, b1b);
+        mma16816_full(o[mt][j], pa[0], pa[1], pa[2], pa[3], b0a, b1a);
+        mma16816_full(o[mt][j + 1], pa[0], pa[1], pa[2], pa[3], b0b, b1b);
       }
     }
     __syncwarp();
@@ -1324,87 +1337,94 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
     for (int k = max(issued - kVStages, 0); k < issued; ++k)
       mbar_wait(smem_u32(&s.full[k % kVStages][warp]), (k / kVStages) & 1, s, p.ws_err, false);
 
-  // ---- merge the 4 warps (partials in the ring memory), then the splits of this block
-  lA += __shfl_xor_sync(0xffffffffu, lA, 1);
-  lA += __shfl_xor_sync(0xffffffffu, lA, 2);
-  lB += __shfl_xor_sync(0xffffffffu, lB, 1);
-  lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+  // ---- merge the 4 warps (partials in the ring memory), then the splits of this pair
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      l[mt][h] += __shfl_xor_sync(0xffffffffu, l[mt][h], 1);
+      l[mt][h] += __shfl_xor_sync(0xffffffffu, l[mt][h], 2);
+    }
   __syncthreads();   // every warp is done with the rings
-  float* ob = reinterpret_cast<float*>(&s.k[0][0][0][0]);   // [kVW][kVRows][kD + 4]
+  float* ob = reinterpret_cast<float*>(&s.k[0][0][0][0]);   // [kVW][R][kD + 4]
   {
     const int c = 2 * (lane & 3);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      *reinterpret_cast<float2*>(&ob[(warp * kVRows + rA) * (kD + 4) + 8 * j + c]) = make_float2(o[j][0], o[j][1]);
-      *reinterpret_cast<float2*>(&ob[(warp * kVRows + rB) * (kD + 4) + 8 * j + c]) = make_float2(o[j][2], o[j][3]);
-    }
-    if ((lane & 3) == 0) {
-      s.red_m[warp][rA] = mA;
-      s.red_l[warp][rA] = lA;
-      s.red_m[warp][rB] = mB;
-      s.red_l[warp][rB] = lB;
+    for (int mt = 0; mt < MT; ++mt) {
+      const int rA = 16 * mt + (lane >> 2), rB = rA + 8;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        *reinterpret_cast<float2*>(&ob[(warp * R + rA) * (kD + 4) + 8 * j + c]) = make_float2(o[mt][j][0], o[mt][j][1]);
+        *reinterpret_cast<float2*>(&ob[(warp * R + rB) * (kD + 4) + 8 * j + c]) = make_float2(o[mt][j][2], o[mt][j][3]);
+      }
+      if ((lane & 3) == 0) {
+        s.red_m[warp][rA] = m[mt][0];
+        s.red_l[warp][rA] = l[mt][0];
+        s.red_m[warp][rB] = m[mt][1];
+        s.red_l[warp][rB] = l[mt][1];
+      }
     }
   }
   __syncthreads();
-  // thread -> row r, dims d0 .. d0 + 15
-  const int r = threadIdx.x >> 3, d0 = (threadIdx.x & 7) * 16;
+  // thread -> row r, dims d0 .. d0 + DPT - 1
+  constexpr int TPR = kVThreads / R, DPT = kD / TPR;
+  const int r = threadIdx.x / TPR, d0 = (threadIdx.x % TPR) * DPT;
   const int j = r / kGroup, g = r % kGroup;
   float M = kNegBig;
 #pragma unroll
   for (int w = 0; w < kVW; ++w) M = fmaxf(M, s.red_m[w][r]);
-  float Lsum = 0.f, O[16];
+  float Lsum = 0.f, O[DPT];
 #pragma unroll
-  for (int e = 0; e < 16; ++e) O[e] = 0.f;
+  for (int e = 0; e < DPT; ++e) O[e] = 0.f;
 #pragma unroll
   for (int w = 0; w < kVW; ++w) {
     const float f = exp2f(s.red_m[w][r] - M);
     Lsum += f * s.red_l[w][r];
 #pragma unroll
-    for (int e = 0; e < 16; e += 4) {
-      const float4 x = *reinterpret_cast<const float4*>(&ob[(w * kVRows + r) * (kD + 4) + d0 + e]);
+    for (int e = 0; e < DPT; e += 4) {
+      const float4 x = *reinterpret_cast<const float4*>(&ob[(w * R + r) * (kD + 4) + d0 + e]);
       O[e] += f * x.x;
       O[e + 1] += f * x.y;
       O[e + 2] += f * x.z;
       O[e + 3] += f * x.w;
     }
   }
-  bf16* dst = p.out + ((static_cast<long long>(b) * p.T + t0 + j) * nq + kvh * kGroup + g) * kD + d0;
+  bf16* dst = p.out + ((static_cast<long long>(b) * T + j) * nq + kvh * kGroup + g) * kD + d0;
   if (p.nsplit == 1) {
-    if (j < nt) {
+    if (j < T) {
       const float inv = 1.0f / Lsum;
 #pragma unroll
-      for (int e = 0; e < 16; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(O[e] * inv, O[e + 1] * inv);
+      for (int e = 0; e < DPT; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(O[e] * inv, O[e + 1] * inv);
     }
     return;
   }
   const long long slot = blockIdx.x;
-  float* po = p.ws_o + (slot * kVRows + r) * kD + d0;
+  float* po = p.ws_o + (slot * R + r) * kD + d0;
 #pragma unroll
-  for (int e = 0; e < 16; e += 4) *reinterpret_cast<float4*>(po + e) = make_float4(O[e], O[e + 1], O[e + 2], O[e + 3]);
-  if ((threadIdx.x & 7) == 0) p.ws_ml[slot * kVRows + r] = make_float2(M, Lsum);
+  for (int e = 0; e < DPT; e += 4) *reinterpret_cast<float4*>(po + e) = make_float4(O[e], O[e + 1], O[e + 2], O[e + 3]);
+  if ((threadIdx.x % TPR) == 0) p.ws_ml[slot * R + r] = make_float2(M, Lsum);
   __syncthreads();
-  const int cnt = pair * p.tblocks + tb;
   if (threadIdx.x == 0) {
     __threadfence();
-    s.last = atomicAdd(&p.ws_cnt[cnt], 1) == p.nsplit - 1;
+    s.last = atomicAdd(&p.ws_cnt[pair], 1) == p.nsplit - 1;
     if (s.last) __threadfence();   // acquire the other splits' partials
   }
   __syncthreads();
   if (!s.last) return;
-  // the last split of the block: online log-sum-exp over every split's partial
+  // the last split of the pair: online log-sum-exp over every split's partial
   const long long first = blockIdx.x - split;
   float Mm = kNegBig, Lm = 0.f;
 #pragma unroll
-  for (int e = 0; e < 16; ++e) O[e] = 0.f;
+  for (int e = 0; e < DPT; ++e) O[e] = 0.f;
   for (int sp = 0; sp < p.nsplit; ++sp) {
     const long long sl = first + sp;
-    const float2 ml = __ldcg(&p.ws_ml[sl * kVRows + r]);
+    const float2 ml = __ldcg(&p.ws_ml[sl * R + r]);
     const float mn = fmaxf(Mm, ml.x);
     const float a = exp2f(Mm - mn), f = exp2f(ml.x - mn);
     Lm = Lm * a + ml.y * f;
-    const float* src = p.ws_o + (sl * kVRows + r) * kD + d0;
+    const float* src = p.ws_o + (sl * R + r) * kD + d0;
 #pragma unroll
-    for (int e = 0; e < 16; e += 4) {
+    for (int e = 0; e < DPT; e += 4) {
       const float4 x = __ldcg(reinterpret_cast<const float4*>(src + e));
       O[e] = O[e] * a + x.x * f;
       O[e + 1] = O[e + 1] * a + x.y * f;
@@ -1413,12 +1433,12 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
     }
     Mm = mn;
   }
-  if (j < nt) {
+  if (j < T) {
     const float inv = 1.0f / Lm;
 #pragma unroll
-    for (int e = 0; e < 16; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(O[e] * inv, O[e + 1] * inv);
+    for (int e = 0; e < DPT; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(O[e] * inv, O[e + 1] * inv);
   }
-  if (threadIdx.x == 0) atomicExch(&p.ws_cnt[cnt], 0);
+  if (threadIdx.x == 0) atomicExch(&p.ws_cnt[pair], 0);
 }
 
 // ------------------------------------------------------------------------------ host side
@@ -1428,14 +1448,13 @@ inline int64_t align256(int64_t x) { return (x + 255) & ~static_cast<int64_t>(25
 struct WsLayout {
   int64_t err, cnt, ml, o, total;
 };
-// counters: one per (pair, token block); partials: rows per slot = 4 (T = 1) or 16 (verify)
+// counters: one per pair; partials: rows per slot = 4 (T = 1) or 16 / 32 (verify, T <= 4 / 8)
 inline WsLayout ws_layout(int B, int nkv, int max_units, int T = 1) {
-  const int blocks = T > 1 ? (T + kVTok - 1) / kVTok : 1;
-  const int rows = T > 1 ? kVRows : kGroup;
+  const int rows = T > 1 ? 16 * verify_tiles(T) : kGroup;
   WsLayout w;
   w.err = 0;
   w.cnt = kHeaderBytes;
-  w.ml = w.cnt + align256(static_cast<int64_t>(B) * nkv * blocks * 4);
+  w.ml = w.cnt + align256(static_cast<int64_t>(B) * nkv * 4);
   w.o = w.ml + align256(static_cast<int64_t>(max_units) * rows * 8);
   w.total = w.o + static_cast<int64_t>(max_units) * rows * kD * 4;
   return w;
@@ -1592,34 +1611,47 @@ int launch_attn(const kopt_plan* plan, Params& p, void* stream) {
   return KOPT_OK;
 }
 
-template <bool PAGED>
+template <bool PAGED, int MT>
 int verify_occupancy(int device, int* blocks_per_sm) {
   static int configured[64] = {0};
   if (device < 0 || device >= 64) return KOPT_ERR_ARG;
-  auto kern = verify_attn_kernel<PAGED>;
+  auto kern = verify_attn_kernel<PAGED, MT>;
   if (!configured[device]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kVSmemBytes)) != cudaSuccess)
+                             static_cast<int>(vsmem_bytes<MT>())) != cudaSuccess)
       return KOPT_ERR_CUDA;
     configured[device] = 1;
   }
   if (blocks_per_sm &&
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kern, kVThreads, kVSmemBytes) !=
-          cudaSuccess)
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kern, kVThreads,
+                                                    vsmem_bytes<MT>()) != cudaSuccess)
     return KOPT_ERR_CUDA;
   return KOPT_OK;
 }
+int verify_configure(int device, int T, int* blocks_per_sm) {
+  int rc = verify_tiles(T) == 1 ? verify_occupancy<true, 1>(device, blocks_per_sm)
+                                : verify_occupancy<true, 2>(device, blocks_per_sm);
+  if (rc) return rc;
+  return verify_tiles(T) == 1 ? verify_occupancy<false, 1>(device, nullptr)
+                              : verify_occupancy<false, 2>(device, nullptr);
+}
 
+template <bool PAGED, int MT>
+int launch_verify_t(const kopt_plan* plan, Params& p, void* stream) {
+  int rc = verify_occupancy<PAGED, MT>(plan->device, nullptr);
+  if (rc) return rc;
+  verify_attn_kernel<PAGED, MT><<<plan->grid, kVThreads, vsmem_bytes<MT>(),
+                                  static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+}
 template <bool PAGED>
 int launch_verify(const kopt_plan* plan, Params& p, void* stream) {
   int rc = set_device(plan->device);
   if (rc) return rc;
-  rc = verify_occupancy<PAGED>(plan->device, nullptr);
-  if (rc) return rc;
-  p.tblocks = (plan->T + kVTok - 1) / kVTok;
-  p.nsplit = plan->grid / (plan->B * plan->nkv * p.tblocks);
-  verify_attn_kernel<PAGED><<<plan->grid, kVThreads, kVSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
-  return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+  p.tblocks = 1;
+  p.nsplit = plan->grid / (plan->B * plan->nkv);
+  return verify_tiles(plan->T) == 1 ? launch_verify_t<PAGED, 1>(plan, p, stream)
+                                    : launch_verify_t<PAGED, 2>(plan, p, stream);
 }
 
 }  // namespace kopt
@@ -1655,17 +1687,17 @@ int kopt_decode_attn_plan(int device, int B, int T, int nq, int nkv, int d, int 
   int sms = 0, occ = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
     return KOPT_ERR_CUDA;
-  if (T > 1) {   // verify: grid = pairs x token blocks x key splits, about two waves
+  if (T > 1) {   // verify: grid = pairs x key splits, one wave
     if (max_len < T) return KOPT_ERR_ARG;
-    rc = verify_occupancy<true>(device, &occ);
-    if (rc) return rc;
-    rc = verify_occupancy<false>(device, nullptr);
+    rc = verify_configure(device, T, &occ);
     if (rc) return rc;
     if (occ < 1) return KOPT_ERR_CUDA;
-    const long long blocks = static_cast<long long>(B) * nkv * ((T + kVTok - 1) / kVTok);
-    const long long target = target_ctas > 0 ? target_ctas : 2ll * sms * occ;
-    long long nsplit = (target + blocks - 1) / blocks;
+    const long long blocks = static_cast<long long>(B) * nkv;
     const long long max_split = (static_cast<long long>(max_len) + 2 * kPage - 1) / (2 * kPage);
+    // one wave: each CTA pays a fixed cost for its q rows and its merge, so fewer and longer
+    // splits win (measured: B=16, T=3, 4099 keys, 52 us at 256 CTAs, 72 us at 1152)
+    const long long slots = target_ctas > 0 ? target_ctas : static_cast<long long>(sms) * occ;
+    long long nsplit = slots / blocks;
     nsplit = nsplit < 1 ? 1 : nsplit > max_split ? max_split : nsplit;
     if (blocks * nsplit >= (1ll << 31)) return KOPT_ERR_ARG;
     plan->B = B;

@@ -55,7 +55,7 @@ def test_verify_one_split_and_many_splits(target_ctas):
     """One split (outputs stored directly) and as many splits as the capacity allows (most of
     them empty for the short sequences, merged by the last)."""
     attn, _ = _run(3, 5, [3, 700, 4100], 4200, seed=7, target_ctas=target_ctas)
-    nsplit = attn.plan.grid // (3 * NKV * 2)
+    nsplit = attn.plan.grid // (3 * NKV)
     assert (nsplit == 1) == (target_ctas == 1)
 
 
