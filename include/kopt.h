@@ -100,8 +100,10 @@ typedef struct kopt_plan {
 #define KOPT_PLAN_OVERLAP_PREV 1
 
 /* Plan a decode-attention launch: B sequences of at most max_len keys, T query tokens each
- * (T == 1), nq = 4 * nkv query heads of dim d == 128. target_ctas <= 0 launches one CTA per
- * resident slot (SM count x resident CTAs per SM); a positive value fixes the grid instead.
+ * (1 .. 8; T > 1 is the verify step, query t of a sequence seeing keys 0 .. pos + t, and only
+ * kopt_decode_attn runs it), nq = 4 * nkv query heads of dim d == 128. target_ctas <= 0 launches
+ * one CTA per resident slot (SM count x resident CTAs per SM); a positive value fixes the grid
+ * (T = 1) or the number of CTAs the key splits may use (T > 1) instead.
  * Replaces DecodeAttention.__init__ (engine/kernels/fused.py:209-219), which also sizes its
  * scratch from the capacity. */
 KOPT_API int kopt_decode_attn_plan(int device, int B, int T, int nq, int nkv, int d, int max_len,
@@ -115,8 +117,9 @@ KOPT_API int kopt_workspace_init(const kopt_plan* plan, void* ws, void* stream);
  * stream. */
 KOPT_API int kopt_read_error(const kopt_plan* plan, void* ws, int* err_out, void* stream);
 
-/* Split-K GQA decode attention over a cache whose new K/V are already written at pos[b]:
- * out[b, h*128:(h+1)*128] = softmax(q_h . K[b, h/4, 0..pos[b]]^T * scale) V[b, h/4, 0..pos[b]].
+/* Split-K GQA decode attention over a cache whose new K/V are already written at pos[b] (and,
+ * for T > 1, at pos[b] + 1 .. pos[b] + T - 1): row b*T + t of out, head h =
+ * softmax(q_(b*T+t),h . K[b, h/4, 0..pos[b]+t]^T * scale) V[b, h/4, 0..pos[b]+t].
  * q, out: [B*T, nq*128] bf16 contiguous; pos: [B] int32 device. Writes out and the workspace.
  * Replaces DecodeAttention.__call__(q, k_cache, v_cache, pos, out) (engine/kernels/fused.py:221). */
 KOPT_API int kopt_decode_attn(const kopt_plan* plan, const void* q, const kopt_kv_cache* cache,
