@@ -125,6 +125,17 @@ KOPT_API int kopt_read_error(const kopt_plan* plan, void* ws, int* err_out, void
 KOPT_API int kopt_decode_attn(const kopt_plan* plan, const void* q, const kopt_kv_cache* cache,
                      const int32_t* pos, void* out, void* ws, float scale, void* stream);
 
+/* ---- decode-step epilogues (the ops around the projections of a layer) -------------------- */
+/* res <- bf16(res + delta) when delta is not NULL; out = bf16(w * bf16(res * rsqrt(mean(res^2)
+ * + eps))) per row, fp32 arithmetic. res, delta, out: [M, N] bf16, w: [N]; N a multiple of 8.
+ * Replaces add_rms_norm(res, delta, weight, out, eps) (engine/kernels/fused.py:39-46). */
+KOPT_API int kopt_add_rms_norm(void* res, const void* delta, const void* weight, void* out, int M,
+                               int N, float eps, void* stream);
+/* out[m, i] = bf16(bf16(silu(gu[m, i])) * gu[m, I + i]): gate and up side by side in
+ * gate_up [M, 2 I], out [M, I] bf16; I a multiple of 8.
+ * Replaces silu_mul(gu, out) (engine/kernels/fused.py:123-127). */
+KOPT_API int kopt_silu_mul(const void* gate_up, void* out, int M, int I, void* stream);
+
 /* Per-head QK-RMSNorm + RoPE + KV append (no attention), reference cast order:
  * qkv [B*T, (nq + 2 nkv) * 128]; q heads -> q_out [B*T, nq*128]; k heads -> cache k at
  * pos[b] + t; v heads copied to cache v at pos[b] + t. cos/sin: [rope_len, 128] bf16.

@@ -43,6 +43,8 @@ EXPORTED = (
     "kopt_ipc_get_handle",
     "kopt_ipc_open",
     "kopt_ipc_close",
+    "kopt_add_rms_norm",
+    "kopt_silu_mul",
 )
 
 IPC_HANDLE_BYTES = 64
@@ -130,6 +132,8 @@ _SIGS = {
     "kopt_ipc_get_handle": (_i32, [_vp, _vp]),
     "kopt_ipc_open": (_i32, [_i32, _vp, ctypes.POINTER(_vp)]),
     "kopt_ipc_close": (_i32, [_i32, _vp]),
+    "kopt_add_rms_norm": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _f32, _vp]),
+    "kopt_silu_mul": (_i32, [_vp, _vp, _i32, _i32, _vp]),
 }
 
 

@@ -1441,6 +1441,102 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
   if (threadIdx.x == 0) atomicExch(&p.ws_cnt[pair], 0);
 }
 
+// ============================================================ decode-step epilogue kernels
+// The two small ops around the projections of a decode step, in the reference's cast order
+// (fused.py:13-46, 107-127, itself Transformers' Qwen3RMSNorm and Qwen3MLP): fp32 arithmetic,
+// rounded to bf16 where the reference rounds.
+
+// res <- bf16(res + delta) (if delta); out = bf16(w * bf16(res * rsqrt(mean(res^2) + eps))).
+// One CTA per row; a thread holds 8-element vectors.
+__global__ void add_rms_norm_kernel(bf16* __restrict__ res, const bf16* __restrict__ delta,
+                                    const bf16* __restrict__ w, bf16* __restrict__ out, int n,
+                                    float eps) {
+  __shared__ float part[32];
+  const long long row = blockIdx.x;
+  const int nv = n / 8;
+  bf16* x = res + row * n;
+  float ss = 0.f;
+  uint4 keep[4];   // up to 4 vectors per thread (n <= 32 * blockDim)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
+    if (v >= nv) break;
+    uint4 a = *reinterpret_cast<const uint4*>(x + v * 8);
+    if (delta != nullptr) {
+      const uint4 d = *reinterpret_cast<const uint4*>(delta + row * n + v * 8);
+      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+      const uint32_t* pd = reinterpret_cast<const uint32_t*>(&d);
+      uint4 sum;
+      uint32_t* ps = reinterpret_cast<uint32_t*>(&sum);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fa = bf2f(pa[e]), fd = bf2f(pd[e]);
+        ps[e] = pack_bf16(__fadd_rn(fa.x, fd.x), __fadd_rn(fa.y, fd.y));
+      }
+      a = sum;
+      *reinterpret_cast<uint4*>(x + v * 8) = a;
+    }
+    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = bf2f(pa[e]);
+      ss = __fadd_rn(ss, __fadd_rn(__fmul_rn(f.x, f.x), __fmul_rn(f.y, f.y)));
+    }
+    keep[i] = a;
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  if (lane == 0) part[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < nw ? part[lane] : 0.f;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, off));
+    if (lane == 0) part[0] = t;
+  }
+  __syncthreads();
+  const float rstd = rsqrtf(__fadd_rn(__fdiv_rn(part[0], static_cast<float>(n)), eps));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
+    if (v >= nv) break;
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + v * 8);
+    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&keep[i]);
+    const uint32_t* pw = reinterpret_cast<const uint32_t*>(&wv);
+    uint4 y;
+    uint32_t* py = reinterpret_cast<uint32_t*>(&y);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = bf2f(pa[e]), fw = bf2f(pw[e]);
+      py[e] = pack_bf16(__fmul_rn(fw.x, bf16r(__fmul_rn(f.x, rstd))),
+                        __fmul_rn(fw.y, bf16r(__fmul_rn(f.y, rstd))));
+    }
+    *reinterpret_cast<uint4*>(out + row * n + v * 8) = y;
+  }
+}
+
+// out[m, i] = bf16(bf16(silu(g)) * u), g = gu[m, i], u = gu[m, I + i]; a thread per 8 columns.
+__global__ void silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ out, int I) {
+  const long long m = blockIdx.y;
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (v >= I / 8) return;
+  const uint4 g = *reinterpret_cast<const uint4*>(gu + m * 2 * I + v * 8);
+  const uint4 u = *reinterpret_cast<const uint4*>(gu + m * 2 * I + I + v * 8);
+  const uint32_t* pg = reinterpret_cast<const uint32_t*>(&g);
+  const uint32_t* pu = reinterpret_cast<const uint32_t*>(&u);
+  uint4 y;
+  uint32_t* py = reinterpret_cast<uint32_t*>(&y);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 fg = bf2f(pg[e]), fu = bf2f(pu[e]);
+    const float s0 = bf16r(__fdiv_rn(fg.x, __fadd_rn(1.0f, expf(-fg.x))));
+    const float s1 = bf16r(__fdiv_rn(fg.y, __fadd_rn(1.0f, expf(-fg.y))));
+    py[e] = pack_bf16(__fmul_rn(s0, fu.x), __fmul_rn(s1, fu.y));
+  }
+  *reinterpret_cast<uint4*>(out + m * I + v * 8) = y;
+}
+
 // ------------------------------------------------------------------------------ host side
 constexpr int64_t kHeaderBytes = 256;
 inline int64_t align256(int64_t x) { return (x + 255) & ~static_cast<int64_t>(255); }
@@ -1662,6 +1758,33 @@ using namespace kopt;
 extern "C" {
 
 int kopt_abi_version(void) { return 1; }
+
+int kopt_add_rms_norm(void* res, const void* delta, const void* weight, void* out, int M, int N,
+                      float eps, void* stream) {
+  if (res == nullptr || weight == nullptr || out == nullptr || M < 1 || N < 8 || N % 8 != 0 ||
+      N > 8 * 4 * 1024 || !aligned16(res) || !aligned16(weight) || !aligned16(out) ||
+      (delta != nullptr && !aligned16(delta)))
+    return KOPT_ERR_ARG;
+  const int nv = N / 8;
+  int threads = (nv + 3) / 4;                         // at most 4 vectors per thread
+  threads = threads < 32 ? 32 : (threads + 31) / 32 * 32;
+  if (threads > 1024) return KOPT_ERR_ARG;
+  add_rms_norm_kernel<<<M, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<bf16*>(res), static_cast<const bf16*>(delta), static_cast<const bf16*>(weight),
+      static_cast<bf16*>(out), N, eps);
+  return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+}
+
+int kopt_silu_mul(const void* gate_up, void* out, int M, int I, void* stream) {
+  if (gate_up == nullptr || out == nullptr || M < 1 || I < 8 || I % 8 != 0 || M > 65535 ||
+      !aligned16(gate_up) || !aligned16(out))
+    return KOPT_ERR_ARG;
+  const int nv = I / 8;
+  const dim3 grid((nv + 255) / 256, M);
+  silu_mul_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const bf16*>(gate_up), static_cast<bf16*>(out), I);
+  return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+}
 
 const char* kopt_strerror(int status) {
   switch (status) {

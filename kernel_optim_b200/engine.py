@@ -11,9 +11,11 @@ Keeps the reference engine's surface (GodRishUniverse/kernel_optim engine/engine
 What changes is the decode step (engine.py:313-341, 388-401): the per-layer ``qk_norm_rope`` +
 ``attn1`` pair becomes one ``PagedDecodeAttention`` launch over a paged KV cache, and the whole step
 is captured once per shape in a CUDA graph and replayed, pipelined one step ahead of the host as in
-engine.py:509-533. Projections, norms, the MLP and the LM head run as the loaded Transformers
-modules (cuBLAS), exactly the native path's arithmetic. Prefill is the native Transformers forward
-with its DynamicCache, whose K/V are copied into the pages (prefill is not the optimised path).
+engine.py:509-533. Around it the layer runs as engine.py:325-340 does: the residual add and RMSNorm
+in one kernel (``add_rms_norm``), the projections as cuBLAS GEMMs against fused weights (q/k/v; gate
+and up), and SwiGLU in one kernel (``silu_mul``), all in Transformers' cast order. Prefill is the
+native Transformers forward with its DynamicCache, whose K/V are copied into the pages (prefill is
+not the optimised path).
 
 Multi-GPU (``group`` = a torch.distributed process group of G ranks, one GPU each, one node): rank r
 keeps kv heads [r*nkv/G, (r+1)*nkv/G) — their QKV weight rows and their pages — and runs attention
@@ -25,10 +27,10 @@ attention is replicated, so every rank emits the same tokens.
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from ._lib import KoptError
 from .paged import PAGE, PagedDecodeAttention, PagedKVCache
+from .fused import add_rms_norm, silu_mul
 from .gather import PeerGather, slot_of
 from .shard import head_range, shard_qkv_weight
 
@@ -76,6 +78,7 @@ class Engine:
         with torch.no_grad():
             for layer in base.layers:
                 a = layer.self_attn
+                mlp = layer.mlp
                 self.layers.append(dict(
                     mod=layer,
                     # this rank's q/k/v rows in one weight, as engine.py:148 fuses them
@@ -83,7 +86,15 @@ class Engine:
                                          self.nkv, self.rank, self.world, self.d),
                     q_norm=a.q_norm.weight.contiguous(),
                     k_norm=a.k_norm.weight.contiguous(),
+                    o=a.o_proj.weight,
+                    # gate rows then up rows, the layout silu_mul reads (engine.py:150)
+                    gu=torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight], 0).contiguous(),
+                    down=mlp.down_proj.weight,
+                    w_in=layer.input_layernorm.weight.contiguous(),
+                    w_post=layer.post_attention_layernorm.weight.contiguous(),
                 ))
+            self.final_norm = base.norm.weight.contiguous()
+            self.inter = base.layers[0].mlp.gate_proj.weight.shape[0]
         self._shape = None
         self.graph = None
         self.pg = None
@@ -114,6 +125,10 @@ class Engine:
         self.ids = torch.zeros(B, dtype=torch.int64, device=dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
         self.attn_out = torch.zeros(B, self.nq_l * self.d, dtype=bf, device=dev)
+        H = self.embed.shape[1]
+        self.hid = torch.zeros(B, H, dtype=bf, device=dev)       # residual stream
+        self.normed = torch.zeros(B, H, dtype=bf, device=dev)
+        self.act = torch.zeros(B, self.inter, dtype=bf, device=dev)
         if self.pg is not None:
             self.pg.close()
             self.pg = None
@@ -152,15 +167,20 @@ class Engine:
                               self.cache, i, self.pos, slot_of(i, self.n_layers))
 
     def _step(self):
-        """One decode step at positions pos[b]; argmax feeds ids, positions advance."""
-        x = F.embedding(self.ids, self.embed)
+        """One decode step at positions pos[b]; argmax feeds ids, positions advance. The layer
+        loop of engine.py:325-340: every residual add is fused into the RMSNorm that follows it."""
+        h, n = self.hid, self.normed
+        torch.index_select(self.embed, 0, self.ids, out=h)
+        delta = None
         for i, lw in enumerate(self.layers):
-            layer = lw["mod"]
-            h = layer.input_layernorm(x)
-            qkv = torch.mm(h, lw["qkv"].t())
-            x = x + layer.self_attn.o_proj(self._attention(i, lw, qkv))
-            x = x + layer.mlp(layer.post_attention_layernorm(x))
-        logits = self.model.lm_head(self.model.model.norm(x))
+            add_rms_norm(h, delta, lw["w_in"], n, self.eps)
+            qkv = torch.mm(n, lw["qkv"].t())
+            o = torch.mm(self._attention(i, lw, qkv), lw["o"].t())
+            add_rms_norm(h, o, lw["w_post"], n, self.eps)
+            silu_mul(torch.mm(n, lw["gu"].t()), self.act)
+            delta = torch.mm(self.act, lw["down"].t())
+        add_rms_norm(h, delta, self.final_norm, n, self.eps)
+        logits = self.model.lm_head(n)
         torch.argmax(logits, dim=-1, out=self.ids)
         self.pos.add_(1)
 

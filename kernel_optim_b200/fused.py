@@ -155,3 +155,33 @@ def qk_norm_rope(qkv, q_w, k_w, cos, sin, pos, q_out, k_cache, v_cache, T, eps, 
                                        cos.shape[0], _ptr(pos), _ptr(q_out), ctypes.byref(cache),
                                        M // T, T, nq, nkv, d, ctypes.c_float(eps), _ptr(err),
                                        dev.index, _stream(dev)), "kopt_qk_norm_rope")
+
+
+def add_rms_norm(res, delta, weight, out, eps):
+    """out = rmsnorm(res + delta) * weight; res <- res + delta (rounded to bf16) when delta is
+    given. Rows contiguous [M, N] bf16. Mirrors engine/kernels/fused.py:39-46."""
+    _require_cuda(res, "res")
+    _require_cuda(weight, "weight")
+    _require_cuda(out, "out")
+    if delta is not None:
+        _require_cuda(delta, "delta")
+    M, N = res.shape
+    if out.shape != res.shape or weight.shape != (N,) or (delta is not None and delta.shape != res.shape):
+        raise KoptError("add_rms_norm: res/delta/out must be [M, N] and weight [N]")
+    for t in (res, weight, out) + ((delta,) if delta is not None else ()):
+        if not t.is_contiguous():
+            raise KoptError("add_rms_norm: tensors must be contiguous")
+    check(_lib.lib().kopt_add_rms_norm(_ptr(res), _ptr(delta), _ptr(weight), _ptr(out), M, N,
+                                       ctypes.c_float(eps), _stream(res.device)), "kopt_add_rms_norm")
+
+
+def silu_mul(gu, out):
+    """out = bf16(bf16(silu(gate)) * up) with gate = gu[:, :I], up = gu[:, I:]; gu [M, 2I], out
+    [M, I] bf16. Mirrors engine/kernels/fused.py:123-127."""
+    _require_cuda(gu, "gu")
+    _require_cuda(out, "out")
+    M, two_i = gu.shape
+    if two_i % 2 or out.shape != (M, two_i // 2) or not gu.is_contiguous() or not out.is_contiguous():
+        raise KoptError("silu_mul: gu must be [M, 2I] and out [M, I], contiguous")
+    check(_lib.lib().kopt_silu_mul(_ptr(gu), _ptr(out), M, two_i // 2, _stream(gu.device)),
+          "kopt_silu_mul")

@@ -112,3 +112,27 @@ def test_verify_oracle_matches_masked_restatement():
     a = verify_attn_fp32(q, k, v, pos, T)
     b = verify_attn_masked_fp32(q, k, v, pos, T)
     assert torch.allclose(a, b, atol=1e-5, rtol=1e-5)
+
+
+def test_epilogue_restatement_matches_transformers():
+    """The decode-step epilogues restated (oracle/epilogue.py) against Transformers' own modules:
+    Qwen3RMSNorm after a bf16 residual add, and Qwen3MLP's act_fn(gate) * up."""
+    from transformers import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm
+    from oracle.epilogue import add_rms_norm_ref, silu_mul_ref
+    g = torch.Generator().manual_seed(4)
+    M, N, I = 5, 256, 96
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    delta = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    norm = Qwen3RMSNorm(N, eps=1e-6)
+    with torch.no_grad():
+        norm.weight.copy_((1 + 0.1 * torch.randn(N, generator=g)).to(torch.float32))
+    norm = norm.to(torch.bfloat16)
+    new_res, y = add_rms_norm_ref(res, delta, norm.weight.data, 1e-6)
+    want_res = res + delta
+    assert torch.equal(new_res, want_res)
+    assert torch.equal(y, norm(want_res))
+    gu = torch.randn(M, 2 * I, generator=g).to(torch.bfloat16)
+    act = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+    assert torch.equal(silu_mul_ref(gu), act)
+    del Qwen3Config
