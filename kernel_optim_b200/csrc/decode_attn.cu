@@ -61,6 +61,8 @@ constexpr int kMaxB = 256;
 constexpr int kMaxRanks = KOPT_MAX_RANKS;   // fused gather: ranks of one node
 constexpr int kBoxBytes = kPage * kHalf * 2;   // 2 KiB: one TMA box
 constexpr int kChunkPages = 32;                // dynamic chunk: 512 keys of the page line
+constexpr int kLateCtas = 4;                   // CTAs whose static piece is shortened (late start)
+constexpr int kLateMax = 24;                   // pages taken off the last CTA's piece
 constexpr int kMaxPend = 8;                    // partial units a CTA holds before releasing them
 constexpr int kDefaultStaticPct = 100;         // share of the page line split statically
 constexpr unsigned long long kTimeoutNs = 1000000000ull;  // 1 s per mbarrier wait
@@ -100,6 +102,7 @@ struct Params {
   int bt_stride, num_pages, cap, rope_len;
   int B, T, nkv;
   int static_pct;        // share of the page line cut into one static piece per CTA
+  int late_skew;         // launched to overlap the previous kernel: the last CTAs start late
   int nsplit, tblocks;   // verify kernel (T > 1): key splits, blocks of 4 query tokens
   float scale_log2, eps;
 };
@@ -127,6 +130,7 @@ struct __align__(1024) Smem {
   int total_pages;
   int static_pages;                     // P: pages of the line split into one piece per CTA
   int total_chunks;                     // grid static pieces + dynamic chunks
+  int late;                             // the last kLateCtas pieces are shortened (see chunk_range)
   volatile int nclaimed;                // ring entries 0 .. nclaimed-1 are valid
   int npend;                            // partial units written, not yet released
   int pend[kMaxPend][5];                // their (pair, first chunk, chunks, sequence, kv head)
@@ -351,16 +355,39 @@ __device__ void compute_plan(const Params& p, Smem& s, int lane) {
     s.total_pages = carry;
     s.static_pages = P;
     s.total_chunks = G + ceil_div_i(carry - P, kChunkPages);
+    s.late = p.late_skew && G > 2 * kLateCtas && P / G >= 4 * kLateMax;
   }
 }
 
 // Chunk k's page range on the line: k < grid is CTA k's static piece [k P / G, (k+1) P / G) of the
 // first P pages (P >= G, so no piece is empty, or P = 0); k >= grid is dynamic chunk k - grid, 32
 // pages from P + 32 (k - grid), clipped to the end of the line.
+// With programmatic dependent launch the last CTAs of the grid are placed last, on the SMs the
+// previous kernel frees last, and start late (device timestamps: ~4.5, ~2.5, ~1-1.5 us for the
+// last, second-to-last and next two on c2); their pieces are shorter by kLatePages and the other
+// CTAs share the difference. Measured on c2: 48.9 -> 48.5 us per call.
+__device__ __forceinline__ int late_pages(int r) { return r == 0 ? kLateMax : r == 1 ? kLateMax / 2 : kLateMax / 4; }
+__device__ __forceinline__ int late_front(const Smem& s) {   // pages of the first G - 4 pieces
+  const int q = s.static_pages / static_cast<int>(gridDim.x);
+  int d = 0;
+  for (int r = 0; r < kLateCtas; ++r) d += late_pages(r);
+  return s.static_pages - (kLateCtas * q - d);
+}
 __device__ __forceinline__ void chunk_range(const Smem& s, int k, int& x0, int& x1) {
   const int G = gridDim.x;
   const long long P = s.static_pages;
-  if (k < G) {
+  if (k < G && s.late) {
+    const int G4 = G - kLateCtas, F = late_front(s), q = s.static_pages / G;
+    if (k < G4) {
+      x0 = static_cast<int>(static_cast<long long>(k) * F / G4);
+      x1 = static_cast<int>(static_cast<long long>(k + 1) * F / G4);
+    } else {   // piece G4 + i is q - late_pages(3 - i) long: the last CTA's is the shortest
+      int x = F;
+      for (int j = 0; j < k - G4; ++j) x += q - late_pages(kLateCtas - 1 - j);
+      x0 = x;
+      x1 = x + q - late_pages(kLateCtas - 1 - (k - G4));
+    }
+  } else if (k < G) {
     x0 = static_cast<int>(k * P / G);
     x1 = static_cast<int>((k + 1) * P / G);
   } else {
@@ -372,6 +399,17 @@ __device__ __forceinline__ void chunk_range(const Smem& s, int k, int& x0, int& 
 __device__ __forceinline__ int chunk_of(const Smem& s, int y) {
   const long long G = gridDim.x;
   const long long P = s.static_pages;
+  if (y < P && s.late) {
+    const int G4 = static_cast<int>(G) - kLateCtas, F = late_front(s);
+    const int q = s.static_pages / static_cast<int>(G);
+    if (y < F) return static_cast<int>((static_cast<long long>(y + 1) * G4 - 1) / F);
+    int x = F, i = 0;
+    while (i < kLateCtas - 1 && x + q - late_pages(kLateCtas - 1 - i) <= y) {
+      x += q - late_pages(kLateCtas - 1 - i);
+      ++i;
+    }
+    return G4 + i;
+  }
   return y < P ? static_cast<int>(((y + 1) * G - 1) / P)
                : static_cast<int>(G) + (y - static_cast<int>(P)) / kChunkPages;
 }
@@ -1690,6 +1728,7 @@ int launch_attn(const kopt_plan* plan, Params& p, void* stream) {
   rc = attn_occupancy<PAGED, FUSED>(plan->device, nullptr);
   if (rc) return rc;
   if (plan->flags & ~KOPT_PLAN_OVERLAP_PREV) return KOPT_ERR_ARG;
+  p.late_skew = (plan->flags & KOPT_PLAN_OVERLAP_PREV) ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(plan->grid);
   cfg.blockDim = dim3(kThreads);

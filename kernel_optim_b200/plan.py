@@ -11,6 +11,8 @@ without a GPU:
 * with P = floor(pct T / 100) (0 when P < grid), chunk k < grid is CTA k's static piece
   [k P / grid, (k+1) P / grid); chunk k >= grid is the dynamic chunk [P + 32 (k - grid), ...)
   clipped to T, claimed at run time;
+* with overlapped launches (skew) and long enough pieces, the last LATE_CTAS pieces are shorter by
+  LATE_PAGES (the last CTA's most) and the first grid - LATE_CTAS pieces share the difference;
 * a unit is a chunk's intersection with one pair; its partial result goes to workspace slot k + q,
   and the last of the pair's n units to finish merges slots c + q for c in c0 .. c0 + n - 1.
 """
@@ -22,6 +24,8 @@ from dataclasses import dataclass
 PAGE = 16
 CHUNK_PAGES = 32
 STATIC_PCT = 100
+LATE_CTAS = 4
+LATE_PAGES = (24, 12, 6, 6)     # taken off the pieces of the last, second-to-last, ... CTA
 
 
 @dataclass(frozen=True)
@@ -49,9 +53,20 @@ class Plan:
     static_pages: int
     total_chunks: int
     grid: int
+    late: bool = False
+
+    def _late_front(self) -> int:
+        q = self.static_pages // self.grid
+        return self.static_pages - (LATE_CTAS * q - sum(LATE_PAGES))
 
     def chunk_range(self, k: int):
         G, P = self.grid, self.static_pages
+        if k < G and self.late:
+            G4, F, q = G - LATE_CTAS, self._late_front(), P // G
+            if k < G4:
+                return k * F // G4, (k + 1) * F // G4
+            x = F + sum(q - LATE_PAGES[LATE_CTAS - 1 - j] for j in range(k - G4))
+            return x, x + q - LATE_PAGES[LATE_CTAS - 1 - (k - G4)]
         if k < G:
             return k * P // G, (k + 1) * P // G
         x0 = P + (k - G) * CHUNK_PAGES
@@ -59,10 +74,21 @@ class Plan:
 
     def chunk_of(self, y: int) -> int:
         G, P = self.grid, self.static_pages
+        if y < P and self.late:
+            G4, F, q = G - LATE_CTAS, self._late_front(), P // G
+            if y < F:
+                return ((y + 1) * G4 - 1) // F
+            x, i = F, 0
+            while i < LATE_CTAS - 1 and x + q - LATE_PAGES[LATE_CTAS - 1 - i] <= y:
+                x += q - LATE_PAGES[LATE_CTAS - 1 - i]
+                i += 1
+            return G4 + i
         return ((y + 1) * G - 1) // P if y < P else G + (y - P) // CHUNK_PAGES
 
 
-def plan(lengths, nkv: int, grid: int, fused: bool, static_pct: int = STATIC_PCT) -> Plan:
+def plan(lengths, nkv: int, grid: int, fused: bool, static_pct: int = STATIC_PCT,
+         skew: bool = False) -> Plan:
+    """skew: launched to overlap the previous kernel (KOPT_PLAN_OVERLAP_PREV)."""
     npages = [max(1, -(-((L - 1) if fused else L) // PAGE)) for L in lengths]
     pstart = [0]
     for n in npages:
@@ -71,7 +97,8 @@ def plan(lengths, nkv: int, grid: int, fused: bool, static_pct: int = STATIC_PCT
     P = T * static_pct // 100
     if P < grid:
         P = 0
-    return Plan(npages, pstart, T, P, grid + -(-(T - P) // CHUNK_PAGES), grid)
+    late = skew and grid > 2 * LATE_CTAS and P // grid >= 4 * LATE_PAGES[0]
+    return Plan(npages, pstart, T, P, grid + -(-(T - P) // CHUNK_PAGES), grid, late)
 
 
 def units_of_chunk(pl: Plan, lengths, nkv: int, fused: bool, k: int) -> list[Unit]:
@@ -93,8 +120,9 @@ def units_of_chunk(pl: Plan, lengths, nkv: int, fused: bool, k: int) -> list[Uni
     return out
 
 
-def all_units(lengths, nkv: int, grid: int, fused: bool, static_pct: int = STATIC_PCT) -> list[Unit]:
-    pl = plan(lengths, nkv, grid, fused, static_pct)
+def all_units(lengths, nkv: int, grid: int, fused: bool, static_pct: int = STATIC_PCT,
+              skew: bool = False) -> list[Unit]:
+    pl = plan(lengths, nkv, grid, fused, static_pct, skew)
     return [u for k in range(pl.total_chunks) for u in units_of_chunk(pl, lengths, nkv, fused, k)]
 
 

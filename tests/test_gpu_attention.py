@@ -298,7 +298,9 @@ def test_rejects_cpu_tensors_and_bad_shapes():
 def test_overlapped_launches_match_plain():
     """KOPT_PLAN_OVERLAP_PREV: back-to-back calls over different layers (each call's split and
     first page copies issued while the previous call finishes) and the same calls behind a QKV
-    GEMM inside a CUDA graph give bit-identical outputs to plain launches."""
+    GEMM inside a CUDA graph. The flag also shortens the last CTAs' pieces, so the split differs
+    from a plain launch: outputs match plain launches within the bf16 tolerance and are
+    bit-identical from one overlapped call to the next, eager or graphed."""
     from kernel_optim_b200.workloads import build_case
     layers = 4
     case = build_case("c2", DEV, seed=3, paged=True, layers=layers)
@@ -317,12 +319,18 @@ def test_overlapped_launches_match_plain():
         plain(qkv, *args, layer, t["pos"], out)
         ref.append(out)
     outs = [torch.empty_like(ref[0]) for _ in range(layers)]
+    first = None
     for rep in range(3):
         for layer in range(layers):
             over(qkv, *args, layer, t["pos"], outs[layer])
         torch.cuda.synchronize()
+        if first is None:
+            first = [o.clone() for o in outs]
+            for layer in range(layers):
+                d = (first[layer].float() - ref[layer].float()).abs()
+                assert float(d.max()) <= MAX_ABS and float(d.mean()) <= MEAN_ABS, f"layer {layer}"
         for layer in range(layers):
-            assert torch.equal(outs[layer], ref[layer]), f"rep {rep} layer {layer}"
+            assert torch.equal(outs[layer], first[layer]), f"rep {rep} layer {layer}"
     # GEMM -> attention pairs in a graph: the attention overlaps the GEMM that produces its qkv
     qkv_g = torch.empty_like(qkv)
     for o in outs:
@@ -341,5 +349,5 @@ def test_overlapped_launches_match_plain():
         graph.replay()
         torch.cuda.synchronize()
         for layer in range(layers):
-            assert torch.equal(outs[layer], ref[layer]), f"graph layer {layer}"
+            assert torch.equal(outs[layer], first[layer]), f"graph layer {layer}"
     assert plain.read_error() == 0 and over.read_error() == 0

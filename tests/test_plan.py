@@ -8,10 +8,10 @@ import pytest
 from kernel_optim_b200.plan import PAGE, all_units, max_units, plan, schedule
 
 
-def check_plan(lengths, nkv, grid, fused, max_len=None, static_pct=100):
-    us = all_units(lengths, nkv, grid, fused, static_pct)
+def check_plan(lengths, nkv, grid, fused, max_len=None, static_pct=100, skew=False):
+    us = all_units(lengths, nkv, grid, fused, static_pct, skew)
     B = len(lengths)
-    pl = plan(lengths, nkv, grid, fused, static_pct)
+    pl = plan(lengths, nkv, grid, fused, static_pct, skew)
     limit = max_units(B, nkv, max_len or max(lengths), grid)
     slots = [u.slot for u in us]
     assert len(slots) == len(set(slots)), "two units share a workspace slot"
@@ -57,7 +57,8 @@ def test_random_lengths_grids_and_heads():
         nkv = rng.choice([1, 2, 4, 8])
         grid = rng.choice([1, 2, 7, 37, 148, 296, 1000])
         lengths = [rng.choice([1, 2, 15, 16, 17, 512, 513, rng.randint(1, 20000)]) for _ in range(B)]
-        check_plan(lengths, nkv, grid, rng.random() < 0.5, static_pct=rng.choice([0, 60, 90, 100]))
+        check_plan(lengths, nkv, grid, rng.random() < 0.5, static_pct=rng.choice([0, 60, 90, 100]),
+                   skew=rng.random() < 0.5)
 
 
 def test_dynamic_claims_take_every_chunk_once():
@@ -68,3 +69,17 @@ def test_dynamic_claims_take_every_chunk_once():
         speeds = [rng.uniform(0.7, 1.3) for _ in range(grid)]
         taken = schedule(n, grid, speeds)
         assert sorted(g for t in taken for g in t) == list(range(n))
+
+
+def test_late_start_allowance():
+    """Overlapped launches on c2: the last 4 pieces are 24, 12, 6 and 6 pages shorter (last CTA
+    shortest), the others share the difference, and the split still covers every key once."""
+    from kernel_optim_b200.plan import LATE_PAGES
+    pl0, _ = check_plan([4097] * 16, 8, 148, True)
+    pl, _ = check_plan([4097] * 16, 8, 148, True, skew=True)
+    assert pl.late and not pl0.late
+    q = pl.static_pages // 148
+    lens = [pl.chunk_range(k)[1] - pl.chunk_range(k)[0] for k in range(148)]
+    assert lens[-4:] == [q - d for d in reversed(LATE_PAGES)]
+    assert min(lens[:-4]) >= q
+    check_plan([5, 130, 77], 8, 148, True, skew=True)      # too short: no allowance
