@@ -60,6 +60,9 @@ def parse_args():
     ap.add_argument("--no-overlap", action="store_true",
                     help="launch without programmatic dependent launch (each call waits for the "
                          "previous kernel before it starts)")
+    ap.add_argument("--no-gemv", action="store_true",
+                    help="c5: cuBLAS GEMMs + separate SwiGLU / residual kernels instead of the "
+                         "skinny-GEMM projections with fused epilogues")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--soak-ms", type=float, default=600.0,
@@ -506,7 +509,7 @@ def run_engine(args):
     model = random_model(QWEN3_4B["layers"], QWEN3_4B["hidden"], QWEN3_4B["intermediate"],
                          QWEN3_4B["vocab"], seed=0, device=dev)
     eng = Engine.from_model(model, dev, group=dist.group.WORLD if dist is not None else None,
-                            overlap=not args.no_overlap)
+                            overlap=not args.no_overlap, gemv=not args.no_gemv)
     g = torch.Generator().manual_seed(5)
     prompts = torch.randint(0, QWEN3_4B["vocab"], (B, S), generator=g).tolist()
     for _ in range(max(1, args.warmup)):
@@ -543,6 +546,7 @@ def run_engine(args):
         "data": "synthetic: random-init Qwen3-4B (std 0.02, seed 0), uniform random prompt ids",
         "config": {"workload": "c5 engine generate", "B": B, "prompt": S, "new_tokens": N,
                    "overlap_prev": not args.no_overlap,
+                   "projections": "cuBLAS" if eng.gemv is None else "kopt_gemv (fused epilogues)",
                    "parallelism": (f"kv-head shard x{world}, all-gather fused into the attention "
                                    "kernel (NVLink stores)" if world > 1 else "single GPU")},
         "decode_tokens_s": round(B / (step_ms * 1e-3), 1), "decode_step_ms": round(step_ms, 4),

@@ -128,6 +128,9 @@ KOPT_API int kopt_decode_attn(const kopt_plan* plan, const void* q, const kopt_k
 /* ---- decode-step epilogues (the ops around the projections of a layer) -------------------- */
 /* res <- bf16(res + delta) when delta is not NULL; out = bf16(w * bf16(res * rsqrt(mean(res^2)
  * + eps))) per row, fp32 arithmetic. res, delta, out: [M, N] bf16, w: [N]; N a multiple of 8.
+ * Launched with programmatic dependent launch: the kernel waits for its predecessor on the stream
+ * before touching memory, so ordering is the plain stream order, while the next kernel (a
+ * projection launched with KOPT_GEMV_OVERLAP_PREV) may start streaming its weights meanwhile.
  * Replaces add_rms_norm(res, delta, weight, out, eps) (engine/kernels/fused.py:39-46). */
 KOPT_API int kopt_add_rms_norm(void* res, const void* delta, const void* weight, void* out, int M,
                                int N, float eps, void* stream);
@@ -216,6 +219,50 @@ KOPT_API int kopt_decode_attn_fused_noalloc(const kopt_plan* plan, const void* q
                                             const kopt_kv_cache* cache, const int32_t* pos,
                                             void* out, void* q_out, float scale, float eps,
                                             int* dev_err, void* stream);
+
+/* ---- decode-step projections (skinny GEMM) ------------------------------------------------ *
+ * y[M, N] = x[M, K] . W[N, K]^T for the rows of a decode batch (M <= 64), bf16 x and W, fp32 sums,
+ * each weight read once for all rows. Replaces Gemv (engine/kernels/gemv.py:109-150) and the
+ * epilogues of its kernel (gemv.py:29-106); the NORM prologue stays a row kernel
+ * (kopt_add_rms_norm), which normalises x once instead of once per weight tile. */
+#define KOPT_GEMV_F32 0     /* y: float [M, N], the fp32 sums */
+#define KOPT_GEMV_BF16 1    /* y: bf16 [M, N] = bf16(sum) */
+#define KOPT_GEMV_RESID 2   /* y: the residual h, bf16 [M, N], updated in place: h = bf16(h + bf16(sum)) */
+#define KOPT_GEMV_SWIGLU 3  /* W: [gate; up] rows, [2N, K]; y: bf16 [M, N] =
+                               bf16(bf16(silu(bf16(gate sum))) * bf16(up sum)) */
+#define KOPT_GEMV_ARGMAX 4  /* y: int64 [M], per row the index of the largest bf16(sum), the
+                               smallest index among equal values: greedy decoding over the LM
+                               head (engine/engine.py:263 logits, then argmax) without writing
+                               the [M, N] logits */
+typedef struct kopt_gemv_plan {
+  int32_t device;
+  int32_t M, N, K;
+  int32_t epi;               /* KOPT_GEMV_* */
+  int32_t splits;            /* CTAs sharing the K range of one weight tile; their fp32 partials
+                                are added in split order, so results never depend on timing */
+  int32_t tiles;             /* weight tiles: N / 64 (SWIGLU: N / 32 gate rows with their up rows) */
+  int32_t grid;              /* tiles x splits */
+  int32_t ctas_per_sm;       /* resident CTAs per SM reported by the occupancy query */
+  int32_t flags;             /* KOPT_GEMV_* bits below: 0 from kopt_gemv_plan_make */
+  int64_t ws_bytes;          /* workspace bytes: error word, split counters, partials (zeroed once) */
+} kopt_gemv_plan;
+
+/* plan->flags bit: launch with programmatic dependent launch. The CTAs start while the kernel
+ * before them on the stream drains and stream their first weight tiles before waiting for it;
+ * x, y (h) and the workspace are touched only after the wait, so any predecessor is safe. */
+#define KOPT_GEMV_OVERLAP_PREV 1
+
+/* Plan a projection of M rows (1 .. 64), N outputs (a multiple of 64; of 32 for SWIGLU) and K
+ * inputs (a multiple of 8). splits = 0 picks the K split from the SM count; a positive value
+ * fixes it (clamped to the number of 64-wide K chunks). */
+KOPT_API int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int splits,
+                                 kopt_gemv_plan* plan);
+/* y = epilogue(x . W^T) on `stream`. x: [M, K] bf16 row-major; W: [N, K] (SWIGLU [2N, K]) bf16
+ * row-major; all 16-byte aligned; ws: plan->ws_bytes, 256-byte aligned, zero before first use. */
+KOPT_API int kopt_gemv(const kopt_gemv_plan* plan, const void* x, const void* w, void* y, void* ws,
+                       void* stream);
+/* Copy the workspace error word (KOPT_DEV_ERR_TIMEOUT) to *err_out and clear it. Synchronises. */
+KOPT_API int kopt_gemv_read_error(const kopt_gemv_plan* plan, void* ws, int* err_out, void* stream);
 
 /* Human-readable text for a KOPT_* status. */
 KOPT_API const char* kopt_strerror(int status);

@@ -45,7 +45,13 @@ EXPORTED = (
     "kopt_ipc_close",
     "kopt_add_rms_norm",
     "kopt_silu_mul",
+    "kopt_gemv_plan_make",
+    "kopt_gemv",
+    "kopt_gemv_read_error",
 )
+
+GEMV_F32, GEMV_BF16, GEMV_RESID, GEMV_SWIGLU, GEMV_ARGMAX = 0, 1, 2, 3, 4
+GEMV_OVERLAP_PREV = 1
 
 IPC_HANDLE_BYTES = 64
 MAX_RANKS = 8
@@ -104,6 +110,24 @@ class Gather(ctypes.Structure):
     ]
 
 
+class GemvPlan(ctypes.Structure):
+    """Mirror of struct kopt_gemv_plan."""
+
+    _fields_ = [
+        ("device", ctypes.c_int32),
+        ("M", ctypes.c_int32),
+        ("N", ctypes.c_int32),
+        ("K", ctypes.c_int32),
+        ("epi", ctypes.c_int32),
+        ("splits", ctypes.c_int32),
+        ("tiles", ctypes.c_int32),
+        ("grid", ctypes.c_int32),
+        ("ctas_per_sm", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("ws_bytes", ctypes.c_int64),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -134,6 +158,10 @@ _SIGS = {
     "kopt_ipc_close": (_i32, [_i32, _vp]),
     "kopt_add_rms_norm": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _f32, _vp]),
     "kopt_silu_mul": (_i32, [_vp, _vp, _i32, _i32, _vp]),
+    "kopt_gemv_plan_make": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(GemvPlan)]),
+    "kopt_gemv": (_i32, [ctypes.POINTER(GemvPlan), _vp, _vp, _vp, _vp, _vp]),
+    "kopt_gemv_read_error": (_i32, [ctypes.POINTER(GemvPlan), _vp, ctypes.POINTER(ctypes.c_int),
+                                    _vp]),
 }
 
 

@@ -1485,11 +1485,15 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
 // rounded to bf16 where the reference rounds.
 
 // res <- bf16(res + delta) (if delta); out = bf16(w * bf16(res * rsqrt(mean(res^2) + eps))).
-// One CTA per row; a thread holds 8-element vectors.
+// One CTA per row; a thread holds 8-element vectors. Launched with programmatic dependent launch:
+// it waits for the kernel before it before touching memory, then lets the next kernel's CTAs
+// start (a projection streams its weights while the rows are normalised).
 __global__ void add_rms_norm_kernel(bf16* __restrict__ res, const bf16* __restrict__ delta,
                                     const bf16* __restrict__ w, bf16* __restrict__ out, int n,
                                     float eps) {
   __shared__ float part[32];
+  griddep_wait();
+  griddep_launch_dependents();
   const long long row = blockIdx.x;
   const int nv = n / 8;
   bf16* x = res + row * n;
@@ -1573,6 +1577,326 @@ __global__ void silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ 
     py[e] = pack_bf16(__fmul_rn(s0, fu.x), __fmul_rn(s1, fu.y));
   }
   *reinterpret_cast<uint4*>(out + m * I + v * 8) = y;
+}
+
+// ============================================================= decode-step skinny GEMM (GEMV)
+// y[M, N] = x[M, K] . W[N, K]^T for M <= 64 rows (the decode batch), fp32 accumulation, with the
+// reference's epilogues (gemv.py:1-20, 29-106): F32 (fp32 store), BF16 (rounded store), RESID
+// (h <- bf16(h + bf16(acc)), in place) and SWIGLU (W = [gate; up] of [2N, K], out =
+// bf16(bf16(silu(bf16 g)) * bf16 u)), plus ARGMAX for the LM head: the index of each row's largest
+// bf16-rounded logit, the first one on ties, as argmax over the reference's bf16 logits
+// (engine.py:263 and the greedy pick after it) without writing the logits. Only the fp32
+// accumulation order differs from cuBLAS.
+//
+// One CTA owns a 64-column tile of W rows (SWIGLU: 32 gate rows + the matching 32 up rows) and a
+// contiguous share of the K chunks (split-K when the tiles alone cannot fill the GPU). A producer
+// warp streams 64 x 64 weight tiles and the matching x tile by TMA through a 4-deep ring; 4
+// consumer warps take 16 W rows each on mma.sync m16n8k16 over all 16 MT rows of x. The tile's
+// fp32 sums go through shared memory to an epilogue layout (4 threads per row, 16 columns each);
+// with split-K every split writes its partial and the split that arrives last adds them in split
+// order, so results do not depend on which CTA finishes first.
+//
+// Launched with programmatic stream serialization, the producer issues the weight copies of the
+// first ring stages before griddepcontrol.wait: weights never depend on the previous kernel, so
+// they stream while it drains. x, h and the workspace are touched only after the wait.
+constexpr int kGW = 4;                   // consumer warps
+constexpr int kGThreads = (kGW + 1) * 32;
+constexpr int kGStages = 4;
+constexpr int kGBN = 64;                 // W rows per tile
+constexpr int kGBK = 64;                 // k per stage
+constexpr int kGLd = kGBN + 8;           // fp32 tile row stride in shared memory (floats)
+constexpr int GEMV_F32 = KOPT_GEMV_F32, GEMV_BF16 = KOPT_GEMV_BF16, GEMV_RESID = KOPT_GEMV_RESID,
+              GEMV_SWIGLU = KOPT_GEMV_SWIGLU, GEMV_ARGMAX = KOPT_GEMV_ARGMAX;
+
+struct GemvParams {
+  CUtensorMap tmw;                       // W [rows, K]: box 64 k x 64 rows (SWIGLU: 32 rows)
+  CUtensorMap tmx;                       // x [M, K]: box 64 k x 16 MT rows (rows >= M read as 0)
+  void* y;                               // F32: float [M, N]; BF16, SWIGLU: bf16 [M, N];
+                                         // RESID: the residual h [M, N], updated in place
+  float* part;                           // split partials [splits][M][tiles * 64]
+  int* cnt;                              // arrivals per tile, then tiles done (zero between launches)
+  unsigned long long* keys;              // ARGMAX: per row, the best (bf16 logit, -index) so far
+  int* err;
+  int M, N, K, splits, nchunks, tiles;
+};
+
+template <int MT>
+struct __align__(1024) GSmem {
+  bf16 w[kGStages][kGBN * kGBK];         // 8 KB per stage; reused as the fp32 tile at the end
+  bf16 x[kGStages][16 * MT * kGBK];
+  unsigned long long full[kGStages], empty[kGStages];
+  int last;
+  int last_all;
+  volatile int abort;
+};
+template <int MT>
+constexpr size_t gsmem_bytes() { return sizeof(GSmem<MT>) + 1024; }
+static_assert(sizeof(float) * 64 * kGLd <= sizeof(bf16) * kGStages * kGBN * kGBK,
+              "the fp32 tile does not fit in the weight ring");
+
+__device__ __forceinline__ float silu_bf16(float g) {   // bf16(g / (1 + exp(-g))), g a bf16 value
+  return bf16r(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+}
+
+template <int MT, int EPI>
+__global__ void __launch_bounds__(kGThreads) gemv_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  GSmem<MT>& s = *reinterpret_cast<GSmem<MT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x % p.splits, tile = blockIdx.x / p.splits;
+  const int c0 = static_cast<int>(static_cast<long long>(split) * p.nchunks / p.splits);
+  const int c1 = static_cast<int>(static_cast<long long>(split + 1) * p.nchunks / p.splits);
+  const int nch = c1 - c0;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGStages; ++i) {
+      mbar_init(smem_u32(&s.full[i]), 1);
+      mbar_init(smem_u32(&s.empty[i]), kGW);
+    }
+    s.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  constexpr uint32_t kStageBytes = (kGBN + 16 * MT) * kGBK * 2;
+  if (warp == kGW) {   // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = evict_first_policy();
+      auto load_w = [&](int i) {
+        const int st = i % kGStages, k = (c0 + i) * kGBK;
+        const uint32_t fb = smem_u32(&s.full[st]);
+        if (EPI == GEMV_SWIGLU) {   // gate rows, then the up rows N further on
+          tma_load_2d(smem_u32(&s.w[st][0]), &p.tmw, k, tile * 32, fb, pol);
+          tma_load_2d(smem_u32(&s.w[st][32 * kGBK]), &p.tmw, k, p.N + tile * 32, fb, pol);
+        } else {
+          tma_load_2d(smem_u32(&s.w[st][0]), &p.tmw, k, tile * kGBN, fb, pol);
+        }
+      };
+      auto load_x = [&](int i) {
+        const int st = i % kGStages;
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(&s.x[st][0])),
+            "l"(&p.tmx), "r"((c0 + i) * kGBK), "r"(0), "r"(smem_u32(&s.full[st]))
+            : "memory");
+      };
+      const int pre = nch < kGStages ? nch : kGStages;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(smem_u32(&s.full[i]), kStageBytes);
+        load_w(i);
+      }
+      griddep_wait();
+      for (int i = 0; i < pre; ++i) load_x(i);
+      int issued = pre;
+      for (int i = pre; i < nch; ++i) {
+        const int st = i % kGStages;
+        if (!mbar_wait(smem_u32(&s.empty[st]), ((i / kGStages) - 1) & 1, s, p.err, true)) break;
+        mbar_arrive_expect_tx(smem_u32(&s.full[st]), kStageBytes);
+        load_w(i);
+        load_x(i);
+        issued = i + 1;
+      }
+      // every copy issued has landed before the CTA may exit (bounded)
+      for (int i = issued > kGStages ? issued - kGStages : 0; i < issued; ++i)
+        mbar_wait(smem_u32(&s.full[i % kGStages]), (i / kGStages) & 1, s, p.err, false);
+    } else {
+      griddep_wait();
+    }
+    griddep_launch_dependents();
+    return;
+  }
+  // ---------------------------------------------------------------------------------- consumers
+  griddep_wait();
+  float acc[MT][2][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
+  {
+    const int mi = lane >> 3, ri = lane & 7;
+    const int wrow = 16 * warp + 8 * (mi >> 1) + ri;   // this lane's W row for ldmatrix
+    for (int i = 0; i < nch; ++i) {
+      const int st = i % kGStages;
+      mbar_wait(smem_u32(&s.full[st]), (i / kGStages) & 1, s, p.err, true);
+      const uint32_t wb = smem_u32(&s.w[st][0]) + wrow * 128;
+      const uint32_t xb = smem_u32(&s.x[st][0]);
+#pragma unroll
+      for (int ks = 0; ks < kGBK / 16; ++ks) {
+        uint32_t b00, b01, b10, b11;   // B fragments of the warp's two 8-row groups
+        ldsm_x4(wb + (((2 * ks + (mi & 1)) ^ ri) << 4), b00, b01, b10, b11);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const int r = 16 * mt + (lane & 15);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(xb + r * 128 + (((2 * ks + (lane >> 4)) ^ (r & 7)) << 4), a0, a1, a2, a3);
+          mma16816_full(acc[mt][0], a0, a1, a2, a3, b00, b01);
+          mma16816_full(acc[mt][1], a0, a1, a2, a3, b10, b11);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&s.empty[st]));
+    }
+  }
+  griddep_launch_dependents();
+  // ---- the tile's fp32 sums to shared memory: rows 16 mt + lane / 4 (+ 8), W rows 16 warp +
+  // 8 nt + 2 (lane % 4) + {0, 1}. The ring is idle: every issued copy was consumed above.
+  float* ct = reinterpret_cast<float*>(&s.w[0][0]);
+  named_bar(1, kGW * 32);
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+        *reinterpret_cast<float2*>(ct + (16 * mt + 8 * h + (lane >> 2)) * kGLd + 16 * warp +
+                                   8 * nt + 2 * (lane & 3)) =
+            make_float2(acc[mt][nt][2 * h], acc[mt][nt][2 * h + 1]);
+  named_bar(1, kGW * 32);
+  // ---- epilogue layout: row r0 + tid / 4, two 8-column segments of the 64-row tile
+  const int tid = threadIdx.x, q = tid & 3;
+  const int sa = EPI == GEMV_SWIGLU ? 8 * q : 16 * q;            // gate (or first) segment
+  const int sb = EPI == GEMV_SWIGLU ? 32 + 8 * q : 16 * q + 8;    // up (or second) segment
+  const long long pw = static_cast<long long>(p.tiles) * kGBN;    // partial row width
+  const long long pcol = static_cast<long long>(tile) * kGBN;
+  constexpr int kRows = 16 * MT;
+  if (p.splits > 1) {
+    for (int r0 = 0; r0 < kRows; r0 += 32) {
+      const int m = r0 + (tid >> 2);
+      if (m < kRows && m < p.M) {
+        float* dst = p.part + (static_cast<long long>(split) * p.M + m) * pw + pcol;
+        const float* src = ct + m * kGLd;
+#pragma unroll
+        for (int j = 0; j < 8; j += 4) {
+          __stcg(reinterpret_cast<float4*>(dst + sa + j), *reinterpret_cast<const float4*>(src + sa + j));
+          __stcg(reinterpret_cast<float4*>(dst + sb + j), *reinterpret_cast<const float4*>(src + sb + j));
+        }
+      }
+    }
+    __threadfence();
+    named_bar(1, kGW * 32);
+    if (tid == 0) {
+      s.last = atomicAdd(&p.cnt[tile], 1) == p.splits - 1;
+      if (s.last) __threadfence();   // acquire the other splits' partials
+    }
+    named_bar(1, kGW * 32);
+    if (!s.last) return;
+    if (tid == 0) atomicExch(&p.cnt[tile], 0);
+  }
+  for (int r0 = 0; r0 < kRows; r0 += 32) {
+    const int m = r0 + (tid >> 2);
+    const bool act = m < kRows && m < p.M;
+    if (EPI != GEMV_ARGMAX && !act) continue;   // ARGMAX: every lane takes part in the shuffles
+    float v[16];
+    if (!act) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = -INFINITY;
+    } else if (p.splits > 1) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = 0.f;
+      for (int sp = 0; sp < p.splits; ++sp) {   // fixed order: split 0 first
+        const float* src = p.part + (static_cast<long long>(sp) * p.M + m) * pw + pcol;
+#pragma unroll
+        for (int j = 0; j < 8; j += 4) {
+          const float4 a = __ldcg(reinterpret_cast<const float4*>(src + sa + j));
+          const float4 b = __ldcg(reinterpret_cast<const float4*>(src + sb + j));
+          v[j] += a.x; v[j + 1] += a.y; v[j + 2] += a.z; v[j + 3] += a.w;
+          v[8 + j] += b.x; v[9 + j] += b.y; v[10 + j] += b.z; v[11 + j] += b.w;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[j] = ct[m * kGLd + sa + j];
+        v[8 + j] = ct[m * kGLd + sb + j];
+      }
+    }
+    if (EPI == GEMV_F32) {
+      float* y = static_cast<float*>(p.y) + static_cast<long long>(m) * p.N + pcol;
+#pragma unroll
+      for (int j = 0; j < 8; j += 4) {
+        *reinterpret_cast<float4*>(y + sa + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        *reinterpret_cast<float4*>(y + sb + j) =
+            make_float4(v[8 + j], v[9 + j], v[10 + j], v[11 + j]);
+      }
+    } else if (EPI == GEMV_BF16) {
+      bf16* y = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + pcol;
+      uint4 a, b;
+      uint32_t* pa = reinterpret_cast<uint32_t*>(&a);
+      uint32_t* pb = reinterpret_cast<uint32_t*>(&b);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        pa[e] = pack_bf16(v[2 * e], v[2 * e + 1]);
+        pb[e] = pack_bf16(v[8 + 2 * e], v[9 + 2 * e]);
+      }
+      *reinterpret_cast<uint4*>(y + sa) = a;
+      *reinterpret_cast<uint4*>(y + sb) = b;
+    } else if (EPI == GEMV_RESID) {   // h <- bf16(h + bf16(acc)) (gemv.py:95-97)
+      bf16* h = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + pcol;
+#pragma unroll
+      for (int seg = 0; seg < 2; ++seg) {
+        bf16* hp = h + (seg == 0 ? sa : sb);
+        uint4 hv = *reinterpret_cast<const uint4*>(hp);
+        uint32_t* ph = reinterpret_cast<uint32_t*>(&hv);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = bf2f(ph[e]);
+          ph[e] = pack_bf16(__fadd_rn(f.x, bf16r(v[8 * seg + 2 * e])),
+                            __fadd_rn(f.y, bf16r(v[8 * seg + 2 * e + 1])));
+        }
+        *reinterpret_cast<uint4*>(hp) = hv;
+      }
+    } else if (EPI == GEMV_ARGMAX) {
+      // this thread's 16 columns, then the row's 4 threads, then all tiles through one 64-bit
+      // atomicMax per row: key = (order-preserving bits of the bf16 logit) << 32 | ~index, so
+      // the larger logit wins and, on equal logits, the smaller index
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float l = bf16r(v[j]) + 0.0f;   // -0 -> +0: equal logits compare equal
+        const int col = static_cast<int>(pcol) + (j < 8 ? sa + j : sb + j - 8);
+        if (l > best || (l == best && col < bi)) {
+          best = l;
+          bi = col;
+        }
+      }
+      const uint32_t u = __float_as_uint(best);
+      const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+      unsigned long long key = (static_cast<unsigned long long>(ord) << 32) |
+                               static_cast<uint32_t>(0xffffffffu - static_cast<uint32_t>(bi));
+      key = max(key, __shfl_xor_sync(0xffffffffu, key, 1));
+      key = max(key, __shfl_xor_sync(0xffffffffu, key, 2));
+      if (q == 0 && act) atomicMax(p.keys + m, key);
+    } else {   // SWIGLU: output columns 32 tile + 8 q .. + 8 (gemv.py:101-105)
+      bf16* y = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + tile * 32 + 8 * q;
+      uint4 o;
+      uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float s0 = silu_bf16(bf16r(v[2 * e])), s1 = silu_bf16(bf16r(v[2 * e + 1]));
+        po[e] = pack_bf16(__fmul_rn(s0, bf16r(v[8 + 2 * e])), __fmul_rn(s1, bf16r(v[9 + 2 * e])));
+      }
+      *reinterpret_cast<uint4*>(y) = o;
+    }
+  }
+  if (EPI == GEMV_ARGMAX) {   // the tile that finishes last turns the keys into token ids
+    __threadfence();
+    named_bar(1, kGW * 32);
+    if (tid == 0) {
+      s.last_all = atomicAdd(&p.cnt[p.tiles], 1) == p.tiles - 1;
+      if (s.last_all) __threadfence();
+    }
+    named_bar(1, kGW * 32);
+    if (s.last_all) {
+      if (tid < p.M) {
+        const unsigned long long key = atomicExch(p.keys + tid, 0ull);   // read and re-arm
+        static_cast<long long*>(p.y)[tid] =
+            static_cast<long long>(0xffffffffu - static_cast<uint32_t>(key & 0xffffffffu));
+      }
+      if (tid == 0) atomicExch(&p.cnt[p.tiles], 0);
+    }
+  }
 }
 
 // ------------------------------------------------------------------------------ host side
@@ -1789,6 +2113,107 @@ int launch_verify(const kopt_plan* plan, Params& p, void* stream) {
                                     : launch_verify_t<PAGED, 2>(plan, p, stream);
 }
 
+
+// ------------------------------------------------------------------------------- GEMV host side
+// Workspace: [0, 256) the error word; one arrival counter per tile and one for tiles done; the
+// ARGMAX keys of up to 64 rows; then the split partials.
+struct GemvWs { int64_t cnt, keys, part, total; };
+GemvWs gemv_ws_layout(int M, int tiles, int splits) {
+  GemvWs w;
+  w.cnt = kHeaderBytes;
+  w.keys = w.cnt + (static_cast<int64_t>(tiles + 1) * 4 + 255) / 256 * 256;
+  w.part = w.keys + 64 * 8;
+  w.total = w.part + (splits > 1 ? static_cast<int64_t>(splits) * M * tiles * kGBN * 4 : 0);
+  return w;
+}
+inline int gemv_mt(int M) { return M <= 16 ? 1 : M <= 32 ? 2 : 4; }
+
+template <int MT, int EPI>
+int gemv_occupancy(int device, int* blocks_per_sm) {
+  static int configured[64] = {0};
+  if (device < 0 || device >= 64) return KOPT_ERR_ARG;
+  auto kern = gemv_kernel<MT, EPI>;
+  if (!configured[device]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(gsmem_bytes<MT>())) != cudaSuccess)
+      return KOPT_ERR_CUDA;
+    configured[device] = 1;
+  }
+  if (blocks_per_sm &&
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kern, kGThreads,
+                                                    gsmem_bytes<MT>()) != cudaSuccess)
+    return KOPT_ERR_CUDA;
+  return KOPT_OK;
+}
+template <int MT>
+int gemv_occupancy_epi(int device, int epi, int* blocks_per_sm) {
+  switch (epi) {
+    case GEMV_F32: return gemv_occupancy<MT, GEMV_F32>(device, blocks_per_sm);
+    case GEMV_BF16: return gemv_occupancy<MT, GEMV_BF16>(device, blocks_per_sm);
+    case GEMV_RESID: return gemv_occupancy<MT, GEMV_RESID>(device, blocks_per_sm);
+    case GEMV_SWIGLU: return gemv_occupancy<MT, GEMV_SWIGLU>(device, blocks_per_sm);
+    default: return gemv_occupancy<MT, GEMV_ARGMAX>(device, blocks_per_sm);
+  }
+}
+int gemv_configure(int device, int M, int epi, int* blocks_per_sm) {
+  const int mt = gemv_mt(M);
+  return mt == 1 ? gemv_occupancy_epi<1>(device, epi, blocks_per_sm)
+                 : mt == 2 ? gemv_occupancy_epi<2>(device, epi, blocks_per_sm)
+                           : gemv_occupancy_epi<4>(device, epi, blocks_per_sm);
+}
+
+// Splits of K per tile. Per SM the CTAs' chunks stream one after another, so the time goes with
+// ceil(tiles * splits / SMs) * ceil(chunks / splits) weight tiles; each split beyond the first adds
+// its fp32 partial (written once, read once, mostly in L2), counted here at a third of its bytes.
+int gemv_pick_splits(int M, int tiles, int nchunks, int sms) {
+  const int cap = nchunks < 32 ? nchunks : 32;
+  int best = 1;
+  double best_cost = 1e30;
+  for (int sp = 1; sp <= cap; ++sp) {
+    const double per_sm = static_cast<double>((static_cast<long long>(tiles) * sp + sms - 1) / sms);
+    const double chunks = per_sm * ((nchunks + sp - 1) / sp);
+    const double part = sp > 1 ? static_cast<double>(tiles) * sp * M * kGBN * 8 /
+                                     (3.0 * kGBN * kGBK * 2) / sms
+                               : 0.0;
+    if (chunks + part < best_cost * 0.98) {
+      best_cost = chunks + part;
+      best = sp;
+    }
+  }
+  return best;
+}
+
+template <int MT, int EPI>
+int gemv_launch_t(const kopt_gemv_plan* plan, GemvParams& p, void* stream) {
+  int rc = gemv_occupancy<MT, EPI>(plan->device, nullptr);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan->grid);
+  cfg.blockDim = dim3(kGThreads);
+  cfg.dynamicSmemBytes = gsmem_bytes<MT>();
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (plan->flags & KOPT_GEMV_OVERLAP_PREV) ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, gemv_kernel<MT, EPI>, p) != cudaSuccess) {
+    cudaGetLastError();
+    return KOPT_ERR_CUDA;
+  }
+  return KOPT_OK;
+}
+template <int MT>
+int gemv_launch_epi(const kopt_gemv_plan* plan, GemvParams& p, void* stream) {
+  switch (plan->epi) {
+    case GEMV_F32: return gemv_launch_t<MT, GEMV_F32>(plan, p, stream);
+    case GEMV_BF16: return gemv_launch_t<MT, GEMV_BF16>(plan, p, stream);
+    case GEMV_RESID: return gemv_launch_t<MT, GEMV_RESID>(plan, p, stream);
+    case GEMV_SWIGLU: return gemv_launch_t<MT, GEMV_SWIGLU>(plan, p, stream);
+    default: return gemv_launch_t<MT, GEMV_ARGMAX>(plan, p, stream);
+  }
+}
+
 }  // namespace kopt
 
 // =================================================================================== C ABI
@@ -1808,10 +2233,22 @@ int kopt_add_rms_norm(void* res, const void* delta, const void* weight, void* ou
   int threads = (nv + 3) / 4;                         // at most 4 vectors per thread
   threads = threads < 32 ? 32 : (threads + 31) / 32 * 32;
   if (threads > 1024) return KOPT_ERR_ARG;
-  add_rms_norm_kernel<<<M, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<bf16*>(res), static_cast<const bf16*>(delta), static_cast<const bf16*>(weight),
-      static_cast<bf16*>(out), N, eps);
-  return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M);
+  cfg.blockDim = dim3(threads);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, add_rms_norm_kernel, static_cast<bf16*>(res),
+                         static_cast<const bf16*>(delta), static_cast<const bf16*>(weight),
+                         static_cast<bf16*>(out), N, eps) != cudaSuccess) {
+    cudaGetLastError();
+    return KOPT_ERR_CUDA;
+  }
+  return KOPT_OK;
 }
 
 int kopt_silu_mul(const void* gate_up, void* out, int M, int I, void* stream) {
@@ -1823,6 +2260,104 @@ int kopt_silu_mul(const void* gate_up, void* out, int M, int I, void* stream) {
   silu_mul_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const bf16*>(gate_up), static_cast<bf16*>(out), I);
   return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+}
+
+int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int splits,
+                        kopt_gemv_plan* plan) {
+  if (plan == nullptr || M < 1 || M > 64 || K < 8 || K % 8 != 0 || N < 1 || epi < GEMV_F32 ||
+      epi > GEMV_ARGMAX || splits < 0)
+    return KOPT_ERR_ARG;
+  if (N % (epi == GEMV_SWIGLU ? 32 : kGBN) != 0) return KOPT_ERR_ARG;
+  int rc = set_device(device);
+  if (rc) return rc;
+  int occ = 0, sms = 0;
+  rc = gemv_configure(device, M, epi, &occ);
+  if (rc) return rc;
+  if (occ < 1) return KOPT_ERR_CUDA;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+    return KOPT_ERR_CUDA;
+  const int tiles = epi == GEMV_SWIGLU ? N / 32 : N / kGBN;
+  const int nchunks = (K + kGBK - 1) / kGBK;
+  if (splits == 0) splits = gemv_pick_splits(M, tiles, nchunks, sms);
+  if (splits > nchunks) splits = nchunks;
+  if (static_cast<long long>(tiles) * splits > 0x7fffffffLL) return KOPT_ERR_ARG;
+  *plan = kopt_gemv_plan{};
+  plan->device = device;
+  plan->M = M;
+  plan->N = N;
+  plan->K = K;
+  plan->epi = epi;
+  plan->splits = splits;
+  plan->tiles = tiles;
+  plan->grid = tiles * splits;
+  plan->ctas_per_sm = occ;
+  plan->flags = 0;
+  plan->ws_bytes = gemv_ws_layout(M, tiles, splits).total;
+  return KOPT_OK;
+}
+
+int kopt_gemv(const kopt_gemv_plan* plan, const void* x, const void* w, void* y, void* ws,
+              void* stream) {
+  if (plan == nullptr || x == nullptr || w == nullptr || y == nullptr || ws == nullptr)
+    return KOPT_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y)) return KOPT_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return KOPT_ERR_WORKSPACE;
+  int rc = set_device(plan->device);
+  if (rc) return rc;
+  EncodeTiledFn enc = encode_tiled();
+  if (enc == nullptr) return KOPT_ERR_CUDA;
+  const int mt = gemv_mt(plan->M);
+  const bool glu = plan->epi == GEMV_SWIGLU;
+  GemvParams p{};
+  const cuuint32_t elem[2] = {1, 1};
+  const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(plan->K),
+                               static_cast<cuuint64_t>(plan->N) * (glu ? 2 : 1)};
+  const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(plan->K), static_cast<cuuint64_t>(plan->M)};
+  const cuuint64_t stride[1] = {static_cast<cuuint64_t>(plan->K) * 2};
+  const cuuint32_t wbox[2] = {kGBK, glu ? 32u : static_cast<cuuint32_t>(kGBN)};
+  const cuuint32_t xbox[2] = {kGBK, static_cast<cuuint32_t>(16 * mt)};
+  if (enc(&p.tmw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(w), wdims, stride, wbox,
+          elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return KOPT_ERR_ARG;
+  if (enc(&p.tmx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdims, stride, xbox,
+          elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return KOPT_ERR_ARG;
+  const GemvWs lay = gemv_ws_layout(plan->M, plan->tiles, plan->splits);
+  if (lay.total != plan->ws_bytes) return KOPT_ERR_WORKSPACE;
+  char* base = static_cast<char*>(ws);
+  p.y = y;
+  p.err = reinterpret_cast<int*>(base);
+  p.cnt = reinterpret_cast<int*>(base + lay.cnt);
+  p.part = reinterpret_cast<float*>(base + lay.part);
+  p.keys = reinterpret_cast<unsigned long long*>(base + lay.keys);
+  p.M = plan->M;
+  p.N = plan->N;
+  p.K = plan->K;
+  p.splits = plan->splits;
+  p.nchunks = (plan->K + kGBK - 1) / kGBK;
+  p.tiles = plan->tiles;
+  return mt == 1 ? gemv_launch_epi<1>(plan, p, stream)
+                 : mt == 2 ? gemv_launch_epi<2>(plan, p, stream) : gemv_launch_epi<4>(plan, p, stream);
+}
+
+int kopt_gemv_read_error(const kopt_gemv_plan* plan, void* ws, int* err_out, void* stream) {
+  if (plan == nullptr || ws == nullptr || err_out == nullptr) return KOPT_ERR_ARG;
+  int rc = set_device(plan->device);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int host = 0;
+  if (cudaMemcpyAsync(&host, ws, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return KOPT_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return KOPT_ERR_CUDA;
+  *err_out = host;
+  if (host != 0 &&   // a timed-out launch may leave counters and keys behind: clear them too
+      cudaMemsetAsync(ws, 0,
+                      static_cast<size_t>(gemv_ws_layout(plan->M, plan->tiles, plan->splits).part),
+                      st) != cudaSuccess)
+    return KOPT_ERR_CUDA;
+  return KOPT_OK;
 }
 
 const char* kopt_strerror(int status) {

@@ -12,8 +12,9 @@ What changes is the decode step (engine.py:313-341, 388-401): the per-layer ``qk
 ``attn1`` pair becomes one ``PagedDecodeAttention`` launch over a paged KV cache, and the whole step
 is captured once per shape in a CUDA graph and replayed, pipelined one step ahead of the host as in
 engine.py:509-533. Around it the layer runs as engine.py:325-340 does: the residual add and RMSNorm
-in one kernel (``add_rms_norm``), the projections as cuBLAS GEMMs against fused weights (q/k/v; gate
-and up), and SwiGLU in one kernel (``silu_mul``), all in Transformers' cast order. Prefill is the
+in one kernel (``add_rms_norm``), the projections as skinny GEMMs against fused weights (q/k/v; gate
+and up; ``Gemv``, engine.py:259-262) with the residual add and SwiGLU as their epilogues, all in
+Transformers' cast order (batches above 64 rows: cuBLAS GEMMs and ``silu_mul``). Prefill is the
 native Transformers forward with its DynamicCache, whose K/V are copied into the pages (prefill is
 not the optimised path).
 
@@ -32,26 +33,28 @@ from ._lib import KoptError
 from .paged import PAGE, PagedDecodeAttention, PagedKVCache
 from .fused import add_rms_norm, silu_mul
 from .gather import PeerGather, slot_of
+from .gemv import EPI_ARGMAX, EPI_BF16, EPI_RESID, EPI_SWIGLU, Gemv
 from .shard import head_range, shard_qkv_weight
 
 
 class Engine:
-    def __init__(self, model_path: str, device: str = "cuda:0", group=None, overlap: bool = True):
+    def __init__(self, model_path: str, device: str = "cuda:0", group=None, overlap: bool = True,
+                 gemv: bool = True):
         from transformers import AutoModelForCausalLM
         model = AutoModelForCausalLM.from_pretrained(
             model_path, dtype=torch.bfloat16, attn_implementation="sdpa", local_files_only=True)
-        self._init(model.eval().to(device), device, group, overlap)
+        self._init(model.eval().to(device), device, group, overlap, gemv)
 
     @classmethod
     def from_model(cls, model, device: str = "cuda:0", group=None,
-                   overlap: bool = True) -> "Engine":
+                   overlap: bool = True, gemv: bool = True) -> "Engine":
         """Wrap an already loaded Qwen3ForCausalLM (bf16, sdpa) instead of reading a checkpoint."""
         self = cls.__new__(cls)
-        self._init(model.eval().to(device), device, group, overlap)
+        self._init(model.eval().to(device), device, group, overlap, gemv)
         return self
 
     # ------------------------------------------------------------------ construction
-    def _init(self, model, device, group, overlap=True):
+    def _init(self, model, device, group, overlap=True, gemv=True):
         torch.backends.cuda.matmul.allow_tf32 = False
         self.device = torch.device(device)
         if self.device.type != "cuda":
@@ -66,6 +69,7 @@ class Engine:
         self.model = model
         self.group = group
         self.overlap = overlap
+        self.use_gemv = gemv
         self.world = 1 if group is None else torch.distributed.get_world_size(group)
         self.rank = 0 if group is None else torch.distributed.get_rank(group)
         h0, _ = head_range(self.nkv, self.rank, self.world)
@@ -129,6 +133,21 @@ class Engine:
         self.hid = torch.zeros(B, H, dtype=bf, device=dev)       # residual stream
         self.normed = torch.zeros(B, H, dtype=bf, device=dev)
         self.act = torch.zeros(B, self.inter, dtype=bf, device=dev)
+        self.gemv = None
+        if self.use_gemv and B <= 64:   # the skinny-GEMM kernel serves up to 64 rows
+            nqkv = self.layers[0]["qkv"].shape[0]
+            ov = self.overlap
+            self.qkv = torch.zeros(B, nqkv, dtype=bf, device=dev)
+            self.gemv = dict(
+                qkv=Gemv(B, nqkv, H, EPI_BF16, device=dev, overlap_prev=ov),
+                o=Gemv(B, H, self.nq * self.d, EPI_RESID, device=dev, overlap_prev=ov),
+                gu=Gemv(B, self.inter, H, EPI_SWIGLU, device=dev, overlap_prev=ov),
+                down=Gemv(B, H, self.inter, EPI_RESID, device=dev, overlap_prev=ov),
+            )
+            lm_w = self.model.lm_head.weight
+            if lm_w.shape[0] % 64 == 0 and lm_w.is_contiguous():
+                # LM head + greedy pick in one kernel: token ids, no logits in HBM
+                self.gemv["lm"] = Gemv(B, lm_w.shape[0], H, EPI_ARGMAX, device=dev, overlap_prev=ov)
         if self.pg is not None:
             self.pg.close()
             self.pg = None
@@ -168,18 +187,35 @@ class Engine:
 
     def _step(self):
         """One decode step at positions pos[b]; argmax feeds ids, positions advance. The layer
-        loop of engine.py:325-340: every residual add is fused into the RMSNorm that follows it."""
+        loop of engine.py:325-340. With the skinny-GEMM kernels (B <= 64) the residual adds and
+        SwiGLU are the projections' epilogues (gemv.py:86-105), as in the reference's decode
+        step; otherwise cuBLAS GEMMs with the residual add fused into the next RMSNorm."""
         h, n = self.hid, self.normed
         torch.index_select(self.embed, 0, self.ids, out=h)
-        delta = None
-        for i, lw in enumerate(self.layers):
-            add_rms_norm(h, delta, lw["w_in"], n, self.eps)
-            qkv = torch.mm(n, lw["qkv"].t())
-            o = torch.mm(self._attention(i, lw, qkv), lw["o"].t())
-            add_rms_norm(h, o, lw["w_post"], n, self.eps)
-            silu_mul(torch.mm(n, lw["gu"].t()), self.act)
-            delta = torch.mm(self.act, lw["down"].t())
-        add_rms_norm(h, delta, self.final_norm, n, self.eps)
+        gv = self.gemv
+        if gv is not None:
+            for i, lw in enumerate(self.layers):
+                add_rms_norm(h, None, lw["w_in"], n, self.eps)
+                gv["qkv"](n, lw["qkv"], self.qkv)
+                gv["o"](self._attention(i, lw, self.qkv), lw["o"], h=h)
+                add_rms_norm(h, None, lw["w_post"], n, self.eps)
+                gv["gu"](n, lw["gu"], self.act)
+                gv["down"](self.act, lw["down"], h=h)
+            add_rms_norm(h, None, self.final_norm, n, self.eps)
+            if "lm" in gv:
+                gv["lm"](n, self.model.lm_head.weight, self.ids)
+                self.pos.add_(1)
+                return
+        else:
+            delta = None
+            for i, lw in enumerate(self.layers):
+                add_rms_norm(h, delta, lw["w_in"], n, self.eps)
+                qkv = torch.mm(n, lw["qkv"].t())
+                o = torch.mm(self._attention(i, lw, qkv), lw["o"].t())
+                add_rms_norm(h, o, lw["w_post"], n, self.eps)
+                silu_mul(torch.mm(n, lw["gu"].t()), self.act)
+                delta = torch.mm(self.act, lw["down"].t())
+            add_rms_norm(h, delta, self.final_norm, n, self.eps)
         logits = self.model.lm_head(n)
         torch.argmax(logits, dim=-1, out=self.ids)
         self.pos.add_(1)

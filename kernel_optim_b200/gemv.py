@@ -1,0 +1,163 @@
+"""Decode-step projections (skinny GEMMs) on the sm_100a library.
+
+Same names and call shape as the reference's ``Gemv`` (GodRishUniverse/kernel_optim
+engine/kernels/gemv.py:109-150): ``Gemv(M, N, K, epi, norm, allow_split, eps)`` builds one
+projection of the decode batch, ``__call__(x, w, y, nw, ss, h, ss_out)`` runs it and ``tune(weights,
+deadline)`` picks the launch configuration by GPU time inside a CUDA graph.
+
+y[M, N] = x[M, K] . w[N, K]^T with fp32 sums and one epilogue (gemv.py:86-105):
+
+* ``EPI_F32``    y float [M, N], the sums (no atomics: split partials are added in split order);
+* ``EPI_BF16``   y bf16 [M, N] = bf16(sum);
+* ``EPI_RESID``  h bf16 [M, N] updated in place: h = bf16(h + bf16(sum));
+* ``EPI_SWIGLU`` w = [gate; up] of [2N, K]; y bf16 [M, N] = bf16(bf16(silu(bf16 g)) * bf16 u);
+* ``EPI_ARGMAX`` y int64 [M]: per row the index of the largest bf16(sum), the first one on ties —
+  the LM head and greedy pick of the reference's decode step (engine.py:263 logits, then argmax)
+  in one kernel that never writes the logits.
+
+``norm=True`` normalises x first, bf16(nw * bf16(x * rstd)) (gemv.py:66-79), with a row kernel that
+writes the normalised rows once: re-normalising x inside every weight tile would repeat the work
+once per tile (96 to 600 times for Qwen3-4B's projections). The row sums of squares are recomputed
+from x there, so ``ss`` and ``ss_out`` (the reference's hand-off of those sums between kernels) are
+neither read nor written. The kernel splits K for every epilogue, not only EPI_F32, so
+``allow_split`` is accepted for the signature and does not restrict the split.
+
+Launches go to the current torch stream of the tensors' device; a missing library raises KoptError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import time
+
+import torch
+
+from . import _lib
+from ._lib import GemvPlan, KoptError, check
+from .fused import _ptr, _require_cuda, _stream, add_rms_norm
+
+EPI_F32, EPI_BF16, EPI_RESID, EPI_SWIGLU, EPI_ARGMAX = (
+    _lib.GEMV_F32, _lib.GEMV_BF16, _lib.GEMV_RESID, _lib.GEMV_SWIGLU, _lib.GEMV_ARGMAX)
+
+
+class Gemv:
+    """One fused projection of M rows; owns its workspace, so calls allocate nothing and can be
+    captured in a CUDA graph. ``splits`` = 0 lets the library pick the K split from the SM count;
+    ``overlap_prev`` launches with programmatic dependent launch (weight tiles stream while the
+    kernel before it on the stream drains)."""
+
+    def __init__(self, M, N, K, epi, norm=False, allow_split=False, eps=1e-6, device=None,
+                 splits=0, overlap_prev=False):
+        self.M, self.N, self.K, self.epi, self.norm, self.eps = M, N, K, epi, norm, eps
+        self.allow_split = allow_split
+        dev = torch.device(device) if device is not None else torch.device("cuda")
+        self.device = dev if dev.index is not None else torch.device("cuda", torch.cuda.current_device())
+        self.overlap_prev = overlap_prev
+        self._xn = torch.empty(M, K, dtype=torch.bfloat16, device=self.device) if norm else None
+        self._plans: dict[int, tuple[GemvPlan, torch.Tensor]] = {}
+        self.cfg = self._plan(splits).splits
+
+    def _plan(self, splits: int) -> GemvPlan:
+        if splits in self._plans:
+            return self._plans[splits][0]
+        plan = GemvPlan()
+        check(_lib.lib().kopt_gemv_plan_make(self.device.index, self.M, self.N, self.K, self.epi,
+                                             splits, ctypes.byref(plan)), "kopt_gemv_plan_make")
+        plan.flags = _lib.GEMV_OVERLAP_PREV if self.overlap_prev else 0
+        ws = torch.zeros(plan.ws_bytes, dtype=torch.uint8, device=self.device)
+        self._plans[splits] = (plan, ws)
+        self._plans[plan.splits] = (plan, ws)
+        return plan
+
+    @property
+    def splits(self) -> int:
+        return self.cfg
+
+    def __call__(self, x, w, y=None, nw=None, ss=None, h=None, ss_out=None, cfg=None):
+        key = self.cfg if cfg is None else cfg
+        plan = self._plan(key)
+        ws = self._plans[key][1]
+        M, N, K = self.M, self.N, self.K
+        _require_cuda(x, "x")
+        _require_cuda(w, "w")
+        rows = 2 * N if self.epi == EPI_SWIGLU else N
+        if x.shape != (M, K) or w.shape != (rows, K) or not x.is_contiguous() or not w.is_contiguous():
+            raise KoptError(f"Gemv: x must be [{M}, {K}] and w [{rows}, {K}], contiguous")
+        if self.epi == EPI_RESID:
+            out = h
+            if out is None:
+                raise KoptError("Gemv(EPI_RESID) needs h")
+        else:
+            out = y
+            if out is None:
+                raise KoptError("Gemv needs y")
+        if self.epi == EPI_ARGMAX:
+            _require_cuda(out, "y", torch.int64)
+            if out.shape != (M,) or not out.is_contiguous():
+                raise KoptError(f"Gemv(EPI_ARGMAX): y must be int64 [{M}]")
+        else:
+            _require_cuda(out, "y", torch.float32 if self.epi == EPI_F32 else torch.bfloat16)
+            if out.shape != (M, N) or not out.is_contiguous():
+                raise KoptError(f"Gemv: output must be [{M}, {N}] contiguous")
+        if self.norm:
+            if nw is None:
+                raise KoptError("Gemv(norm=True) needs nw")
+            add_rms_norm(x, None, nw, self._xn, self.eps)
+            x = self._xn
+        check(_lib.lib().kopt_gemv(ctypes.byref(plan), _ptr(x), _ptr(w), _ptr(out), _ptr(ws),
+                                   _stream(x.device)), "kopt_gemv")
+
+    def read_error(self) -> int:
+        """KOPT_DEV_ERR_* bits of past calls (synchronises); clears them."""
+        plan, ws = self._plans[self.cfg]
+        err = ctypes.c_int(0)
+        check(_lib.lib().kopt_gemv_read_error(ctypes.byref(plan), _ptr(ws), ctypes.byref(err),
+                                              _stream(self.device)), "kopt_gemv_read_error")
+        return err.value
+
+    def candidates(self) -> list[int]:
+        """K splits worth timing: the library's pick first, then a spread up to the chunk count."""
+        nchunks = (self.K + 63) // 64
+        auto = self._plan(0).splits
+        out = [auto] + [s for s in (1, 2, 3, 4, 6, 8, 11, 16, 24) if s <= nchunks]
+        return list(dict.fromkeys(out))
+
+    def tune(self, weights, deadline):
+        """Pick the K split by GPU time: one call per real layer weight (cold, as in a decode step),
+        captured in a CUDA graph; stops trying new candidates after ``deadline``
+        (time.monotonic()), keeping the best so far. Mirrors gemv.py:152-199."""
+        dev = weights[0].device
+        M, N, K = self.M, self.N, self.K
+        x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+        if self.epi == EPI_ARGMAX:
+            y = torch.zeros(M, device=dev, dtype=torch.int64)
+        else:
+            y = torch.zeros(M, N, device=dev,
+                            dtype=torch.float32 if self.epi == EPI_F32 else torch.bfloat16)
+        nw = torch.ones(K, device=dev, dtype=torch.bfloat16)
+        h = torch.zeros(M, N, device=dev, dtype=torch.bfloat16)
+        best = None
+        for cfg in self.candidates():
+            if time.monotonic() > deadline:
+                break
+            self(x, weights[0], y, nw, None, h, None, cfg=cfg)
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for wt in weights:
+                    self(x, wt, y, nw, None, h, None, cfg=cfg)
+            g.replay()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize(dev)
+            t = a.elapsed_time(b)
+            del g
+            if best is None or t < best[0]:
+                best = (t, cfg)
+        if best is not None:
+            self.cfg = self._plan(best[1]).splits
+            self.us = best[0] / (2 * len(weights)) * 1e3
+        return self.cfg

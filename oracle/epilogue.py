@@ -2,8 +2,9 @@
 imports it).
 
 add_rms_norm follows engine/kernels/fused.py:16-37 (Transformers' Qwen3RMSNorm after the residual
-add of Qwen3DecoderLayer); silu_mul follows fused.py:111-120 (Qwen3MLP's act_fn(gate) * up). All
-arithmetic in fp32, rounded to bf16 where the reference rounds.
+add of Qwen3DecoderLayer); silu_mul follows fused.py:111-120 (Qwen3MLP's act_fn(gate) * up);
+gemv_ref follows the epilogues of engine/kernels/gemv.py:86-105. All arithmetic in fp32, rounded to
+bf16 where the reference rounds.
 """
 
 from __future__ import annotations
@@ -33,3 +34,29 @@ def silu_mul_ref(gu: torch.Tensor) -> torch.Tensor:
     g, u = gu[:, :I].float(), gu[:, I:].float()
     s = bf16r(g / (1.0 + torch.exp(-g)))                   # act_fn(gate) in bf16
     return bf16r(s * u).to(torch.bfloat16)                 # * up, rounded
+
+
+GEMV_F32, GEMV_BF16, GEMV_RESID, GEMV_SWIGLU, GEMV_ARGMAX = 0, 1, 2, 3, 4
+
+
+def gemv_ref(x: torch.Tensor, w: torch.Tensor, epi: int, h: torch.Tensor | None = None) -> torch.Tensor:
+    """x [M, K], w [N, K] ([2N, K] gate|up for SWIGLU), bf16 -> the epilogue's output: fp32 sums
+    (F32), bf16(sum) (BF16), bf16(h + bf16(sum)) (RESID, gemv.py:95-97),
+    bf16(bf16(silu(bf16 g)) * bf16 u) (SWIGLU, gemv.py:101-105), or the int64 index of each row's
+    largest bf16(sum) (ARGMAX: engine.py:263's bf16 logits, then the greedy argmax)."""
+    acc = x.float() @ w.float().t()
+    if epi == GEMV_F32:
+        return acc
+    if epi == GEMV_BF16:
+        return acc.to(torch.bfloat16)
+    if epi == GEMV_RESID:
+        return bf16r(h.float() + bf16r(acc)).to(torch.bfloat16)
+    if epi == GEMV_ARGMAX:   # greedy pick over bf16 logits, first index among equal values
+        logits = bf16r(acc)
+        top = logits.max(dim=1, keepdim=True).values
+        cols = torch.arange(logits.shape[1]).expand_as(logits)
+        return torch.where(logits == top, cols, logits.shape[1]).min(dim=1).values
+    n = acc.shape[1] // 2
+    g, u = bf16r(acc[:, :n]), bf16r(acc[:, n:])
+    s = bf16r(g / (1.0 + torch.exp(-g)))
+    return bf16r(s * u).to(torch.bfloat16)

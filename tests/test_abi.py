@@ -46,6 +46,8 @@ def test_struct_layouts_match_header():
     assert ctypes.sizeof(_lib.Plan) == 56
     # kopt_gather: 8 + 8 pointers, pointer, 2 int32, int64 -> 152 bytes
     assert ctypes.sizeof(_lib.Gather) == 152
+    # kopt_gemv_plan: 10 int32, int64 -> 48 bytes
+    assert ctypes.sizeof(_lib.GemvPlan) == 48
 
 
 @pytest.mark.parametrize("args", [
@@ -76,3 +78,25 @@ def test_launchers_reject_null_arguments(lib):
     assert lib.kopt_workspace_init(None, None, None) == _lib.KOPT_ERR_ARG
     err = ctypes.c_int(0)
     assert lib.kopt_read_error(None, None, ctypes.byref(err), None) == _lib.KOPT_ERR_ARG
+
+
+@pytest.mark.parametrize("args", [
+    (0, 0, 64, 64, 1, 0),       # no rows
+    (0, 65, 64, 64, 1, 0),      # more rows than the kernel's 64
+    (0, 8, 96, 64, 1, 0),       # N not a multiple of the 64-row weight tile
+    (0, 8, 48, 64, 3, 0),       # SWIGLU N not a multiple of 32
+    (0, 8, 64, 60, 1, 0),       # K not a multiple of 8 (TMA row stride)
+    (0, 8, 64, 64, 5, 0),       # unknown epilogue
+    (0, 8, 64, 64, 1, -1),      # negative split
+])
+def test_gemv_plan_rejects_bad_shapes(lib, args):
+    plan = _lib.GemvPlan()
+    assert lib.kopt_gemv_plan_make(*args, ctypes.byref(plan)) == _lib.KOPT_ERR_ARG
+
+
+def test_gemv_rejects_null_arguments(lib):
+    plan = _lib.GemvPlan()
+    assert lib.kopt_gemv(None, None, None, None, None, None) == _lib.KOPT_ERR_ARG
+    assert lib.kopt_gemv(ctypes.byref(plan), None, None, None, None, None) == _lib.KOPT_ERR_ARG
+    err = ctypes.c_int(0)
+    assert lib.kopt_gemv_read_error(None, None, ctypes.byref(err), None) == _lib.KOPT_ERR_ARG

@@ -1,0 +1,210 @@
+"""GPU: the decode-step projections (kopt_gemv through kernel_optim_b200.gemv.Gemv) against the
+fp32 restatement of the reference's epilogues (oracle/epilogue.py gemv_ref, gemv.py:86-105).
+
+The kernel and the oracle add the same fp32 products in different orders, so:
+  F32     every element within 1e-4 absolute of the oracle (outputs are O(1));
+  BF16    equal to the oracle's bf16 rounding, or one bf16 ulp away where the fp32 sum sits on a
+          rounding boundary, in under 1% of the elements;
+  RESID   h + bf16(sum) rounded: at most one ulp of the sum plus one of the result;
+  SWIGLU  a flipped rounding of g or u passes through silu and the product: within 4 bf16 ulps
+          of the oracle value (plus 1e-3 absolute near zero), in under 2% of the elements.
+Repeated calls, CUDA-graph replays and programmatically overlapped launches are bit-identical
+(the split partials are added in split order, whichever CTA finishes last).
+"""
+
+import pytest
+import torch
+
+from kernel_optim_b200 import KoptError
+from kernel_optim_b200.fused import add_rms_norm
+from kernel_optim_b200.gemv import EPI_ARGMAX, EPI_BF16, EPI_F32, EPI_RESID, EPI_SWIGLU, Gemv
+from oracle.epilogue import add_rms_norm_ref, gemv_ref
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def _inputs(M, N, K, epi, seed):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    rows = 2 * N if epi == EPI_SWIGLU else N
+    x = torch.randn(M, K, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(rows, K, generator=g, device=DEV) * (2.0 / K ** 0.5)).to(torch.bfloat16)
+    h = torch.randn(M, N, generator=g, device=DEV).to(torch.bfloat16)
+    return x, w, h
+
+
+def _out(M, N, epi):
+    return torch.zeros(M, N, device=DEV, dtype=torch.float32 if epi == EPI_F32 else torch.bfloat16)
+
+
+def _run(op, x, w, h, epi):
+    y = _out(op.M, op.N, epi)
+    hh = h.clone()
+    op(x, w, y, h=hh)
+    torch.cuda.synchronize()
+    return hh if epi == EPI_RESID else y
+
+
+def _check(got, x, w, h, epi):
+    ref = gemv_ref(x.cpu(), w.cpu(), epi, h.cpu())
+    g, r = got.float().cpu(), ref.float()
+    diff = (g - r).abs()
+    if epi == EPI_F32:
+        assert float(diff.max()) <= 1e-4, f"max diff {float(diff.max())}"
+        return
+    if epi == EPI_BF16:
+        bound, frac = r.abs() * 2.0 ** -7, 0.01
+    elif epi == EPI_RESID:
+        acc = x.cpu().float() @ w.cpu().float().t()
+        bound, frac = (acc.abs() + r.abs()) * 2.0 ** -7, 0.01
+    else:
+        bound, frac = r.abs() * 2.0 ** -5 + 1e-3, 0.02
+    assert bool((diff <= bound + 1e-30).all()), f"max diff {float(diff.max())} (epi {epi})"
+    mism = float((diff > 0).float().mean())
+    assert mism <= frac, f"{mism:.4f} of the elements differ (epi {epi})"
+
+
+# Qwen3-4B decode shapes at batch 32 (qkv, o, gate|up, down) and edge cases: one row, rows not a
+# multiple of 16, 64 rows (4 row tiles), K not a multiple of the 64-wide chunk, a single tile.
+CASES = [
+    (32, 6144, 2560, EPI_BF16),
+    (32, 2560, 4096, EPI_RESID),
+    (32, 9728, 2560, EPI_SWIGLU),
+    (32, 2560, 9728, EPI_RESID),
+    (1, 256, 128, EPI_BF16),
+    (5, 64, 64, EPI_F32),
+    (17, 128, 200, EPI_BF16),
+    (64, 192, 512, EPI_F32),
+    (64, 96, 1024, EPI_SWIGLU),
+    (3, 32, 136, EPI_SWIGLU),
+    (16, 512, 2048, EPI_RESID),
+]
+
+
+@pytest.mark.parametrize("M,N,K,epi", CASES)
+def test_gemv_matches_oracle(M, N, K, epi):
+    x, w, h = _inputs(M, N, K, epi, seed=M * 7 + N + K + epi)
+    op = Gemv(M, N, K, epi, device=DEV)
+    got = _run(op, x, w, h, epi)
+    _check(got, x, w, h, epi)
+    assert op.read_error() == 0
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 64])
+@pytest.mark.parametrize("epi", [EPI_F32, EPI_BF16, EPI_RESID, EPI_SWIGLU])
+def test_every_split_count(splits, epi):
+    M, N, K = 24, 256, 4096
+    x, w, h = _inputs(M, N, K, epi, seed=splits + 10 * epi)
+    op = Gemv(M, N, K, epi, device=DEV, splits=splits)
+    assert op.splits == splits
+    a = _run(op, x, w, h, epi)
+    _check(a, x, w, h, epi)
+    b = _run(op, x, w, h, epi)        # the arrival counters were reset by the first call
+    assert torch.equal(a, b)
+
+
+def test_graph_replay_and_overlap_are_bit_identical():
+    M, N, K = 32, 2560, 9728
+    x, w, h = _inputs(M, N, K, EPI_RESID, seed=5)
+    plain = Gemv(M, N, K, EPI_RESID, device=DEV)
+    want = _run(plain, x, w, h, EPI_RESID)
+    ov = Gemv(M, N, K, EPI_RESID, device=DEV, overlap_prev=True)
+    hh = h.clone()
+    s = torch.cuda.Stream(DEV)
+    with torch.cuda.stream(s):
+        torch.mm(x[:, :2560], x[:, :2560].t())   # a kernel for the launch to overlap
+        ov(x, w, None, h=hh)
+    torch.cuda.synchronize()
+    assert torch.equal(hh, want)
+    # three chained in-place updates in one graph = three eager calls
+    g = torch.cuda.CUDAGraph()
+    hg = h.clone()
+    with torch.cuda.graph(g):
+        for _ in range(3):
+            ov(x, w, None, h=hg)
+    he = h.clone()
+    for _ in range(3):
+        plain(x, w, None, h=he)
+    hg.copy_(h)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(hg, he)
+    del g
+
+
+def test_norm_prologue():
+    M, N, K = 32, 6144, 2560
+    x, w, _ = _inputs(M, N, K, EPI_BF16, seed=9)
+    nw = (1 + 0.1 * torch.randn(K, device=DEV)).to(torch.bfloat16)
+    op = Gemv(M, N, K, EPI_BF16, norm=True, device=DEV)
+    y = _out(M, N, EPI_BF16)
+    op(x, w, y, nw=nw)
+    torch.cuda.synchronize()
+    xn = torch.empty_like(x)
+    add_rms_norm(x, None, nw, xn, 1e-6)
+    _check(y, xn, w, None, EPI_BF16)
+    # and the normalised rows themselves follow the reference's cast order
+    _, want_xn = add_rms_norm_ref(x.cpu(), None, nw.cpu(), 1e-6)
+    assert float((xn.cpu().float() - want_xn.float()).abs().max()) <= float(want_xn.float().abs().max()) * 2 ** -7
+
+
+def test_tune_picks_a_listed_split():
+    M, N, K = 32, 2560, 4096
+    ws = [torch.randn(N, K, device=DEV).to(torch.bfloat16) for _ in range(3)]
+    op = Gemv(M, N, K, EPI_BF16, device=DEV)
+    import time
+    cfg = op.tune(ws, time.monotonic() + 30)
+    assert cfg in op.candidates() and op.us > 0
+    x, _, h = _inputs(M, N, K, EPI_BF16, seed=1)
+    _check(_run(op, x, ws[0], h, EPI_BF16), x, ws[0], h, EPI_BF16)
+
+
+def test_bad_arguments_raise():
+    with pytest.raises(KoptError):
+        Gemv(65, 64, 64, EPI_BF16, device=DEV)
+    with pytest.raises(KoptError):
+        Gemv(4, 100, 64, EPI_BF16, device=DEV)
+    op = Gemv(4, 64, 64, EPI_BF16, device=DEV)
+    x = torch.zeros(4, 64, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(KoptError):
+        op(x, torch.zeros(32, 64, dtype=torch.bfloat16, device=DEV), _out(4, 64, EPI_BF16))
+    with pytest.raises(KoptError):
+        op(x, torch.zeros(64, 64, dtype=torch.bfloat16, device=DEV), _out(4, 64, EPI_F32))
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(32, 151936, 2560, 0), (1, 4096, 256, 0), (7, 640, 1024, 5),
+                                          (64, 1024, 512, 1)])
+def test_argmax_epilogue(M, N, K, splits):
+    """The LM head's greedy pick: the kernel's index must hold the row's largest bf16 logit of the
+    oracle (a flipped rounding can only swap indices whose logits are one bf16 ulp apart), and
+    equal the oracle's first-index pick in nearly every row."""
+    x, w, _ = _inputs(M, N, K, EPI_BF16, seed=N + M)
+    op = Gemv(M, N, K, EPI_ARGMAX, device=DEV, splits=splits)
+    ids = torch.full((M,), -1, dtype=torch.int64, device=DEV)
+    for _ in range(2):                       # the keys are re-armed by the first call
+        op(x, w, ids)
+        torch.cuda.synchronize()
+        want = gemv_ref(x.cpu(), w.cpu(), EPI_ARGMAX)
+        logits = (x.cpu().float() @ w.cpu().float().t()).to(torch.bfloat16).float()
+        got = ids.cpu()
+        assert bool(((got >= 0) & (got < N)).all())
+        top = logits.max(dim=1).values
+        picked = logits.gather(1, got.unsqueeze(1)).squeeze(1)
+        assert bool((top - picked <= top.abs() * 2.0 ** -7 + 1e-30).all())
+        assert float((got == want).float().mean()) >= 0.9
+
+
+def test_argmax_ties_take_the_first_index():
+    M, N, K = 4, 512, 64
+    x = torch.ones(M, K, dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros(N, K, dtype=torch.bfloat16, device=DEV)
+    w[[70, 300, 301, 499]] = 1.0              # equal logits at four columns of different tiles
+    ids = torch.empty(M, dtype=torch.int64, device=DEV)
+    Gemv(M, N, K, EPI_ARGMAX, device=DEV)(x, w, ids)
+    torch.cuda.synchronize()
+    assert ids.tolist() == [70] * M
+    w.zero_()                                  # all logits +0 / -0: column 0
+    w[5, 0] = -0.0
+    Gemv(M, N, K, EPI_ARGMAX, device=DEV)(x, w, ids)
+    torch.cuda.synchronize()
+    assert ids.tolist() == [0] * M

@@ -136,3 +136,44 @@ def test_epilogue_restatement_matches_transformers():
     act = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
     assert torch.equal(silu_mul_ref(gu), act)
     del Qwen3Config
+
+
+def test_gemv_restatement_matches_transformers_layers():
+    """gemv_ref's epilogues against the modules they replace, on CPU in bf16: Qwen3MLP's
+    down(act_fn(gate(x)) * up(x)) with the residual add of Qwen3DecoderLayer, and the LM head's
+    greedy argmax. Only fp32 summation order differs (Transformers' bf16 Linear vs one fp32
+    matmul), so a bf16 rounding may flip in a few elements, by one ulp."""
+    from transformers import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP
+    from oracle.epilogue import GEMV_ARGMAX, GEMV_BF16, GEMV_RESID, GEMV_SWIGLU, gemv_ref
+    g = torch.Generator().manual_seed(6)
+    M, H, I, V = 6, 256, 512, 1000 - 1000 % 64
+    cfg = Qwen3Config(hidden_size=H, intermediate_size=I, hidden_act="silu")
+    mlp = Qwen3MLP(cfg).to(torch.bfloat16)
+    with torch.no_grad():
+        for lin in (mlp.gate_proj, mlp.up_proj, mlp.down_proj):
+            lin.weight.copy_(torch.randn(lin.weight.shape, generator=g) * lin.weight.shape[1] ** -0.5)
+    x = torch.randn(M, H, generator=g).to(torch.bfloat16)
+    h = torch.randn(M, H, generator=g).to(torch.bfloat16)
+    with torch.no_grad():
+        act_want = mlp.act_fn(mlp.gate_proj(x)) * mlp.up_proj(x)
+        h_want = h + mlp.down_proj(act_want)
+    gu = torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight], 0)
+    act = gemv_ref(x, gu.data, GEMV_SWIGLU)
+    h_new = gemv_ref(act_want, mlp.down_proj.weight.data, GEMV_RESID, h)
+
+    def close(a, b, frac):
+        d = (a.float() - b.float()).abs()
+        assert bool((d <= (a.float().abs() + b.float().abs()) * 2.0 ** -7 + 1e-6).all())
+        assert float((d > 0).float().mean()) <= frac
+    close(act, act_want, 0.03)
+    close(h_new, h_want, 0.03)
+    lm = torch.randn(V, H, generator=g).to(torch.bfloat16) * H ** -0.5
+    logits = gemv_ref(x, lm, GEMV_BF16)
+    want = torch.nn.functional.linear(x, lm).argmax(dim=-1)
+    got = gemv_ref(x, lm, GEMV_ARGMAX)
+    assert bool((logits.float().gather(1, got[:, None]) >= logits.float().gather(1, want[:, None]) - 1e-2).all())
+    # ties: the first index among equal bf16 logits, as torch.argmax
+    w = torch.zeros(128, 4, dtype=torch.bfloat16)
+    w[[9, 40, 77]] = 1.0
+    assert gemv_ref(torch.ones(2, 4, dtype=torch.bfloat16), w, GEMV_ARGMAX).tolist() == [9, 9]
