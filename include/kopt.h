@@ -238,13 +238,15 @@ typedef struct kopt_gemv_plan {
   int32_t device;
   int32_t M, N, K;
   int32_t epi;               /* KOPT_GEMV_* */
-  int32_t splits;            /* CTAs sharing the K range of one weight tile; their fp32 partials
-                                are added in split order, so results never depend on timing */
+  int32_t units_per_cta;     /* (weight tile, 64-wide K chunk) units per CTA: each CTA streams one
+                                contiguous run of them, tile-major; a tile whose units fall to
+                                several CTAs is summed from their fp32 partials in CTA order, so
+                                results never depend on timing */
   int32_t tiles;             /* weight tiles: N / 64 (SWIGLU: N / 32 gate rows with their up rows) */
-  int32_t grid;              /* tiles x splits */
+  int32_t grid;              /* CTAs: ceil(tiles * ceil(K / 64) / units_per_cta) */
   int32_t ctas_per_sm;       /* resident CTAs per SM reported by the occupancy query */
   int32_t flags;             /* KOPT_GEMV_* bits below: 0 from kopt_gemv_plan_make */
-  int64_t ws_bytes;          /* workspace bytes: error word, split counters, partials (zeroed once) */
+  int64_t ws_bytes;          /* workspace bytes: error word, counters, partials (zeroed once) */
 } kopt_gemv_plan;
 
 /* plan->flags bit: launch with programmatic dependent launch. The CTAs start while the kernel
@@ -253,9 +255,9 @@ typedef struct kopt_gemv_plan {
 #define KOPT_GEMV_OVERLAP_PREV 1
 
 /* Plan a projection of M rows (1 .. 64), N outputs (a multiple of 64; of 32 for SWIGLU) and K
- * inputs (a multiple of 8). splits = 0 picks the K split from the SM count; a positive value
- * fixes it (clamped to the number of 64-wide K chunks). */
-KOPT_API int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int splits,
+ * inputs (a multiple of 8). target_ctas = 0 launches one resident wave (SM count x resident CTAs
+ * per SM); a positive value asks for that many CTAs instead (at most one per unit). */
+KOPT_API int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int target_ctas,
                                  kopt_gemv_plan* plan);
 /* y = epilogue(x . W^T) on `stream`. x: [M, K] bf16 row-major; W: [N, K] (SWIGLU [2N, K]) bf16
  * row-major; all 16-byte aligned; ws: plan->ws_bytes, 256-byte aligned, zero before first use. */

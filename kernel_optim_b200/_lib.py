@@ -119,7 +119,7 @@ class GemvPlan(ctypes.Structure):
         ("N", ctypes.c_int32),
         ("K", ctypes.c_int32),
         ("epi", ctypes.c_int32),
-        ("splits", ctypes.c_int32),
+        ("units_per_cta", ctypes.c_int32),
         ("tiles", ctypes.c_int32),
         ("grid", ctypes.c_int32),
         ("ctas_per_sm", ctypes.c_int32),

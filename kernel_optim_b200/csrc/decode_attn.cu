@@ -1011,6 +1011,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
       if (issued == consumed) pump();   // this tile's copy must be in flight before waiting
       const int slot = consumed % kStages;
       mbar_wait(smem_u32(&s.full[slot][warp]), (consumed / kStages) & 1, s, p.ws_err, true);
+      __syncwarp();   // lanes leave the bounded spin at different times: reconverge before mma.sync
       page_step(smem_u32(&s.k[slot][warp][0][0]), smem_u32(&s.v[slot][warp][0][0]), ntok, qa,
                 p.scale_log2, st, lane);
       ++consumed;
@@ -1283,6 +1284,7 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
   for (int k = 0; k < mine; ++k) {
     const int slot = k % kVStages;
     mbar_wait(smem_u32(&s.full[slot][warp]), (k / kVStages) & 1, s, p.ws_err, true);
+    __syncwarp();   // reconverge after the per-lane spin before ldmatrix / mma.sync
     const int key0 = (pg0 + warp + k * kVW) * kPage;
     const uint32_t kbase = smem_u32(&s.k[slot][warp][0][0]);
     const uint32_t vbase = smem_u32(&s.v[slot][warp][0][0]);
@@ -1588,51 +1590,61 @@ __global__ void silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ 
 // (engine.py:263 and the greedy pick after it) without writing the logits. Only the fp32
 // accumulation order differs from cuBLAS.
 //
-// One CTA owns a 64-column tile of W rows (SWIGLU: 32 gate rows + the matching 32 up rows) and a
-// contiguous share of the K chunks (split-K when the tiles alone cannot fill the GPU). A producer
-// warp streams 64 x 64 weight tiles and the matching x tile by TMA through a 4-deep ring; 4
-// consumer warps take 16 W rows each on mma.sync m16n8k16 over all 16 MT rows of x. The tile's
-// fp32 sums go through shared memory to an epilogue layout (4 threads per row, 16 columns each);
-// with split-K every split writes its partial and the split that arrives last adds them in split
-// order, so results do not depend on which CTA finishes first.
+// Persistent stream-K: the weight is cut into 64-row tiles (SWIGLU: 32 gate rows + the matching
+// 32 up rows) of 64-wide K chunks; the (tile, chunk) units, tile-major, are dealt to the CTAs in
+// equal contiguous runs, one run per CTA, two CTAs per SM. A producer warp streams each unit's
+// 64 x 64 weight tile and the matching x tile by TMA through a deep ring, across tile boundaries,
+// so HBM never waits on an epilogue; 4 consumer warps take 16 weight rows each on mma.sync
+// m16n8k16 over all 16 MT rows of x. Where a run ends inside a tile, that segment's fp32 partial
+// goes to the workspace and the CTA that arrives last at the tile adds the segments in CTA order
+// (fixed, whichever finishes first) before the epilogue.
 //
 // Launched with programmatic stream serialization, the producer issues the weight copies of the
 // first ring stages before griddepcontrol.wait: weights never depend on the previous kernel, so
 // they stream while it drains. x, h and the workspace are touched only after the wait.
 constexpr int kGW = 4;                   // consumer warps
 constexpr int kGThreads = (kGW + 1) * 32;
-constexpr int kGStages = 4;
 constexpr int kGBN = 64;                 // W rows per tile
-constexpr int kGBK = 64;                 // k per stage
+constexpr int kGBK = 64;                 // k per chunk (one ring stage)
 constexpr int kGLd = kGBN + 8;           // fp32 tile row stride in shared memory (floats)
 constexpr int GEMV_F32 = KOPT_GEMV_F32, GEMV_BF16 = KOPT_GEMV_BF16, GEMV_RESID = KOPT_GEMV_RESID,
               GEMV_SWIGLU = KOPT_GEMV_SWIGLU, GEMV_ARGMAX = KOPT_GEMV_ARGMAX;
+// ring depth: about 100 KB of shared memory per CTA, two CTAs per SM
+template <int MT>
+__host__ __device__ constexpr int gemv_stages() { return MT == 1 ? 10 : MT == 2 ? 8 : 5; }
 
 struct GemvParams {
   CUtensorMap tmw;                       // W [rows, K]: box 64 k x 64 rows (SWIGLU: 32 rows)
   CUtensorMap tmx;                       // x [M, K]: box 64 k x 16 MT rows (rows >= M read as 0)
   void* y;                               // F32: float [M, N]; BF16, SWIGLU: bf16 [M, N];
-                                         // RESID: the residual h [M, N], updated in place
-  float* part;                           // split partials [splits][M][tiles * 64]
+                                         // RESID: the residual h [M, N], updated in place;
+                                         // ARGMAX: int64 [M]
+  float* part;                           // segment partials [2 grid][M][64]: 2c = CTA c's first
+                                         // segment, 2c + 1 = its last
   int* cnt;                              // arrivals per tile, then tiles done (zero between launches)
   unsigned long long* keys;              // ARGMAX: per row, the best (bf16 logit, -index) so far
   int* err;
-  int M, N, K, splits, nchunks, tiles;
+  long long units;                       // tiles x nchunks
+  int M, N, K, nchunks, tiles, per;      // per: units per CTA
 };
 
 template <int MT>
 struct __align__(1024) GSmem {
-  bf16 w[kGStages][kGBN * kGBK];         // 8 KB per stage; reused as the fp32 tile at the end
-  bf16 x[kGStages][16 * MT * kGBK];
-  unsigned long long full[kGStages], empty[kGStages];
+  static constexpr int S = gemv_stages<MT>();
+  bf16 w[S][kGBN * kGBK];                // 8 KB per stage
+  bf16 x[S][16 * MT * kGBK];
+  float ct[16 * MT][kGLd];               // a finished segment's fp32 sums
+  unsigned long long full[S], empty[S];
   int last;
   int last_all;
   volatile int abort;
 };
 template <int MT>
 constexpr size_t gsmem_bytes() { return sizeof(GSmem<MT>) + 1024; }
-static_assert(sizeof(float) * 64 * kGLd <= sizeof(bf16) * kGStages * kGBN * kGBK,
-              "the fp32 tile does not fit in the weight ring");
+static_assert(2 * (gsmem_bytes<1>() + 1024) <= 228 * 1024 &&
+                  2 * (gsmem_bytes<2>() + 1024) <= 228 * 1024 &&
+                  2 * (gsmem_bytes<4>() + 1024) <= 228 * 1024,
+              "two GEMV CTAs no longer fit on an SM");
 
 __device__ __forceinline__ float silu_bf16(float g) {   // bf16(g / (1 + exp(-g))), g a bf16 value
   return bf16r(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
@@ -1640,16 +1652,16 @@ __device__ __forceinline__ float silu_bf16(float g) {   // bf16(g / (1 + exp(-g)
 
 template <int MT, int EPI>
 __global__ void __launch_bounds__(kGThreads) gemv_kernel(const __grid_constant__ GemvParams p) {
+  constexpr int S = gemv_stages<MT>();
   extern __shared__ unsigned char smem_raw[];
   GSmem<MT>& s = *reinterpret_cast<GSmem<MT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int split = blockIdx.x % p.splits, tile = blockIdx.x / p.splits;
-  const int c0 = static_cast<int>(static_cast<long long>(split) * p.nchunks / p.splits);
-  const int c1 = static_cast<int>(static_cast<long long>(split + 1) * p.nchunks / p.splits);
-  const int nch = c1 - c0;
+  const long long u0 = static_cast<long long>(blockIdx.x) * p.per;
+  const long long u1 = min(u0 + p.per, p.units);
+  const int n = static_cast<int>(u1 - u0);   // >= 1: the grid is ceil(units / per)
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kGStages; ++i) {
+    for (int i = 0; i < S; ++i) {
       mbar_init(smem_u32(&s.full[i]), 1);
       mbar_init(smem_u32(&s.empty[i]), kGW);
     }
@@ -1662,7 +1674,10 @@ __global__ void __launch_bounds__(kGThreads) gemv_kernel(const __grid_constant__
     if (lane == 0) {
       const uint64_t pol = evict_first_policy();
       auto load_w = [&](int i) {
-        const int st = i % kGStages, k = (c0 + i) * kGBK;
+        const long long u = u0 + i;
+        const int tile = static_cast<int>(u / p.nchunks);
+        const int k = static_cast<int>(u % p.nchunks) * kGBK;
+        const int st = i % S;
         const uint32_t fb = smem_u32(&s.full[st]);
         if (EPI == GEMV_SWIGLU) {   // gate rows, then the up rows N further on
           tma_load_2d(smem_u32(&s.w[st][0]), &p.tmw, k, tile * 32, fb, pol);
@@ -1672,14 +1687,15 @@ __global__ void __launch_bounds__(kGThreads) gemv_kernel(const __grid_constant__
         }
       };
       auto load_x = [&](int i) {
-        const int st = i % kGStages;
+        const int st = i % S;
+        const int k = static_cast<int>((u0 + i) % p.nchunks) * kGBK;
         asm volatile(
             "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
             " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(&s.x[st][0])),
-            "l"(&p.tmx), "r"((c0 + i) * kGBK), "r"(0), "r"(smem_u32(&s.full[st]))
+            "l"(&p.tmx), "r"(k), "r"(0), "r"(smem_u32(&s.full[st]))
             : "memory");
       };
-      const int pre = nch < kGStages ? nch : kGStages;
+      const int pre = n < S ? n : S;
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(smem_u32(&s.full[i]), kStageBytes);
         load_w(i);
@@ -1687,17 +1703,17 @@ __global__ void __launch_bounds__(kGThreads) gemv_kernel(const __grid_constant__
       griddep_wait();
       for (int i = 0; i < pre; ++i) load_x(i);
       int issued = pre;
-      for (int i = pre; i < nch; ++i) {
-        const int st = i % kGStages;
-        if (!mbar_wait(smem_u32(&s.empty[st]), ((i / kGStages) - 1) & 1, s, p.err, true)) break;
+      for (int i = pre; i < n; ++i) {
+        const int st = i % S;
+        if (!mbar_wait(smem_u32(&s.empty[st]), ((i / S) - 1) & 1, s, p.err, true)) break;
         mbar_arrive_expect_tx(smem_u32(&s.full[st]), kStageBytes);
         load_w(i);
         load_x(i);
         issued = i + 1;
       }
       // every copy issued has landed before the CTA may exit (bounded)
-      for (int i = issued > kGStages ? issued - kGStages : 0; i < issued; ++i)
-        mbar_wait(smem_u32(&s.full[i % kGStages]), (i / kGStages) & 1, s, p.err, false);
+      for (int i = issued > S ? issued - S : 0; i < issued; ++i)
+        mbar_wait(smem_u32(&s.full[i % S]), (i / S) & 1, s, p.err, false);
     } else {
       griddep_wait();
     }
@@ -1706,19 +1722,33 @@ __global__ void __launch_bounds__(kGThreads) gemv_kernel(const __grid_constant__
   }
   // ---------------------------------------------------------------------------------- consumers
   griddep_wait();
-  float acc[MT][2][4];
+  const int mi = lane >> 3, ri = lane & 7;
+  const int wrow = 16 * warp + 8 * (mi >> 1) + ri;   // this lane's W row for ldmatrix
+  const int tid = threadIdx.x, q = tid & 3;
+  // epilogue layout: row r0 + tid / 4, two 8-column segments of the 64-row tile
+  const int sa = EPI == GEMV_SWIGLU ? 8 * q : 16 * q;            // gate (or first) segment
+  const int sb = EPI == GEMV_SWIGLU ? 32 + 8 * q : 16 * q + 8;    // up (or second) segment
+  constexpr int kRows = 16 * MT;
+  int i = 0;   // ring position
+  for (long long u = u0; u < u1;) {
+    const int tile = static_cast<int>(u / p.nchunks);
+    const int a = static_cast<int>(u % p.nchunks);
+    const long long rest = u1 - u;
+    const int b = rest < p.nchunks - a ? a + static_cast<int>(rest) : p.nchunks;
+    const bool first_seg = u == u0;
+    float acc[MT][2][4];
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
-  {
-    const int mi = lane >> 3, ri = lane & 7;
-    const int wrow = 16 * warp + 8 * (mi >> 1) + ri;   // this lane's W row for ldmatrix
-    for (int i = 0; i < nch; ++i) {
-      const int st = i % kGStages;
-      mbar_wait(smem_u32(&s.full[st]), (i / kGStages) & 1, s, p.err, true);
+        for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
+    for (int c = a; c < b; ++c, ++i) {
+      const int st = i % S;
+      mbar_wait(smem_u32(&s.full[st]), (i / S) & 1, s, p.err, true);
+      // each lane spins on its own and may leave the loop at another time: ldmatrix and mma.sync
+      // are .aligned (all 32 lanes together), so reconverge first
+      __syncwarp();
       const uint32_t wb = smem_u32(&s.w[st][0]) + wrow * 128;
       const uint32_t xb = smem_u32(&s.x[st][0]);
 #pragma unroll
@@ -1737,164 +1767,165 @@ __global__ void __launch_bounds__(kGThreads) gemv_kernel(const __grid_constant__
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&s.empty[st]));
     }
-  }
-  griddep_launch_dependents();
-  // ---- the tile's fp32 sums to shared memory: rows 16 mt + lane / 4 (+ 8), W rows 16 warp +
-  // 8 nt + 2 (lane % 4) + {0, 1}. The ring is idle: every issued copy was consumed above.
-  float* ct = reinterpret_cast<float*>(&s.w[0][0]);
-  named_bar(1, kGW * 32);
+    u += b - a;
+    if (u >= u1) griddep_launch_dependents();
+    // ---- the segment's fp32 sums to shared memory: rows 16 mt + lane / 4 (+ 8), W rows
+    // 16 warp + 8 nt + 2 (lane % 4) + {0, 1}
+    named_bar(1, kGW * 32);   // the previous segment's epilogue is done with ct
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-        *reinterpret_cast<float2*>(ct + (16 * mt + 8 * h + (lane >> 2)) * kGLd + 16 * warp +
-                                   8 * nt + 2 * (lane & 3)) =
-            make_float2(acc[mt][nt][2 * h], acc[mt][nt][2 * h + 1]);
-  named_bar(1, kGW * 32);
-  // ---- epilogue layout: row r0 + tid / 4, two 8-column segments of the 64-row tile
-  const int tid = threadIdx.x, q = tid & 3;
-  const int sa = EPI == GEMV_SWIGLU ? 8 * q : 16 * q;            // gate (or first) segment
-  const int sb = EPI == GEMV_SWIGLU ? 32 + 8 * q : 16 * q + 8;    // up (or second) segment
-  const long long pw = static_cast<long long>(p.tiles) * kGBN;    // partial row width
-  const long long pcol = static_cast<long long>(tile) * kGBN;
-  constexpr int kRows = 16 * MT;
-  if (p.splits > 1) {
+        for (int nt = 0; nt < 2; ++nt)
+          *reinterpret_cast<float2*>(&s.ct[16 * mt + 8 * h + (lane >> 2)]
+                                          [16 * warp + 8 * nt + 2 * (lane & 3)]) =
+              make_float2(acc[mt][nt][2 * h], acc[mt][nt][2 * h + 1]);
+    named_bar(1, kGW * 32);
+    // ---- a tile split between CTAs: partial out, the last arriver adds the segments
+    const bool whole = a == 0 && b == p.nchunks;
+    const long long tu0 = static_cast<long long>(tile) * p.nchunks;
+    const int kfirst = static_cast<int>(tu0 / p.per);                    // CTAs holding the tile
+    const int klast = static_cast<int>((tu0 + p.nchunks - 1) / p.per);
+    if (!whole) {
+      const int slot = 2 * blockIdx.x + (first_seg ? 0 : 1);
+      for (int r0 = 0; r0 < kRows; r0 += 32) {
+        const int m = r0 + (tid >> 2);
+        if (m < kRows && m < p.M) {
+          float* dst = p.part + (static_cast<long long>(slot) * p.M + m) * kGBN;
+          const float* src = &s.ct[m][0];
+#pragma unroll
+          for (int j = 0; j < 8; j += 4) {
+            __stcg(reinterpret_cast<float4*>(dst + sa + j), *reinterpret_cast<const float4*>(src + sa + j));
+            __stcg(reinterpret_cast<float4*>(dst + sb + j), *reinterpret_cast<const float4*>(src + sb + j));
+          }
+        }
+      }
+      __threadfence();
+      named_bar(1, kGW * 32);
+      if (tid == 0) {
+        s.last = atomicAdd(&p.cnt[tile], 1) == klast - kfirst;
+        if (s.last) __threadfence();   // acquire the other segments' partials
+      }
+      named_bar(1, kGW * 32);
+      if (!s.last) continue;
+      if (tid == 0) atomicExch(&p.cnt[tile], 0);
+    }
     for (int r0 = 0; r0 < kRows; r0 += 32) {
       const int m = r0 + (tid >> 2);
-      if (m < kRows && m < p.M) {
-        float* dst = p.part + (static_cast<long long>(split) * p.M + m) * pw + pcol;
-        const float* src = ct + m * kGLd;
+      const bool act = m < kRows && m < p.M;
+      if (EPI != GEMV_ARGMAX && !act) continue;   // ARGMAX: every lane takes part in the shuffles
+      float v[16];
+      if (!act) {
 #pragma unroll
-        for (int j = 0; j < 8; j += 4) {
-          __stcg(reinterpret_cast<float4*>(dst + sa + j), *reinterpret_cast<const float4*>(src + sa + j));
-          __stcg(reinterpret_cast<float4*>(dst + sb + j), *reinterpret_cast<const float4*>(src + sb + j));
+        for (int j = 0; j < 16; ++j) v[j] = -INFINITY;
+      } else if (!whole) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = 0.f;
+        for (int k = kfirst; k <= klast; ++k) {   // fixed order: the tile's first CTA first
+          const bool kfirst_seg = static_cast<long long>(k) * p.per >= tu0;
+          const float* src = p.part + (static_cast<long long>(2 * k + (kfirst_seg ? 0 : 1)) * p.M + m) * kGBN;
+#pragma unroll
+          for (int j = 0; j < 8; j += 4) {
+            const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src + sa + j));
+            const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + sb + j));
+            v[j] += x0.x; v[j + 1] += x0.y; v[j + 2] += x0.z; v[j + 3] += x0.w;
+            v[8 + j] += x1.x; v[9 + j] += x1.y; v[10 + j] += x1.z; v[11 + j] += x1.w;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[j] = s.ct[m][sa + j];
+          v[8 + j] = s.ct[m][sb + j];
         }
       }
-    }
-    __threadfence();
-    named_bar(1, kGW * 32);
-    if (tid == 0) {
-      s.last = atomicAdd(&p.cnt[tile], 1) == p.splits - 1;
-      if (s.last) __threadfence();   // acquire the other splits' partials
-    }
-    named_bar(1, kGW * 32);
-    if (!s.last) return;
-    if (tid == 0) atomicExch(&p.cnt[tile], 0);
-  }
-  for (int r0 = 0; r0 < kRows; r0 += 32) {
-    const int m = r0 + (tid >> 2);
-    const bool act = m < kRows && m < p.M;
-    if (EPI != GEMV_ARGMAX && !act) continue;   // ARGMAX: every lane takes part in the shuffles
-    float v[16];
-    if (!act) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = -INFINITY;
-    } else if (p.splits > 1) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = 0.f;
-      for (int sp = 0; sp < p.splits; ++sp) {   // fixed order: split 0 first
-        const float* src = p.part + (static_cast<long long>(sp) * p.M + m) * pw + pcol;
+      const long long pcol = static_cast<long long>(tile) * kGBN;
+      if (EPI == GEMV_F32) {
+        float* y = static_cast<float*>(p.y) + static_cast<long long>(m) * p.N + pcol;
 #pragma unroll
         for (int j = 0; j < 8; j += 4) {
-          const float4 a = __ldcg(reinterpret_cast<const float4*>(src + sa + j));
-          const float4 b = __ldcg(reinterpret_cast<const float4*>(src + sb + j));
-          v[j] += a.x; v[j + 1] += a.y; v[j + 2] += a.z; v[j + 3] += a.w;
-          v[8 + j] += b.x; v[9 + j] += b.y; v[10 + j] += b.z; v[11 + j] += b.w;
+          *reinterpret_cast<float4*>(y + sa + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          *reinterpret_cast<float4*>(y + sb + j) =
+              make_float4(v[8 + j], v[9 + j], v[10 + j], v[11 + j]);
         }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        v[j] = ct[m * kGLd + sa + j];
-        v[8 + j] = ct[m * kGLd + sb + j];
-      }
-    }
-    if (EPI == GEMV_F32) {
-      float* y = static_cast<float*>(p.y) + static_cast<long long>(m) * p.N + pcol;
-#pragma unroll
-      for (int j = 0; j < 8; j += 4) {
-        *reinterpret_cast<float4*>(y + sa + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        *reinterpret_cast<float4*>(y + sb + j) =
-            make_float4(v[8 + j], v[9 + j], v[10 + j], v[11 + j]);
-      }
-    } else if (EPI == GEMV_BF16) {
-      bf16* y = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + pcol;
-      uint4 a, b;
-      uint32_t* pa = reinterpret_cast<uint32_t*>(&a);
-      uint32_t* pb = reinterpret_cast<uint32_t*>(&b);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        pa[e] = pack_bf16(v[2 * e], v[2 * e + 1]);
-        pb[e] = pack_bf16(v[8 + 2 * e], v[9 + 2 * e]);
-      }
-      *reinterpret_cast<uint4*>(y + sa) = a;
-      *reinterpret_cast<uint4*>(y + sb) = b;
-    } else if (EPI == GEMV_RESID) {   // h <- bf16(h + bf16(acc)) (gemv.py:95-97)
-      bf16* h = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + pcol;
-#pragma unroll
-      for (int seg = 0; seg < 2; ++seg) {
-        bf16* hp = h + (seg == 0 ? sa : sb);
-        uint4 hv = *reinterpret_cast<const uint4*>(hp);
-        uint32_t* ph = reinterpret_cast<uint32_t*>(&hv);
+      } else if (EPI == GEMV_BF16) {
+        bf16* y = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + pcol;
+        uint4 o0, o1;
+        uint32_t* p0 = reinterpret_cast<uint32_t*>(&o0);
+        uint32_t* p1 = reinterpret_cast<uint32_t*>(&o1);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float2 f = bf2f(ph[e]);
-          ph[e] = pack_bf16(__fadd_rn(f.x, bf16r(v[8 * seg + 2 * e])),
-                            __fadd_rn(f.y, bf16r(v[8 * seg + 2 * e + 1])));
+          p0[e] = pack_bf16(v[2 * e], v[2 * e + 1]);
+          p1[e] = pack_bf16(v[8 + 2 * e], v[9 + 2 * e]);
         }
-        *reinterpret_cast<uint4*>(hp) = hv;
-      }
-    } else if (EPI == GEMV_ARGMAX) {
-      // this thread's 16 columns, then the row's 4 threads, then all tiles through one 64-bit
-      // atomicMax per row: key = (order-preserving bits of the bf16 logit) << 32 | ~index, so
-      // the larger logit wins and, on equal logits, the smaller index
-      float best = -INFINITY;
-      int bi = 0x7fffffff;
+        *reinterpret_cast<uint4*>(y + sa) = o0;
+        *reinterpret_cast<uint4*>(y + sb) = o1;
+      } else if (EPI == GEMV_RESID) {   // h <- bf16(h + bf16(acc)) (gemv.py:95-97)
+        bf16* h = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + pcol;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float l = bf16r(v[j]) + 0.0f;   // -0 -> +0: equal logits compare equal
-        const int col = static_cast<int>(pcol) + (j < 8 ? sa + j : sb + j - 8);
-        if (l > best || (l == best && col < bi)) {
-          best = l;
-          bi = col;
+        for (int seg = 0; seg < 2; ++seg) {
+          bf16* hp = h + (seg == 0 ? sa : sb);
+          uint4 hv = *reinterpret_cast<const uint4*>(hp);
+          uint32_t* ph = reinterpret_cast<uint32_t*>(&hv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = bf2f(ph[e]);
+            ph[e] = pack_bf16(__fadd_rn(f.x, bf16r(v[8 * seg + 2 * e])),
+                              __fadd_rn(f.y, bf16r(v[8 * seg + 2 * e + 1])));
+          }
+          *reinterpret_cast<uint4*>(hp) = hv;
         }
-      }
-      const uint32_t u = __float_as_uint(best);
-      const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-      unsigned long long key = (static_cast<unsigned long long>(ord) << 32) |
-                               static_cast<uint32_t>(0xffffffffu - static_cast<uint32_t>(bi));
-      key = max(key, __shfl_xor_sync(0xffffffffu, key, 1));
-      key = max(key, __shfl_xor_sync(0xffffffffu, key, 2));
-      if (q == 0 && act) atomicMax(p.keys + m, key);
-    } else {   // SWIGLU: output columns 32 tile + 8 q .. + 8 (gemv.py:101-105)
-      bf16* y = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + tile * 32 + 8 * q;
-      uint4 o;
-      uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+      } else if (EPI == GEMV_ARGMAX) {
+        // this thread's 16 columns, then the row's 4 threads, then all tiles through one 64-bit
+        // atomicMax per row: key = (order-preserving bits of the bf16 logit) << 32 | ~index, so
+        // the larger logit wins and, on equal logits, the smaller index
+        float best = -INFINITY;
+        int bi = 0x7fffffff;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float s0 = silu_bf16(bf16r(v[2 * e])), s1 = silu_bf16(bf16r(v[2 * e + 1]));
-        po[e] = pack_bf16(__fmul_rn(s0, bf16r(v[8 + 2 * e])), __fmul_rn(s1, bf16r(v[9 + 2 * e])));
+        for (int j = 0; j < 16; ++j) {
+          const float l = bf16r(v[j]) + 0.0f;   // -0 -> +0: equal logits compare equal
+          const int col = static_cast<int>(pcol) + (j < 8 ? sa + j : sb + j - 8);
+          if (l > best || (l == best && col < bi)) {
+            best = l;
+            bi = col;
+          }
+        }
+        const uint32_t ub = __float_as_uint(best);
+        const uint32_t ord = (ub & 0x80000000u) ? ~ub : (ub | 0x80000000u);
+        unsigned long long key = (static_cast<unsigned long long>(ord) << 32) |
+                                 static_cast<uint32_t>(0xffffffffu - static_cast<uint32_t>(bi));
+        key = max(key, __shfl_xor_sync(0xffffffffu, key, 1));
+        key = max(key, __shfl_xor_sync(0xffffffffu, key, 2));
+        if (q == 0 && act) atomicMax(p.keys + m, key);
+      } else {   // SWIGLU: output columns 32 tile + 8 q .. + 8 (gemv.py:101-105)
+        bf16* y = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + tile * 32 + 8 * q;
+        uint4 o;
+        uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float s0 = silu_bf16(bf16r(v[2 * e])), s1 = silu_bf16(bf16r(v[2 * e + 1]));
+          po[e] = pack_bf16(__fmul_rn(s0, bf16r(v[8 + 2 * e])), __fmul_rn(s1, bf16r(v[9 + 2 * e])));
+        }
+        *reinterpret_cast<uint4*>(y) = o;
       }
-      *reinterpret_cast<uint4*>(y) = o;
     }
-  }
-  if (EPI == GEMV_ARGMAX) {   // the tile that finishes last turns the keys into token ids
-    __threadfence();
-    named_bar(1, kGW * 32);
-    if (tid == 0) {
-      s.last_all = atomicAdd(&p.cnt[p.tiles], 1) == p.tiles - 1;
-      if (s.last_all) __threadfence();
-    }
-    named_bar(1, kGW * 32);
-    if (s.last_all) {
-      if (tid < p.M) {
-        const unsigned long long key = atomicExch(p.keys + tid, 0ull);   // read and re-arm
-        static_cast<long long*>(p.y)[tid] =
-            static_cast<long long>(0xffffffffu - static_cast<uint32_t>(key & 0xffffffffu));
+    if (EPI == GEMV_ARGMAX) {   // the tile that finishes last turns the keys into token ids
+      __threadfence();
+      named_bar(1, kGW * 32);
+      if (tid == 0) {
+        s.last_all = atomicAdd(&p.cnt[p.tiles], 1) == p.tiles - 1;
+        if (s.last_all) __threadfence();
       }
-      if (tid == 0) atomicExch(&p.cnt[p.tiles], 0);
+      named_bar(1, kGW * 32);
+      if (s.last_all) {
+        if (tid < p.M) {
+          const unsigned long long key = atomicExch(p.keys + tid, 0ull);   // read and re-arm
+          static_cast<long long*>(p.y)[tid] =
+              static_cast<long long>(0xffffffffu - static_cast<uint32_t>(key & 0xffffffffu));
+        }
+        if (tid == 0) atomicExch(&p.cnt[p.tiles], 0);
+      }
     }
   }
 }
@@ -2116,14 +2147,14 @@ int launch_verify(const kopt_plan* plan, Params& p, void* stream) {
 
 // ------------------------------------------------------------------------------- GEMV host side
 // Workspace: [0, 256) the error word; one arrival counter per tile and one for tiles done; the
-// ARGMAX keys of up to 64 rows; then the split partials.
+// ARGMAX keys of up to 64 rows; then two fp32 segment partials [M][64] per CTA.
 struct GemvWs { int64_t cnt, keys, part, total; };
-GemvWs gemv_ws_layout(int M, int tiles, int splits) {
+GemvWs gemv_ws_layout(int M, int tiles, int grid) {
   GemvWs w;
   w.cnt = kHeaderBytes;
   w.keys = w.cnt + (static_cast<int64_t>(tiles + 1) * 4 + 255) / 256 * 256;
   w.part = w.keys + 64 * 8;
-  w.total = w.part + (splits > 1 ? static_cast<int64_t>(splits) * M * tiles * kGBN * 4 : 0);
+  w.total = w.part + 2 * static_cast<int64_t>(grid) * M * kGBN * 4;
   return w;
 }
 inline int gemv_mt(int M) { return M <= 16 ? 1 : M <= 32 ? 2 : 4; }
@@ -2160,27 +2191,6 @@ int gemv_configure(int device, int M, int epi, int* blocks_per_sm) {
   return mt == 1 ? gemv_occupancy_epi<1>(device, epi, blocks_per_sm)
                  : mt == 2 ? gemv_occupancy_epi<2>(device, epi, blocks_per_sm)
                            : gemv_occupancy_epi<4>(device, epi, blocks_per_sm);
-}
-
-// Splits of K per tile. Per SM the CTAs' chunks stream one after another, so the time goes with
-// ceil(tiles * splits / SMs) * ceil(chunks / splits) weight tiles; each split beyond the first adds
-// its fp32 partial (written once, read once, mostly in L2), counted here at a third of its bytes.
-int gemv_pick_splits(int M, int tiles, int nchunks, int sms) {
-  const int cap = nchunks < 32 ? nchunks : 32;
-  int best = 1;
-  double best_cost = 1e30;
-  for (int sp = 1; sp <= cap; ++sp) {
-    const double per_sm = static_cast<double>((static_cast<long long>(tiles) * sp + sms - 1) / sms);
-    const double chunks = per_sm * ((nchunks + sp - 1) / sp);
-    const double part = sp > 1 ? static_cast<double>(tiles) * sp * M * kGBN * 8 /
-                                     (3.0 * kGBN * kGBK * 2) / sms
-                               : 0.0;
-    if (chunks + part < best_cost * 0.98) {
-      best_cost = chunks + part;
-      best = sp;
-    }
-  }
-  return best;
 }
 
 template <int MT, int EPI>
@@ -2262,10 +2272,10 @@ int kopt_silu_mul(const void* gate_up, void* out, int M, int I, void* stream) {
   return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
 }
 
-int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int splits,
+int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int target_ctas,
                         kopt_gemv_plan* plan) {
   if (plan == nullptr || M < 1 || M > 64 || K < 8 || K % 8 != 0 || N < 1 || epi < GEMV_F32 ||
-      epi > GEMV_ARGMAX || splits < 0)
+      epi > GEMV_ARGMAX || target_ctas < 0)
     return KOPT_ERR_ARG;
   if (N % (epi == GEMV_SWIGLU ? 32 : kGBN) != 0) return KOPT_ERR_ARG;
   int rc = set_device(device);
@@ -2278,21 +2288,25 @@ int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int splits,
     return KOPT_ERR_CUDA;
   const int tiles = epi == GEMV_SWIGLU ? N / 32 : N / kGBN;
   const int nchunks = (K + kGBK - 1) / kGBK;
-  if (splits == 0) splits = gemv_pick_splits(M, tiles, nchunks, sms);
-  if (splits > nchunks) splits = nchunks;
-  if (static_cast<long long>(tiles) * splits > 0x7fffffffLL) return KOPT_ERR_ARG;
+  const long long units = static_cast<long long>(tiles) * nchunks;
+  // one resident wave: every CTA streams one equal run of units
+  long long ctas = target_ctas > 0 ? target_ctas : static_cast<long long>(sms) * occ;
+  if (ctas > units) ctas = units;
+  const long long per = (units + ctas - 1) / ctas;
+  const long long grid = (units + per - 1) / per;
+  if (per > 0x7fffffffLL || grid > 0x7fffffffLL) return KOPT_ERR_ARG;
   *plan = kopt_gemv_plan{};
   plan->device = device;
   plan->M = M;
   plan->N = N;
   plan->K = K;
   plan->epi = epi;
-  plan->splits = splits;
+  plan->units_per_cta = static_cast<int32_t>(per);
   plan->tiles = tiles;
-  plan->grid = tiles * splits;
+  plan->grid = static_cast<int32_t>(grid);
   plan->ctas_per_sm = occ;
   plan->flags = 0;
-  plan->ws_bytes = gemv_ws_layout(M, tiles, splits).total;
+  plan->ws_bytes = gemv_ws_layout(M, tiles, plan->grid).total;
   return KOPT_OK;
 }
 
@@ -2324,7 +2338,11 @@ int kopt_gemv(const kopt_gemv_plan* plan, const void* x, const void* w, void* y,
           elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return KOPT_ERR_ARG;
-  const GemvWs lay = gemv_ws_layout(plan->M, plan->tiles, plan->splits);
+  const int nchunks = (plan->K + kGBK - 1) / kGBK;
+  const long long units = static_cast<long long>(plan->tiles) * nchunks;
+  if (plan->units_per_cta < 1 || plan->grid != (units + plan->units_per_cta - 1) / plan->units_per_cta)
+    return KOPT_ERR_ARG;
+  const GemvWs lay = gemv_ws_layout(plan->M, plan->tiles, plan->grid);
   if (lay.total != plan->ws_bytes) return KOPT_ERR_WORKSPACE;
   char* base = static_cast<char*>(ws);
   p.y = y;
@@ -2332,12 +2350,13 @@ int kopt_gemv(const kopt_gemv_plan* plan, const void* x, const void* w, void* y,
   p.cnt = reinterpret_cast<int*>(base + lay.cnt);
   p.part = reinterpret_cast<float*>(base + lay.part);
   p.keys = reinterpret_cast<unsigned long long*>(base + lay.keys);
+  p.units = units;
   p.M = plan->M;
   p.N = plan->N;
   p.K = plan->K;
-  p.splits = plan->splits;
-  p.nchunks = (plan->K + kGBK - 1) / kGBK;
+  p.nchunks = nchunks;
   p.tiles = plan->tiles;
+  p.per = plan->units_per_cta;
   return mt == 1 ? gemv_launch_epi<1>(plan, p, stream)
                  : mt == 2 ? gemv_launch_epi<2>(plan, p, stream) : gemv_launch_epi<4>(plan, p, stream);
 }
@@ -2354,7 +2373,7 @@ int kopt_gemv_read_error(const kopt_gemv_plan* plan, void* ws, int* err_out, voi
   *err_out = host;
   if (host != 0 &&   // a timed-out launch may leave counters and keys behind: clear them too
       cudaMemsetAsync(ws, 0,
-                      static_cast<size_t>(gemv_ws_layout(plan->M, plan->tiles, plan->splits).part),
+                      static_cast<size_t>(gemv_ws_layout(plan->M, plan->tiles, plan->grid).part),
                       st) != cudaSuccess)
     return KOPT_ERR_CUDA;
   return KOPT_OK;

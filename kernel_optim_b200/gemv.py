@@ -19,8 +19,9 @@ y[M, N] = x[M, K] . w[N, K]^T with fp32 sums and one epilogue (gemv.py:86-105):
 writes the normalised rows once: re-normalising x inside every weight tile would repeat the work
 once per tile (96 to 600 times for Qwen3-4B's projections). The row sums of squares are recomputed
 from x there, so ``ss`` and ``ss_out`` (the reference's hand-off of those sums between kernels) are
-neither read nor written. The kernel splits K for every epilogue, not only EPI_F32, so
-``allow_split`` is accepted for the signature and does not restrict the split.
+neither read nor written. The kernel splits K wherever a tile's chunks fall to several CTAs, for
+every epilogue (their fp32 partials are added in CTA order), so ``allow_split`` is accepted for
+the signature and does not restrict the split.
 
 Launches go to the current torch stream of the tensors' device; a missing library raises KoptError.
 """
@@ -42,12 +43,13 @@ EPI_F32, EPI_BF16, EPI_RESID, EPI_SWIGLU, EPI_ARGMAX = (
 
 class Gemv:
     """One fused projection of M rows; owns its workspace, so calls allocate nothing and can be
-    captured in a CUDA graph. ``splits`` = 0 lets the library pick the K split from the SM count;
+    captured in a CUDA graph. ``ctas`` = 0 launches one resident wave of persistent CTAs, each
+    streaming an equal run of (weight tile, K chunk) units; a positive value sets the CTA count.
     ``overlap_prev`` launches with programmatic dependent launch (weight tiles stream while the
     kernel before it on the stream drains)."""
 
     def __init__(self, M, N, K, epi, norm=False, allow_split=False, eps=1e-6, device=None,
-                 splits=0, overlap_prev=False):
+                 ctas=0, overlap_prev=False):
         self.M, self.N, self.K, self.epi, self.norm, self.eps = M, N, K, epi, norm, eps
         self.allow_split = allow_split
         dev = torch.device(device) if device is not None else torch.device("cuda")
@@ -55,22 +57,27 @@ class Gemv:
         self.overlap_prev = overlap_prev
         self._xn = torch.empty(M, K, dtype=torch.bfloat16, device=self.device) if norm else None
         self._plans: dict[int, tuple[GemvPlan, torch.Tensor]] = {}
-        self.cfg = self._plan(splits).splits
+        self.cfg = self._plan(ctas).grid
 
-    def _plan(self, splits: int) -> GemvPlan:
-        if splits in self._plans:
-            return self._plans[splits][0]
+    def _plan(self, ctas: int) -> GemvPlan:
+        """Plan (and workspace) for a requested CTA count; cached under the request and under the
+        grid it resolves to, which is what ``cfg`` holds."""
+        if ctas in self._plans:
+            return self._plans[ctas][0]
         plan = GemvPlan()
         check(_lib.lib().kopt_gemv_plan_make(self.device.index, self.M, self.N, self.K, self.epi,
-                                             splits, ctypes.byref(plan)), "kopt_gemv_plan_make")
+                                             ctas, ctypes.byref(plan)), "kopt_gemv_plan_make")
         plan.flags = _lib.GEMV_OVERLAP_PREV if self.overlap_prev else 0
+        if plan.grid in self._plans:
+            self._plans[ctas] = self._plans[plan.grid]
+            return self._plans[ctas][0]
         ws = torch.zeros(plan.ws_bytes, dtype=torch.uint8, device=self.device)
-        self._plans[splits] = (plan, ws)
-        self._plans[plan.splits] = (plan, ws)
+        self._plans[ctas] = (plan, ws)
+        self._plans[plan.grid] = (plan, ws)
         return plan
 
     @property
-    def splits(self) -> int:
+    def grid(self) -> int:
         return self.cfg
 
     def __call__(self, x, w, y=None, nw=None, ss=None, h=None, ss_out=None, cfg=None):
@@ -116,14 +123,14 @@ class Gemv:
         return err.value
 
     def candidates(self) -> list[int]:
-        """K splits worth timing: the library's pick first, then a spread up to the chunk count."""
-        nchunks = (self.K + 63) // 64
-        auto = self._plan(0).splits
-        out = [auto] + [s for s in (1, 2, 3, 4, 6, 8, 11, 16, 24) if s <= nchunks]
+        """Grid sizes worth timing: the library's one resident wave first, then fractions of it."""
+        auto = self._plan(0)
+        sms = auto.grid // max(auto.ctas_per_sm, 1)
+        out = [auto.grid] + [self._plan(c).grid for c in (sms, 3 * sms // 2, 3 * sms) if c > 0]
         return list(dict.fromkeys(out))
 
     def tune(self, weights, deadline):
-        """Pick the K split by GPU time: one call per real layer weight (cold, as in a decode step),
+        """Pick the grid by GPU time: one call per real layer weight (cold, as in a decode step),
         captured in a CUDA graph; stops trying new candidates after ``deadline``
         (time.monotonic()), keeping the best so far. Mirrors gemv.py:152-199."""
         dev = weights[0].device
@@ -158,6 +165,6 @@ class Gemv:
             if best is None or t < best[0]:
                 best = (t, cfg)
         if best is not None:
-            self.cfg = self._plan(best[1]).splits
+            self.cfg = self._plan(best[1]).grid
             self.us = best[0] / (2 * len(weights)) * 1e3
         return self.cfg

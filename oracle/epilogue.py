@@ -39,19 +39,19 @@ def silu_mul_ref(gu: torch.Tensor) -> torch.Tensor:
 GEMV_F32, GEMV_BF16, GEMV_RESID, GEMV_SWIGLU, GEMV_ARGMAX = 0, 1, 2, 3, 4
 
 
-def gemv_ref(x: torch.Tensor, w: torch.Tensor, epi: int, h: torch.Tensor | None = None) -> torch.Tensor:
-    """x [M, K], w [N, K] ([2N, K] gate|up for SWIGLU), bf16 -> the epilogue's output: fp32 sums
-    (F32), bf16(sum) (BF16), bf16(h + bf16(sum)) (RESID, gemv.py:95-97),
+def gemv_epilogue_ref(acc: torch.Tensor, epi: int, h: torch.Tensor | None = None) -> torch.Tensor:
+    """The epilogues of gemv.py:86-105 applied to fp32 sums acc [M, N] ([M, 2N] gate|up for
+    SWIGLU): acc (F32), bf16(acc) (BF16), bf16(h + bf16(acc)) (RESID, gemv.py:95-97),
     bf16(bf16(silu(bf16 g)) * bf16 u) (SWIGLU, gemv.py:101-105), or the int64 index of each row's
-    largest bf16(sum) (ARGMAX: engine.py:263's bf16 logits, then the greedy argmax)."""
-    acc = x.float() @ w.float().t()
+    largest bf16(acc), the first one among equal values (ARGMAX: engine.py:263's bf16 logits,
+    then the greedy argmax)."""
     if epi == GEMV_F32:
         return acc
     if epi == GEMV_BF16:
         return acc.to(torch.bfloat16)
     if epi == GEMV_RESID:
         return bf16r(h.float() + bf16r(acc)).to(torch.bfloat16)
-    if epi == GEMV_ARGMAX:   # greedy pick over bf16 logits, first index among equal values
+    if epi == GEMV_ARGMAX:
         logits = bf16r(acc)
         top = logits.max(dim=1, keepdim=True).values
         cols = torch.arange(logits.shape[1]).expand_as(logits)
@@ -60,3 +60,9 @@ def gemv_ref(x: torch.Tensor, w: torch.Tensor, epi: int, h: torch.Tensor | None 
     g, u = bf16r(acc[:, :n]), bf16r(acc[:, n:])
     s = bf16r(g / (1.0 + torch.exp(-g)))
     return bf16r(s * u).to(torch.bfloat16)
+
+
+def gemv_ref(x: torch.Tensor, w: torch.Tensor, epi: int, h: torch.Tensor | None = None) -> torch.Tensor:
+    """x [M, K], w [N, K] ([2N, K] gate|up for SWIGLU), bf16 -> gemv_epilogue_ref of the fp32
+    sums x . w^T."""
+    return gemv_epilogue_ref(x.float() @ w.float().t(), epi, h)
