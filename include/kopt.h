@@ -222,7 +222,9 @@ KOPT_API int kopt_decode_attn_fused_noalloc(const kopt_plan* plan, const void* q
 
 /* ---- decode-step projections (skinny GEMM) ------------------------------------------------ *
  * y[M, N] = x[M, K] . W[N, K]^T for the rows of a decode batch (M <= 64), bf16 x and W, fp32 sums,
- * each weight read once for all rows. Replaces Gemv (engine/kernels/gemv.py:109-150) and the
+ * each weight read once for all rows, on the tcgen05 tensor cores (weight rows as the MMA's M = 128,
+ * decode rows as its N, fp32 accumulators in tensor memory). Replaces Gemv
+ * (engine/kernels/gemv.py:109-150) and the
  * epilogues of its kernel (gemv.py:29-106); the NORM prologue stays a row kernel
  * (kopt_add_rms_norm), which normalises x once instead of once per weight tile. */
 #define KOPT_GEMV_F32 0     /* y: float [M, N], the fp32 sums */
@@ -242,7 +244,8 @@ typedef struct kopt_gemv_plan {
                                 contiguous run of them, tile-major; a tile whose units fall to
                                 several CTAs is summed from their fp32 partials in CTA order, so
                                 results never depend on timing */
-  int32_t tiles;             /* weight tiles: N / 64 (SWIGLU: N / 32 gate rows with their up rows) */
+  int32_t tiles;             /* weight tiles: ceil(N / 128) (SWIGLU: N / 64 gate rows with their up
+                                rows) */
   int32_t grid;              /* CTAs: ceil(tiles * ceil(K / 64) / units_per_cta) */
   int32_t ctas_per_sm;       /* resident CTAs per SM reported by the occupancy query */
   int32_t flags;             /* KOPT_GEMV_* bits below: 0 from kopt_gemv_plan_make */
@@ -254,9 +257,9 @@ typedef struct kopt_gemv_plan {
  * x, y (h) and the workspace are touched only after the wait, so any predecessor is safe. */
 #define KOPT_GEMV_OVERLAP_PREV 1
 
-/* Plan a projection of M rows (1 .. 64), N outputs (a multiple of 64; of 32 for SWIGLU) and K
- * inputs (a multiple of 8). target_ctas = 0 launches one resident wave (SM count x resident CTAs
- * per SM); a positive value asks for that many CTAs instead (at most one per unit). */
+/* Plan a projection of M rows (1 .. 64), N outputs (a multiple of 16; of 64 for SWIGLU) and K
+ * inputs (a multiple of 8). target_ctas = 0 launches one resident wave (one CTA per SM); a
+ * positive value asks for that many CTAs instead (at most one per unit). */
 KOPT_API int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int target_ctas,
                                  kopt_gemv_plan* plan);
 /* y = epilogue(x . W^T) on `stream`. x: [M, K] bf16 row-major; W: [N, K] (SWIGLU [2N, K]) bf16

@@ -1590,36 +1590,45 @@ __global__ void silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ 
 // (engine.py:263 and the greedy pick after it) without writing the logits. Only the fp32
 // accumulation order differs from cuBLAS.
 //
-// Persistent stream-K: the weight is cut into 64-row tiles (SWIGLU: 32 gate rows + the matching
-// 32 up rows) of 64-wide K chunks; the (tile, chunk) units, tile-major, are dealt to the CTAs in
-// equal contiguous runs, one run per CTA, two CTAs per SM. A producer warp streams each unit's
-// 64 x 64 weight tile and the matching x tile by TMA through a deep ring, across tile boundaries,
-// so HBM never waits on an epilogue; 4 consumer warps take 16 weight rows each on mma.sync
-// m16n8k16 over all 16 MT rows of x. Where a run ends inside a tile, that segment's fp32 partial
-// goes to the workspace and the CTA that arrives last at the tile adds the segments in CTA order
-// (fixed, whichever finishes first) before the epilogue.
+// The weight is the MMA's A operand and the decode rows its B operand: D[128 weight rows][16 MT
+// decode rows] += W[128][K] . x[16 MT][K]^T on the 5th-generation tensor cores (tcgen05.mma,
+// kind::f16, bf16 in, fp32 accumulators in tensor memory). Persistent stream-K, one CTA per SM:
+// the weight is cut into 128-row tiles (SWIGLU: 64 gate rows + the matching 64 up rows) of 64-wide
+// K chunks; the (tile, chunk) units, tile-major, are dealt to the CTAs in equal contiguous runs.
+//   warp 4  TMA producer: each unit's 128 x 64 weight tile and the matching x tile into a deep
+//           ring (128-byte swizzle, the layout the MMA descriptors name);
+//   warp 5  allocates tensor memory and one thread issues the MMAs, 4 of K = 16 per chunk, into
+//           one of two accumulators, releasing each stage and each finished accumulator with
+//           tcgen05.commit;
+//   warps 0-3 read a finished accumulator (tcgen05.ld, lanes 32w..32w+31), hand it back, and run
+//           the epilogue while the next segment accumulates in the other one.
+// Where a run ends inside a tile, that segment's fp32 partial goes to the workspace and the CTA
+// that arrives last at the tile adds the segments in CTA order (fixed, whichever finishes first)
+// before the epilogue.
 //
 // Launched with programmatic stream serialization, the producer issues the weight copies of the
 // first ring stages before griddepcontrol.wait: weights never depend on the previous kernel, so
 // they stream while it drains. x, h and the workspace are touched only after the wait.
-constexpr int kGW = 4;                   // consumer warps
-constexpr int kGThreads = (kGW + 1) * 32;
-constexpr int kGBN = 64;                 // W rows per tile
-constexpr int kGBK = 64;                 // k per chunk (one ring stage)
-constexpr int kGLd = kGBN + 8;           // fp32 tile row stride in shared memory (floats)
+constexpr int kGEpiWarps = 4;            // epilogue warps: tensor-memory lanes 0-127
+constexpr int kGProducerWarp = 4;
+constexpr int kGMmaWarp = 5;
+constexpr int kGThreads = 6 * 32;
+constexpr int kGRows = 128;              // weight rows per tile = the MMA's M
+constexpr int kGBK = 64;                 // k per chunk (one ring stage: 4 MMAs of K = 16)
+constexpr int kGLd = kGRows + 4;         // fp32 tile row stride in shared memory (floats)
 constexpr int GEMV_F32 = KOPT_GEMV_F32, GEMV_BF16 = KOPT_GEMV_BF16, GEMV_RESID = KOPT_GEMV_RESID,
               GEMV_SWIGLU = KOPT_GEMV_SWIGLU, GEMV_ARGMAX = KOPT_GEMV_ARGMAX;
-// ring depth: about 100 KB of shared memory per CTA, two CTAs per SM
+// ring depth: as many stages as fit in shared memory next to the fp32 tile
 template <int MT>
-__host__ __device__ constexpr int gemv_stages() { return MT == 1 ? 10 : MT == 2 ? 8 : 5; }
+__host__ __device__ constexpr int gemv_stages() { return MT == 1 ? 11 : MT == 2 ? 10 : 7; }
 
 struct GemvParams {
-  CUtensorMap tmw;                       // W [rows, K]: box 64 k x 64 rows (SWIGLU: 32 rows)
+  CUtensorMap tmw;                       // W [rows, K]: box 64 k x 128 rows (SWIGLU: 64 rows)
   CUtensorMap tmx;                       // x [M, K]: box 64 k x 16 MT rows (rows >= M read as 0)
   void* y;                               // F32: float [M, N]; BF16, SWIGLU: bf16 [M, N];
                                          // RESID: the residual h [M, N], updated in place;
                                          // ARGMAX: int64 [M]
-  float* part;                           // segment partials [2 grid][M][64]: 2c = CTA c's first
+  float* part;                           // segment partials [2 grid][M][128]: 2c = CTA c's first
                                          // segment, 2c + 1 = its last
   int* cnt;                              // arrivals per tile, then tiles done (zero between launches)
   unsigned long long* keys;              // ARGMAX: per row, the best (bf16 logit, -index) so far
@@ -1631,28 +1640,92 @@ struct GemvParams {
 template <int MT>
 struct __align__(1024) GSmem {
   static constexpr int S = gemv_stages<MT>();
-  bf16 w[S][kGBN * kGBK];                // 8 KB per stage
-  bf16 x[S][16 * MT * kGBK];
-  float ct[16 * MT][kGLd];               // a finished segment's fp32 sums
-  unsigned long long full[S], empty[S];
+  bf16 w[S][kGRows * kGBK];              // 16 KB per stage
+  bf16 x[S][16 * MT * kGBK];             // 2 KB per 16 decode rows per stage
+  float ct[16 * MT][kGLd];               // a finished segment's fp32 sums, [decode row][weight row]
+  unsigned long long full[S], empty[S], tfull[2], tempty[2], fin;
+  uint32_t tmem;                         // tensor-memory base from tcgen05.alloc
   int last;
   int last_all;
   volatile int abort;
 };
 template <int MT>
 constexpr size_t gsmem_bytes() { return sizeof(GSmem<MT>) + 1024; }
-static_assert(2 * (gsmem_bytes<1>() + 1024) <= 228 * 1024 &&
-                  2 * (gsmem_bytes<2>() + 1024) <= 228 * 1024 &&
-                  2 * (gsmem_bytes<4>() + 1024) <= 228 * 1024,
-              "two GEMV CTAs no longer fit on an SM");
+static_assert(gsmem_bytes<1>() <= 232448 && gsmem_bytes<2>() <= 232448 && gsmem_bytes<4>() <= 232448,
+              "GEMV shared memory above the 227 KiB per-CTA limit");
 
 __device__ __forceinline__ float silu_bf16(float g) {   // bf16(g / (1 + exp(-g))), g a bf16 value
   return bf16r(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
 }
 
+// ---- tcgen05 (tensor memory + 5th-generation MMA) helpers
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Shared-memory matrix descriptor: K-major tile written by TMA with the 128-byte swizzle, rows of
+// 128 bytes, 8-row groups 1024 bytes apart (stride byte offset); the leading byte offset is not
+// used by swizzled K-major layouts; version 1 (bits 46-47); layout 2 = 128-byte swizzle (61-63).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), A and B bf16 (7-9, 10-12 =
+// 1), both K-major (15, 16 = 0), N >> 3 (17-22), M >> 4 (24-28).
+__host__ __device__ constexpr uint32_t gemv_idesc(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(kGRows >> 4) << 24);
+}
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the mbarrier when every tcgen05.mma this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+// 16 consecutive fp32 columns of this thread's tensor-memory lane; the wait is in the same
+// statement, so the registers are complete when the statement ends.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* r) {
+  uint32_t v[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];\n\ttcgen05.wait::ld.sync.aligned;"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int j = 0; j < 16; ++j) r[j] = __uint_as_float(v[j]);
+}
+
 template <int MT, int EPI>
-__global__ void __launch_bounds__(kGThreads) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
   constexpr int S = gemv_stages<MT>();
+  constexpr int NM = 16 * MT;                  // the MMA's N: decode rows, padded
+  constexpr uint32_t kCols = 2 * NM;           // two accumulators (32, 64 or 128 columns)
   extern __shared__ unsigned char smem_raw[];
   GSmem<MT>& s = *reinterpret_cast<GSmem<MT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -1663,14 +1736,26 @@ __global__ void __launch_bounds__(kGThreads) gemv_kernel(const __grid_constant__
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(smem_u32(&s.full[i]), 1);
-      mbar_init(smem_u32(&s.empty[i]), kGW);
+      mbar_init(smem_u32(&s.empty[i]), 1);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&s.tfull[b]), 1);
+      mbar_init(smem_u32(&s.tempty[b]), kGEpiWarps);
+    }
+    mbar_init(smem_u32(&s.fin), 1);
     s.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (warp == kGMmaWarp) {
+    tmem_alloc(smem_u32(&s.tmem), kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
   __syncthreads();
-  constexpr uint32_t kStageBytes = (kGBN + 16 * MT) * kGBK * 2;
-  if (warp == kGW) {   // ------------------------------------------------------------ producer
+  tc_fence_after();
+  const uint32_t tmem = s.tmem;
+  constexpr uint32_t kStageBytes = (kGRows + NM) * kGBK * 2;
+  if (warp == kGProducerWarp) {   // --------------------------------------------------- producer
     if (lane == 0) {
       const uint64_t pol = evict_first_policy();
       auto load_w = [&](int i) {
@@ -1680,10 +1765,10 @@ __global__ void __launch_bounds__(kGThreads) gemv_kernel(const __grid_constant__
         const int st = i % S;
         const uint32_t fb = smem_u32(&s.full[st]);
         if (EPI == GEMV_SWIGLU) {   // gate rows, then the up rows N further on
-          tma_load_2d(smem_u32(&s.w[st][0]), &p.tmw, k, tile * 32, fb, pol);
-          tma_load_2d(smem_u32(&s.w[st][32 * kGBK]), &p.tmw, k, p.N + tile * 32, fb, pol);
+          tma_load_2d(smem_u32(&s.w[st][0]), &p.tmw, k, tile * 64, fb, pol);
+          tma_load_2d(smem_u32(&s.w[st][64 * kGBK]), &p.tmw, k, p.N + tile * 64, fb, pol);
         } else {
-          tma_load_2d(smem_u32(&s.w[st][0]), &p.tmw, k, tile * kGBN, fb, pol);
+          tma_load_2d(smem_u32(&s.w[st][0]), &p.tmw, k, tile * kGRows, fb, pol);
         }
       };
       auto load_x = [&](int i) {
@@ -1718,215 +1803,249 @@ __global__ void __launch_bounds__(kGThreads) gemv_kernel(const __grid_constant__
       griddep_wait();
     }
     griddep_launch_dependents();
-    return;
-  }
-  // ---------------------------------------------------------------------------------- consumers
-  griddep_wait();
-  const int mi = lane >> 3, ri = lane & 7;
-  const int wrow = 16 * warp + 8 * (mi >> 1) + ri;   // this lane's W row for ldmatrix
-  const int tid = threadIdx.x, q = tid & 3;
-  // epilogue layout: row r0 + tid / 4, two 8-column segments of the 64-row tile
-  const int sa = EPI == GEMV_SWIGLU ? 8 * q : 16 * q;            // gate (or first) segment
-  const int sb = EPI == GEMV_SWIGLU ? 32 + 8 * q : 16 * q + 8;    // up (or second) segment
-  constexpr int kRows = 16 * MT;
-  int i = 0;   // ring position
-  for (long long u = u0; u < u1;) {
-    const int tile = static_cast<int>(u / p.nchunks);
-    const int a = static_cast<int>(u % p.nchunks);
-    const long long rest = u1 - u;
-    const int b = rest < p.nchunks - a ? a + static_cast<int>(rest) : p.nchunks;
-    const bool first_seg = u == u0;
-    float acc[MT][2][4];
+  } else if (warp == kGMmaWarp) {   // ----------------------------------------------- MMA issue
+    griddep_wait();
+    if (lane == 0) {
+      constexpr uint32_t idesc = gemv_idesc(NM);
+      int i = 0, seg = 0;
+      bool ok = true;
+      for (long long u = u0; ok && u < u1; ++seg) {
+        const int a = static_cast<int>(u % p.nchunks);
+        const long long rest = u1 - u;
+        const int b = rest < p.nchunks - a ? a + static_cast<int>(rest) : p.nchunks;
+        const int buf = seg & 1;
+        if (seg >= 2 && !mbar_wait(smem_u32(&s.tempty[buf]), ((seg >> 1) - 1) & 1, s, p.err, true))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * NM);
+        for (int c = a; c < b; ++c, ++i) {
+          const int st = i % S;
+          if (!mbar_wait(smem_u32(&s.full[st]), (i / S) & 1, s, p.err, true)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t wa = smem_u32(&s.w[st][0]), xa = smem_u32(&s.x[st][0]);
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
-    for (int c = a; c < b; ++c, ++i) {
-      const int st = i % S;
-      mbar_wait(smem_u32(&s.full[st]), (i / S) & 1, s, p.err, true);
-      // each lane spins on its own and may leave the loop at another time: ldmatrix and mma.sync
-      // are .aligned (all 32 lanes together), so reconverge first
-      __syncwarp();
-      const uint32_t wb = smem_u32(&s.w[st][0]) + wrow * 128;
-      const uint32_t xb = smem_u32(&s.x[st][0]);
-#pragma unroll
-      for (int ks = 0; ks < kGBK / 16; ++ks) {
-        uint32_t b00, b01, b10, b11;   // B fragments of the warp's two 8-row groups
-        ldsm_x4(wb + (((2 * ks + (mi & 1)) ^ ri) << 4), b00, b01, b10, b11);
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          const int r = 16 * mt + (lane & 15);
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(xb + r * 128 + (((2 * ks + (lane >> 4)) ^ (r & 7)) << 4), a0, a1, a2, a3);
-          mma16816_full(acc[mt][0], a0, a1, a2, a3, b00, b01);
-          mma16816_full(acc[mt][1], a0, a1, a2, a3, b10, b11);
+          for (int ks = 0; ks < kGBK / 16; ++ks)
+            umma_bf16(d, sw128_desc(wa + 32 * ks), sw128_desc(xa + 32 * ks), idesc,
+                      (c > a || ks > 0) ? 1u : 0u);
+          umma_commit(smem_u32(&s.empty[st]));   // the stage is free once these MMAs read it
         }
+        if (!ok) break;
+        umma_commit(smem_u32(&s.tfull[buf]));   // the accumulator is complete
+        u += b - a;
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&s.empty[st]));
+      umma_commit(smem_u32(&s.fin));   // every MMA issued has completed: tensor memory may go
+      mbar_wait(smem_u32(&s.fin), 0, s, p.err, false);
     }
-    u += b - a;
-    if (u >= u1) griddep_launch_dependents();
-    // ---- the segment's fp32 sums to shared memory: rows 16 mt + lane / 4 (+ 8), W rows
-    // 16 warp + 8 nt + 2 (lane % 4) + {0, 1}
-    named_bar(1, kGW * 32);   // the previous segment's epilogue is done with ct
+    __syncwarp();
+    griddep_launch_dependents();
+  } else {   // ------------------------------------------------------------- epilogue warps 0-3
+    griddep_wait();
+    const int tid = threadIdx.x, q = tid & 3;
+    // epilogue layout: row r0 + tid / 4, two 16-column segments of the tile
+    const int sa = EPI == GEMV_SWIGLU ? 16 * q : 32 * q;            // gate (or first) segment
+    const int sb = EPI == GEMV_SWIGLU ? 64 + 16 * q : 32 * q + 16;   // up (or second) segment
+    int seg = 0;
+    for (long long u = u0; u < u1; ++seg) {
+      const int tile = static_cast<int>(u / p.nchunks);
+      const int a = static_cast<int>(u % p.nchunks);
+      const long long rest = u1 - u;
+      const int b = rest < p.nchunks - a ? a + static_cast<int>(rest) : p.nchunks;
+      const bool first_seg = u == u0;
+      const int buf = seg & 1;
+      mbar_wait(smem_u32(&s.tfull[buf]), (seg >> 1) & 1, s, p.err, true);
+      __syncwarp();   // tcgen05.ld is .aligned: the lanes leave the bounded spin at other times
+      tc_fence_after();
+      float r[NM];    // D[weight row 32 warp + lane][decode rows 0 .. NM)
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+      for (int c = 0; c < NM; c += 16)
+        tmem_ld16(tmem + (static_cast<uint32_t>(32 * warp) << 16) + static_cast<uint32_t>(buf * NM + c),
+                  r + c);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&s.tempty[buf]));
+      u += b - a;
+      if (u >= u1) griddep_launch_dependents();
+      named_bar(1, kGEpiWarps * 32);   // the previous segment's epilogue is done with ct
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+      for (int j = 0; j < NM; ++j) s.ct[j][32 * warp + lane] = r[j];
+      named_bar(1, kGEpiWarps * 32);
+      // ---- a tile split between CTAs: partial out, the last arriver adds the segments
+      const bool whole = a == 0 && b == p.nchunks;
+      const long long tu0 = static_cast<long long>(tile) * p.nchunks;
+      const int kfirst = static_cast<int>(tu0 / p.per);                    // CTAs holding the tile
+      const int klast = static_cast<int>((tu0 + p.nchunks - 1) / p.per);
+      if (!whole) {
+        const int slot = 2 * blockIdx.x + (first_seg ? 0 : 1);
+        for (int r0 = 0; r0 < NM; r0 += 32) {
+          const int m = r0 + (tid >> 2);
+          if (m < NM && m < p.M) {
+            float* dst = p.part + (static_cast<long long>(slot) * p.M + m) * kGRows;
+            const float* src = &s.ct[m][0];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-          *reinterpret_cast<float2*>(&s.ct[16 * mt + 8 * h + (lane >> 2)]
-                                          [16 * warp + 8 * nt + 2 * (lane & 3)]) =
-              make_float2(acc[mt][nt][2 * h], acc[mt][nt][2 * h + 1]);
-    named_bar(1, kGW * 32);
-    // ---- a tile split between CTAs: partial out, the last arriver adds the segments
-    const bool whole = a == 0 && b == p.nchunks;
-    const long long tu0 = static_cast<long long>(tile) * p.nchunks;
-    const int kfirst = static_cast<int>(tu0 / p.per);                    // CTAs holding the tile
-    const int klast = static_cast<int>((tu0 + p.nchunks - 1) / p.per);
-    if (!whole) {
-      const int slot = 2 * blockIdx.x + (first_seg ? 0 : 1);
-      for (int r0 = 0; r0 < kRows; r0 += 32) {
+            for (int j = 0; j < 16; j += 4) {
+              __stcg(reinterpret_cast<float4*>(dst + sa + j), *reinterpret_cast<const float4*>(src + sa + j));
+              __stcg(reinterpret_cast<float4*>(dst + sb + j), *reinterpret_cast<const float4*>(src + sb + j));
+            }
+          }
+        }
+        __threadfence();
+        named_bar(1, kGEpiWarps * 32);
+        if (tid == 0) {
+          s.last = atomicAdd(&p.cnt[tile], 1) == klast - kfirst;
+          if (s.last) __threadfence();   // acquire the other segments' partials
+        }
+        named_bar(1, kGEpiWarps * 32);
+        if (!s.last) continue;
+        if (tid == 0) atomicExch(&p.cnt[tile], 0);
+      }
+      const int tcol = EPI == GEMV_SWIGLU ? tile * 64 : tile * kGRows;   // first output column
+      // SWIGLU covers its 64 columns whole (N % 64 == 0); otherwise a 16-column segment is
+      // either inside N or past it (N % 16 == 0)
+      const bool va = EPI == GEMV_SWIGLU || tcol + sa < p.N;
+      const bool vb = EPI == GEMV_SWIGLU || tcol + sb < p.N;
+      for (int r0 = 0; r0 < NM; r0 += 32) {
         const int m = r0 + (tid >> 2);
-        if (m < kRows && m < p.M) {
-          float* dst = p.part + (static_cast<long long>(slot) * p.M + m) * kGBN;
-          const float* src = &s.ct[m][0];
+        const bool act = m < NM && m < p.M;
+        if (EPI != GEMV_ARGMAX && !act) continue;   // ARGMAX: every lane takes part in the shuffles
+        float v[32];
+        if (!act) {
 #pragma unroll
-          for (int j = 0; j < 8; j += 4) {
-            __stcg(reinterpret_cast<float4*>(dst + sa + j), *reinterpret_cast<const float4*>(src + sa + j));
-            __stcg(reinterpret_cast<float4*>(dst + sb + j), *reinterpret_cast<const float4*>(src + sb + j));
+          for (int j = 0; j < 32; ++j) v[j] = -INFINITY;
+        } else if (!whole) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+#pragma unroll 2
+          for (int k = kfirst; k <= klast; ++k) {   // fixed order: the tile's first CTA first
+            const bool kfirst_seg = static_cast<long long>(k) * p.per >= tu0;
+            const float* src =
+                p.part + (static_cast<long long>(2 * k + (kfirst_seg ? 0 : 1)) * p.M + m) * kGRows;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src + sa + j));
+              const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + sb + j));
+              v[j] += x0.x; v[j + 1] += x0.y; v[j + 2] += x0.z; v[j + 3] += x0.w;
+              v[16 + j] += x1.x; v[17 + j] += x1.y; v[18 + j] += x1.z; v[19 + j] += x1.w;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            v[j] = s.ct[m][sa + j];
+            v[16 + j] = s.ct[m][sb + j];
+          }
+        }
+        const long long row = static_cast<long long>(m) * p.N + tcol;
+        if (EPI == GEMV_F32) {
+          float* y = static_cast<float*>(p.y) + row;
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            if (va) *reinterpret_cast<float4*>(y + sa + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            if (vb)
+              *reinterpret_cast<float4*>(y + sb + j) =
+                  make_float4(v[16 + j], v[17 + j], v[18 + j], v[19 + j]);
+          }
+        } else if (EPI == GEMV_BF16) {
+          bf16* y = static_cast<bf16*>(p.y) + row;
+#pragma unroll
+          for (int seg2 = 0; seg2 < 2; ++seg2) {
+            if (!(seg2 == 0 ? va : vb)) continue;
+            uint4 o0, o1;
+            uint32_t* p0 = reinterpret_cast<uint32_t*>(&o0);
+            uint32_t* p1 = reinterpret_cast<uint32_t*>(&o1);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              p0[e] = pack_bf16(v[16 * seg2 + 2 * e], v[16 * seg2 + 2 * e + 1]);
+              p1[e] = pack_bf16(v[16 * seg2 + 8 + 2 * e], v[16 * seg2 + 9 + 2 * e]);
+            }
+            bf16* dst = y + (seg2 == 0 ? sa : sb);
+            *reinterpret_cast<uint4*>(dst) = o0;
+            *reinterpret_cast<uint4*>(dst + 8) = o1;
+          }
+        } else if (EPI == GEMV_RESID) {   // h <- bf16(h + bf16(acc)) (gemv.py:95-97)
+          bf16* h = static_cast<bf16*>(p.y) + row;
+#pragma unroll
+          for (int seg2 = 0; seg2 < 2; ++seg2) {
+            if (!(seg2 == 0 ? va : vb)) continue;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              bf16* hp = h + (seg2 == 0 ? sa : sb) + 8 * half;
+              uint4 hv = *reinterpret_cast<const uint4*>(hp);
+              uint32_t* ph = reinterpret_cast<uint32_t*>(&hv);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = bf2f(ph[e]);
+                const int j = 16 * seg2 + 8 * half + 2 * e;
+                ph[e] = pack_bf16(__fadd_rn(f.x, bf16r(v[j])), __fadd_rn(f.y, bf16r(v[j + 1])));
+              }
+              *reinterpret_cast<uint4*>(hp) = hv;
+            }
+          }
+        } else if (EPI == GEMV_ARGMAX) {
+          // this thread's 32 columns, then the row's 4 threads, then all tiles through one 64-bit
+          // atomicMax per row: key = (order-preserving bits of the bf16 logit) << 32 | ~index, so
+          // the larger logit wins and, on equal logits, the smaller index
+          float best = -INFINITY;
+          int bi = 0x7fffffff;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int col = tcol + (j < 16 ? sa + j : sb + j - 16);
+            const float l = bf16r(v[j]) + 0.0f;   // -0 -> +0: equal logits compare equal
+            if (col < p.N && (l > best || (l == best && col < bi))) {
+              best = l;
+              bi = col;
+            }
+          }
+          const uint32_t ub = __float_as_uint(best);
+          const uint32_t ord = (ub & 0x80000000u) ? ~ub : (ub | 0x80000000u);
+          unsigned long long key = (static_cast<unsigned long long>(ord) << 32) |
+                                   static_cast<uint32_t>(0xffffffffu - static_cast<uint32_t>(bi));
+          key = max(key, __shfl_xor_sync(0xffffffffu, key, 1));
+          key = max(key, __shfl_xor_sync(0xffffffffu, key, 2));
+          if (q == 0 && act) atomicMax(p.keys + m, key);
+        } else {   // SWIGLU: output columns 64 tile + 16 q .. + 16 (gemv.py:101-105)
+          bf16* y = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + tcol + 16 * q;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint4 o;
+            uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j = 8 * half + 2 * e;
+              const float s0 = silu_bf16(bf16r(v[j])), s1 = silu_bf16(bf16r(v[j + 1]));
+              po[e] = pack_bf16(__fmul_rn(s0, bf16r(v[16 + j])), __fmul_rn(s1, bf16r(v[17 + j])));
+            }
+            *reinterpret_cast<uint4*>(y + 8 * half) = o;
           }
         }
       }
-      __threadfence();
-      named_bar(1, kGW * 32);
-      if (tid == 0) {
-        s.last = atomicAdd(&p.cnt[tile], 1) == klast - kfirst;
-        if (s.last) __threadfence();   // acquire the other segments' partials
-      }
-      named_bar(1, kGW * 32);
-      if (!s.last) continue;
-      if (tid == 0) atomicExch(&p.cnt[tile], 0);
-    }
-    for (int r0 = 0; r0 < kRows; r0 += 32) {
-      const int m = r0 + (tid >> 2);
-      const bool act = m < kRows && m < p.M;
-      if (EPI != GEMV_ARGMAX && !act) continue;   // ARGMAX: every lane takes part in the shuffles
-      float v[16];
-      if (!act) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = -INFINITY;
-      } else if (!whole) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0.f;
-        for (int k = kfirst; k <= klast; ++k) {   // fixed order: the tile's first CTA first
-          const bool kfirst_seg = static_cast<long long>(k) * p.per >= tu0;
-          const float* src = p.part + (static_cast<long long>(2 * k + (kfirst_seg ? 0 : 1)) * p.M + m) * kGBN;
-#pragma unroll
-          for (int j = 0; j < 8; j += 4) {
-            const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src + sa + j));
-            const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + sb + j));
-            v[j] += x0.x; v[j + 1] += x0.y; v[j + 2] += x0.z; v[j + 3] += x0.w;
-            v[8 + j] += x1.x; v[9 + j] += x1.y; v[10 + j] += x1.z; v[11 + j] += x1.w;
+      if (EPI == GEMV_ARGMAX) {   // the tile that finishes last turns the keys into token ids
+        __threadfence();
+        named_bar(1, kGEpiWarps * 32);
+        if (tid == 0) {
+          s.last_all = atomicAdd(&p.cnt[p.tiles], 1) == p.tiles - 1;
+          if (s.last_all) __threadfence();
+        }
+        named_bar(1, kGEpiWarps * 32);
+        if (s.last_all) {
+          if (tid < p.M) {
+            const unsigned long long key = atomicExch(p.keys + tid, 0ull);   // read and re-arm
+            static_cast<long long*>(p.y)[tid] =
+                static_cast<long long>(0xffffffffu - static_cast<uint32_t>(key & 0xffffffffu));
           }
+          if (tid == 0) atomicExch(&p.cnt[p.tiles], 0);
         }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          v[j] = s.ct[m][sa + j];
-          v[8 + j] = s.ct[m][sb + j];
-        }
-      }
-      const long long pcol = static_cast<long long>(tile) * kGBN;
-      if (EPI == GEMV_F32) {
-        float* y = static_cast<float*>(p.y) + static_cast<long long>(m) * p.N + pcol;
-#pragma unroll
-        for (int j = 0; j < 8; j += 4) {
-          *reinterpret_cast<float4*>(y + sa + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-          *reinterpret_cast<float4*>(y + sb + j) =
-              make_float4(v[8 + j], v[9 + j], v[10 + j], v[11 + j]);
-        }
-      } else if (EPI == GEMV_BF16) {
-        bf16* y = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + pcol;
-        uint4 o0, o1;
-        uint32_t* p0 = reinterpret_cast<uint32_t*>(&o0);
-        uint32_t* p1 = reinterpret_cast<uint32_t*>(&o1);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          p0[e] = pack_bf16(v[2 * e], v[2 * e + 1]);
-          p1[e] = pack_bf16(v[8 + 2 * e], v[9 + 2 * e]);
-        }
-        *reinterpret_cast<uint4*>(y + sa) = o0;
-        *reinterpret_cast<uint4*>(y + sb) = o1;
-      } else if (EPI == GEMV_RESID) {   // h <- bf16(h + bf16(acc)) (gemv.py:95-97)
-        bf16* h = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + pcol;
-#pragma unroll
-        for (int seg = 0; seg < 2; ++seg) {
-          bf16* hp = h + (seg == 0 ? sa : sb);
-          uint4 hv = *reinterpret_cast<const uint4*>(hp);
-          uint32_t* ph = reinterpret_cast<uint32_t*>(&hv);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = bf2f(ph[e]);
-            ph[e] = pack_bf16(__fadd_rn(f.x, bf16r(v[8 * seg + 2 * e])),
-                              __fadd_rn(f.y, bf16r(v[8 * seg + 2 * e + 1])));
-          }
-          *reinterpret_cast<uint4*>(hp) = hv;
-        }
-      } else if (EPI == GEMV_ARGMAX) {
-        // this thread's 16 columns, then the row's 4 threads, then all tiles through one 64-bit
-        // atomicMax per row: key = (order-preserving bits of the bf16 logit) << 32 | ~index, so
-        // the larger logit wins and, on equal logits, the smaller index
-        float best = -INFINITY;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float l = bf16r(v[j]) + 0.0f;   // -0 -> +0: equal logits compare equal
-          const int col = static_cast<int>(pcol) + (j < 8 ? sa + j : sb + j - 8);
-          if (l > best || (l == best && col < bi)) {
-            best = l;
-            bi = col;
-          }
-        }
-        const uint32_t ub = __float_as_uint(best);
-        const uint32_t ord = (ub & 0x80000000u) ? ~ub : (ub | 0x80000000u);
-        unsigned long long key = (static_cast<unsigned long long>(ord) << 32) |
-                                 static_cast<uint32_t>(0xffffffffu - static_cast<uint32_t>(bi));
-        key = max(key, __shfl_xor_sync(0xffffffffu, key, 1));
-        key = max(key, __shfl_xor_sync(0xffffffffu, key, 2));
-        if (q == 0 && act) atomicMax(p.keys + m, key);
-      } else {   // SWIGLU: output columns 32 tile + 8 q .. + 8 (gemv.py:101-105)
-        bf16* y = static_cast<bf16*>(p.y) + static_cast<long long>(m) * p.N + tile * 32 + 8 * q;
-        uint4 o;
-        uint32_t* po = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float s0 = silu_bf16(bf16r(v[2 * e])), s1 = silu_bf16(bf16r(v[2 * e + 1]));
-          po[e] = pack_bf16(__fmul_rn(s0, bf16r(v[8 + 2 * e])), __fmul_rn(s1, bf16r(v[9 + 2 * e])));
-        }
-        *reinterpret_cast<uint4*>(y) = o;
-      }
-    }
-    if (EPI == GEMV_ARGMAX) {   // the tile that finishes last turns the keys into token ids
-      __threadfence();
-      named_bar(1, kGW * 32);
-      if (tid == 0) {
-        s.last_all = atomicAdd(&p.cnt[p.tiles], 1) == p.tiles - 1;
-        if (s.last_all) __threadfence();
-      }
-      named_bar(1, kGW * 32);
-      if (s.last_all) {
-        if (tid < p.M) {
-          const unsigned long long key = atomicExch(p.keys + tid, 0ull);   // read and re-arm
-          static_cast<long long*>(p.y)[tid] =
-              static_cast<long long>(0xffffffffu - static_cast<uint32_t>(key & 0xffffffffu));
-        }
-        if (tid == 0) atomicExch(&p.cnt[p.tiles], 0);
       }
     }
+  }
+  // ---- tensor memory goes back once every MMA has completed and every load from it is done
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kGMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kCols);
   }
 }
 
@@ -2147,14 +2266,14 @@ int launch_verify(const kopt_plan* plan, Params& p, void* stream) {
 
 // ------------------------------------------------------------------------------- GEMV host side
 // Workspace: [0, 256) the error word; one arrival counter per tile and one for tiles done; the
-// ARGMAX keys of up to 64 rows; then two fp32 segment partials [M][64] per CTA.
+// ARGMAX keys of up to 64 rows; then two fp32 segment partials [M][128] per CTA.
 struct GemvWs { int64_t cnt, keys, part, total; };
 GemvWs gemv_ws_layout(int M, int tiles, int grid) {
   GemvWs w;
   w.cnt = kHeaderBytes;
   w.keys = w.cnt + (static_cast<int64_t>(tiles + 1) * 4 + 255) / 256 * 256;
   w.part = w.keys + 64 * 8;
-  w.total = w.part + 2 * static_cast<int64_t>(grid) * M * kGBN * 4;
+  w.total = w.part + 2 * static_cast<int64_t>(grid) * M * kGRows * 4;
   return w;
 }
 inline int gemv_mt(int M) { return M <= 16 ? 1 : M <= 32 ? 2 : 4; }
@@ -2277,7 +2396,7 @@ int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int target_cta
   if (plan == nullptr || M < 1 || M > 64 || K < 8 || K % 8 != 0 || N < 1 || epi < GEMV_F32 ||
       epi > GEMV_ARGMAX || target_ctas < 0)
     return KOPT_ERR_ARG;
-  if (N % (epi == GEMV_SWIGLU ? 32 : kGBN) != 0) return KOPT_ERR_ARG;
+  if (N % (epi == GEMV_SWIGLU ? 64 : 16) != 0) return KOPT_ERR_ARG;
   int rc = set_device(device);
   if (rc) return rc;
   int occ = 0, sms = 0;
@@ -2286,7 +2405,7 @@ int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int target_cta
   if (occ < 1) return KOPT_ERR_CUDA;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
     return KOPT_ERR_CUDA;
-  const int tiles = epi == GEMV_SWIGLU ? N / 32 : N / kGBN;
+  const int tiles = epi == GEMV_SWIGLU ? N / 64 : (N + kGRows - 1) / kGRows;
   const int nchunks = (K + kGBK - 1) / kGBK;
   const long long units = static_cast<long long>(tiles) * nchunks;
   // one resident wave: every CTA streams one equal run of units
@@ -2328,7 +2447,7 @@ int kopt_gemv(const kopt_gemv_plan* plan, const void* x, const void* w, void* y,
                                static_cast<cuuint64_t>(plan->N) * (glu ? 2 : 1)};
   const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(plan->K), static_cast<cuuint64_t>(plan->M)};
   const cuuint64_t stride[1] = {static_cast<cuuint64_t>(plan->K) * 2};
-  const cuuint32_t wbox[2] = {kGBK, glu ? 32u : static_cast<cuuint32_t>(kGBN)};
+  const cuuint32_t wbox[2] = {kGBK, glu ? 64u : static_cast<cuuint32_t>(kGRows)};
   const cuuint32_t xbox[2] = {kGBK, static_cast<cuuint32_t>(16 * mt)};
   if (enc(&p.tmw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(w), wdims, stride, wbox,
           elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -83,8 +83,8 @@ def test_launchers_reject_null_arguments(lib):
 @pytest.mark.parametrize("args", [
     (0, 0, 64, 64, 1, 0),       # no rows
     (0, 65, 64, 64, 1, 0),      # more rows than the kernel's 64
-    (0, 8, 96, 64, 1, 0),       # N not a multiple of the 64-row weight tile
-    (0, 8, 48, 64, 3, 0),       # SWIGLU N not a multiple of 32
+    (0, 8, 100, 64, 1, 0),      # N not a multiple of 16 (16-column output segments)
+    (0, 8, 48, 64, 3, 0),       # SWIGLU N not a multiple of 64 (gate/up tile halves)
     (0, 8, 64, 60, 1, 0),       # K not a multiple of 8 (TMA row stride)
     (0, 8, 64, 64, 5, 0),       # unknown epilogue
     (0, 8, 64, 64, 1, -1),      # negative split

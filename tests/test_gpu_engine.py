@@ -35,12 +35,16 @@ def small_model(tmp_path_factory):
     return path
 
 
-def test_generate_passes_the_reference_quality_rule(small_model):
-    eng = Engine(str(small_model), DEV)
+@pytest.mark.parametrize("gemv", [False, True], ids=["cublas", "kopt_gemv"])
+def test_generate_passes_the_reference_quality_rule(small_model, gemv):
+    """Both projection paths: cuBLAS GEMMs with the epilogue kernels, and the skinny-GEMM kernel
+    with residual / SwiGLU / LM-head argmax epilogues."""
+    eng = Engine(str(small_model), DEV, gemv=gemv)
     g = torch.Generator().manual_seed(1)
     B, S, N = 4, 96, 64
     prompts = torch.randint(0, 4096, (B, S), generator=g)
     steps = list(eng.generate(prompts.tolist(), N))
+    assert (eng.gemv is not None) == gemv
     assert len(steps) == N and all(len(s) == B for s in steps)
     assert eng.read_error() == 0
     generated = torch.tensor(steps).t()                      # [B, N]

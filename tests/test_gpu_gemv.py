@@ -79,7 +79,8 @@ def _check(got, x, w, h, epi):
 
 
 # Qwen3-4B decode shapes at batch 32 (qkv, o, gate|up, down) and edge cases: one row, rows not a
-# multiple of 16, 64 rows (4 row tiles), K not a multiple of the 64-wide chunk, a single tile.
+# multiple of 16, 64 rows, K not a multiple of the 64-wide chunk, a single tile, N not a multiple
+# of the 128-row weight tile (the last tile's rows past N are read as zero and not stored).
 CASES = [
     (32, 6144, 2560, EPI_BF16),
     (32, 2560, 4096, EPI_RESID),
@@ -89,8 +90,9 @@ CASES = [
     (5, 64, 64, EPI_F32),
     (17, 128, 200, EPI_BF16),
     (64, 192, 512, EPI_F32),
-    (64, 96, 1024, EPI_SWIGLU),
-    (3, 32, 136, EPI_SWIGLU),
+    (64, 128, 1024, EPI_SWIGLU),
+    (3, 64, 136, EPI_SWIGLU),
+    (9, 336, 512, EPI_RESID),
     (16, 512, 2048, EPI_RESID),
 ]
 
