@@ -60,9 +60,9 @@ def parse_args():
     ap.add_argument("--no-overlap", action="store_true",
                     help="launch without programmatic dependent launch (each call waits for the "
                          "previous kernel before it starts)")
-    ap.add_argument("--gemv", action="store_true",
-                    help="c5: the skinny-GEMM projections with fused epilogues (kopt_gemv) instead "
-                         "of cuBLAS GEMMs + separate SwiGLU / residual kernels")
+    ap.add_argument("--no-gemv", action="store_true",
+                    help="c5: cuBLAS GEMMs + separate SwiGLU / residual kernels instead of the "
+                         "tcgen05 skinny-GEMM projections with fused epilogues (kopt_gemv)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--soak-ms", type=float, default=600.0,
@@ -509,7 +509,7 @@ def run_engine(args):
     model = random_model(QWEN3_4B["layers"], QWEN3_4B["hidden"], QWEN3_4B["intermediate"],
                          QWEN3_4B["vocab"], seed=0, device=dev)
     eng = Engine.from_model(model, dev, group=dist.group.WORLD if dist is not None else None,
-                            overlap=not args.no_overlap, gemv=args.gemv)
+                            overlap=not args.no_overlap, gemv=not args.no_gemv)
     g = torch.Generator().manual_seed(5)
     prompts = torch.randint(0, QWEN3_4B["vocab"], (B, S), generator=g).tolist()
     for _ in range(max(1, args.warmup)):

@@ -1878,19 +1878,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constan
       const int kfirst = static_cast<int>(tu0 / p.per);                    // CTAs holding the tile
       const int klast = static_cast<int>((tu0 + p.nchunks - 1) / p.per);
       if (!whole) {
+        // partial out and, for the last arriver, the segments' sum back into ct, both with a warp
+        // on whole 512-byte rows (lane l: columns 4l .. 4l + 3; warp w: rows w, w + 4, ...)
         const int slot = 2 * blockIdx.x + (first_seg ? 0 : 1);
-        for (int r0 = 0; r0 < NM; r0 += 32) {
-          const int m = r0 + (tid >> 2);
-          if (m < NM && m < p.M) {
-            float* dst = p.part + (static_cast<long long>(slot) * p.M + m) * kGRows;
-            const float* src = &s.ct[m][0];
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              __stcg(reinterpret_cast<float4*>(dst + sa + j), *reinterpret_cast<const float4*>(src + sa + j));
-              __stcg(reinterpret_cast<float4*>(dst + sb + j), *reinterpret_cast<const float4*>(src + sb + j));
-            }
-          }
-        }
+        const int rows = NM < p.M ? NM : p.M;
+        for (int m = warp; m < rows; m += kGEpiWarps)
+          __stcg(reinterpret_cast<float4*>(p.part + (static_cast<long long>(slot) * p.M + m) * kGRows) + lane,
+                 *reinterpret_cast<const float4*>(&s.ct[m][4 * lane]));
         __threadfence();
         named_bar(1, kGEpiWarps * 32);
         if (tid == 0) {
@@ -1900,6 +1894,48 @@ __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constan
         named_bar(1, kGEpiWarps * 32);
         if (!s.last) continue;
         if (tid == 0) atomicExch(&p.cnt[tile], 0);
+        constexpr int kR = (NM + kGEpiWarps - 1) / kGEpiWarps;   // rows per warp
+        float4 acc4[kR];
+#pragma unroll
+        for (int r = 0; r < kR; ++r) acc4[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        // segments in a fixed order (the tile's first CTA first), KP of them per round so that
+        // KP x kR loads are in flight together
+        constexpr int KP = kR <= 8 ? 2 : 1;
+        auto seg_src = [&](int k) {
+          const bool kfirst_seg = static_cast<long long>(k) * p.per >= tu0;
+          return reinterpret_cast<const float4*>(
+              p.part + static_cast<long long>(2 * k + (kfirst_seg ? 0 : 1)) * p.M * kGRows);
+        };
+        for (int k = kfirst; k <= klast; k += KP) {
+          float4 x4[KP][kR];
+#pragma unroll
+          for (int j = 0; j < KP; ++j) {
+            const bool have = k + j <= klast;
+            const float4* src = seg_src(have ? k + j : k);
+#pragma unroll
+            for (int r = 0; r < kR; ++r) {
+              const int m = warp + kGEpiWarps * r;
+              x4[j][r] = have && m < rows
+                             ? __ldcg(src + static_cast<long long>(m) * (kGRows / 4) + lane)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < KP; ++j)
+#pragma unroll
+            for (int r = 0; r < kR; ++r) {
+              acc4[r].x += x4[j][r].x;
+              acc4[r].y += x4[j][r].y;
+              acc4[r].z += x4[j][r].z;
+              acc4[r].w += x4[j][r].w;
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kR; ++r) {
+          const int m = warp + kGEpiWarps * r;
+          if (m < rows) *reinterpret_cast<float4*>(&s.ct[m][4 * lane]) = acc4[r];
+        }
+        named_bar(1, kGEpiWarps * 32);
       }
       const int tcol = EPI == GEMV_SWIGLU ? tile * 64 : tile * kGRows;   // first output column
       // SWIGLU covers its 64 columns whole (N % 64 == 0); otherwise a 16-column segment is
@@ -1914,22 +1950,6 @@ __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constan
         if (!act) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = -INFINITY;
-        } else if (!whole) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.f;
-#pragma unroll 2
-          for (int k = kfirst; k <= klast; ++k) {   // fixed order: the tile's first CTA first
-            const bool kfirst_seg = static_cast<long long>(k) * p.per >= tu0;
-            const float* src =
-                p.part + (static_cast<long long>(2 * k + (kfirst_seg ? 0 : 1)) * p.M + m) * kGRows;
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src + sa + j));
-              const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + sb + j));
-              v[j] += x0.x; v[j + 1] += x0.y; v[j + 2] += x0.z; v[j + 3] += x0.w;
-              v[16 + j] += x1.x; v[17 + j] += x1.y; v[18 + j] += x1.z; v[19 + j] += x1.w;
-            }
-          }
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {

@@ -39,7 +39,7 @@ from .shard import head_range, shard_qkv_weight
 
 class Engine:
     def __init__(self, model_path: str, device: str = "cuda:0", group=None, overlap: bool = True,
-                 gemv: bool = False):
+                 gemv: bool = True):
         from transformers import AutoModelForCausalLM
         model = AutoModelForCausalLM.from_pretrained(
             model_path, dtype=torch.bfloat16, attn_implementation="sdpa", local_files_only=True)
@@ -47,14 +47,14 @@ class Engine:
 
     @classmethod
     def from_model(cls, model, device: str = "cuda:0", group=None,
-                   overlap: bool = True, gemv: bool = False) -> "Engine":
+                   overlap: bool = True, gemv: bool = True) -> "Engine":
         """Wrap an already loaded Qwen3ForCausalLM (bf16, sdpa) instead of reading a checkpoint."""
         self = cls.__new__(cls)
         self._init(model.eval().to(device), device, group, overlap, gemv)
         return self
 
     # ------------------------------------------------------------------ construction
-    def _init(self, model, device, group, overlap=True, gemv=False):
+    def _init(self, model, device, group, overlap=True, gemv=True):
         torch.backends.cuda.matmul.allow_tf32 = False
         self.device = torch.device(device)
         if self.device.type != "cuda":
