@@ -19,6 +19,9 @@ e2e: the same metric through the public call with host buffers: each step copies
 qkv and positions from pinned host memory, runs the step and copies the output back.
 --impl reference: the reference's CPU path (Transformers' q/k norm + RoPE + sdpa, oracle/cpu_path.py)
 on the same config, rank 0 only.
+
+Other workloads: c3/c4 (longer contexts), v3/v5/v7 (the T > 1 verify step), c5 (the engine end to
+end, tokens/s) and p5 (the projections of one decode step on the skinny-GEMM kernel, TB/s).
 """
 
 from __future__ import annotations
@@ -51,7 +54,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "v3", "v5", "v7"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "v3", "v5", "v7", "p5"], default="c2",
                     help="c2-c4: one decode-attention call per step; c5: the engine end to end")
     ap.add_argument("--layers", type=int, default=8, help="layer caches rotated across steps")
     ap.add_argument("--layout", choices=["paged", "contiguous"], default="paged")
@@ -60,6 +63,9 @@ def parse_args():
     ap.add_argument("--no-overlap", action="store_true",
                     help="launch without programmatic dependent launch (each call waits for the "
                          "previous kernel before it starts)")
+    ap.add_argument("--p5-layers", type=int, default=36,
+                    help="p5: transformer layers in the step (36 = Qwen3-4B; fewer for a small "
+                         "profiling case)")
     ap.add_argument("--no-gemv", action="store_true",
                     help="c5: cuBLAS GEMMs + separate SwiGLU / residual kernels instead of the "
                          "tcgen05 skinny-GEMM projections with fused epilogues (kopt_gemv)")
@@ -493,6 +499,172 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------- p5: a decode step's projections
+P5_METRIC = "decode-step projections achieved HBM TB/s (kopt_gemv, Qwen3-4B, B=32)"
+
+
+def run_proj(args):
+    """Workload p5: the projections of one Qwen3-4B decode step at B = 32 rows, on the skinny-GEMM
+    kernel with the reference's epilogues (engine.py:259-263): per layer QKV (bf16 out), o_proj
+    (residual add), gate|up (SwiGLU) and down_proj (residual add), 36 layers with their own
+    weights, then the LM head with the greedy argmax. Random weights (std 0.02, seeded), random
+    inputs; the step is one CUDA graph of its 145 launches, replayed; consecutive launches overlap
+    by programmatic dependent launch. value: weight + activation bytes per step / device time.
+    N > 1: independent replicas (the projections are replicated in the sharded engine)."""
+    from kernel_optim_b200.checkpoint import QWEN3_4B
+    from kernel_optim_b200.gemv import EPI_ARGMAX, EPI_BF16, EPI_RESID, EPI_SWIGLU, Gemv
+    world, rank, local = dist_env()
+    dist = init_dist(world, local)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, H, I, V, L = 32, QWEN3_4B["hidden"], QWEN3_4B["intermediate"], QWEN3_4B["vocab"], args.p5_layers
+    NQKV, NATT = 32 * 128 + 2 * 8 * 128, 32 * 128
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rnd(*shape, std=0.02):
+        return (torch.randn(*shape, generator=g, device=dev) * std).to(bf)
+
+    W = [dict(qkv=rnd(NQKV, H), o=rnd(H, NATT), gu=rnd(2 * I, H), down=rnd(H, I)) for _ in range(L)]
+    lm = rnd(V, H)
+    xn, attn = rnd(B, H, std=1.0), rnd(B, NATT, std=1.0)
+    h = rnd(B, H, std=1.0)
+    qkv = torch.empty(B, NQKV, dtype=bf, device=dev)
+    act = torch.empty(B, I, dtype=bf, device=dev)
+    ids = torch.empty(B, dtype=torch.int64, device=dev)
+    ov = not args.no_overlap
+    G = dict(qkv=Gemv(B, NQKV, H, EPI_BF16, device=dev, overlap_prev=ov),
+             o=Gemv(B, H, NATT, EPI_RESID, device=dev, overlap_prev=ov),
+             gu=Gemv(B, I, H, EPI_SWIGLU, device=dev, overlap_prev=ov),
+             down=Gemv(B, H, I, EPI_RESID, device=dev, overlap_prev=ov),
+             lm=Gemv(B, V, H, EPI_ARGMAX, device=dev, overlap_prev=ov))
+    launches = 4 * L + 1
+
+    def step(x=xn):
+        for w in W:
+            G["qkv"](x, w["qkv"], qkv)
+            G["o"](attn, w["o"], h=h)
+            G["gu"](x, w["gu"], act)
+            G["down"](act, w["down"], h=h)
+        G["lm"](x, lm, ids)
+
+    wbytes = sum(t.numel() * 2 for w in W for t in w.values()) + lm.numel() * 2
+    # activations: x read once per weight tile would be an L2 effect; count each input row block
+    # once per projection and every output (h read and written by the residual epilogues)
+    abytes = L * (B * H * 2 * 2 + B * NATT * 2 + B * I * 2 * 2 + B * NQKV * 2 + 4 * B * H * 2) + B * H * 2 + B * 8
+    bytes_step = wbytes + abytes
+
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(max(1, args.warmup)):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    t_end = time.perf_counter() + args.soak_ms / 1e3
+    while time.perf_counter() < t_end:
+        graph.replay()
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms_step = max_over_ranks(dist, e0.elapsed_time(e1)) / args.steps
+    errs = {k: op.read_error() for k, op in G.items()}
+    if any(errs.values()):
+        raise RuntimeError(f"device error words {errs}")
+    value = world * bytes_step / (ms_step * 1e-3) / 1e12
+    peak, peak_src = peaks()
+    achieved = bytes_step / (ms_step * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": ncu_traffic("p5"),
+                "peak_source": peak_src,
+                "kernel": f"gemv_kernel<MT=2, EPI> (every launch of the step: {launches} per step)",
+                "algorithmic_bytes_per_step": bytes_step, "weight_bytes_per_step": wbytes}
+
+    e2e = None
+    if not args.no_e2e:
+        # through the public call (Gemv.__call__, eager): the step's input rows come from pinned
+        # host memory, the token ids go back to it, both inside the timed region
+        host_x = torch.empty(B, H, dtype=bf, pin_memory=True)
+        host_x.copy_(xn.cpu())
+        host_ids = torch.empty(B, dtype=torch.int64, pin_memory=True)
+        x_dev = torch.empty_like(xn)
+        for _ in range(2):
+            x_dev.copy_(host_x, non_blocking=True)
+            step(x_dev)
+            host_ids.copy_(ids, non_blocking=True)
+        torch.cuda.synchronize()
+        n_e2e = max(1, min(args.steps, 10))
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(n_e2e):
+            x_dev.copy_(host_x, non_blocking=True)
+            step(x_dev)
+            host_ids.copy_(ids, non_blocking=True)
+        a1.record()
+        torch.cuda.synchronize()
+        ms_e2e = max_over_ranks(dist, a0.elapsed_time(a1)) / n_e2e
+        e2e = {"value": round(world * bytes_step / (ms_e2e * 1e-3) / 1e12, 4), "unit": "TB/s",
+               "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": B * H * 2,
+               "d2h_bytes_per_step": B * 8, "steps": n_e2e,
+               "path": f"eager Gemv.__call__ per projection ({launches} C-ABI calls per step)"}
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        from oracle.epilogue import GEMV_BF16, GEMV_RESID, GEMV_SWIGLU, gemv_ref
+        w0 = {k: v.cpu() for k, v in W[0].items()}
+        xc, ac, hc = xn.cpu(), attn.cpu(), h.cpu()
+        t0 = time.perf_counter()
+        reps = 0
+        while reps < 1 or time.perf_counter() - t0 < 10.0:
+            gemv_ref(xc, w0["qkv"], GEMV_BF16)
+            gemv_ref(ac, w0["o"], GEMV_RESID, hc)
+            a_c = gemv_ref(xc, w0["gu"], GEMV_SWIGLU)
+            gemv_ref(a_c, w0["down"], GEMV_RESID, hc)
+            reps += 1
+        secs = (time.perf_counter() - t0) / reps
+        lbytes = sum(t.numel() * 2 for t in w0.values())
+        cpu = {"value": round(lbytes / secs / 1e12, 6), "unit": "TB/s", "cores": torch.get_num_threads(),
+               "kind": "port",
+               "sample": f"one layer's four projections with their epilogues (oracle/epilogue.py "
+                         f"gemv_ref, fp32 torch on the host) x{reps}, {secs * 1e3:.1f} ms per layer"}
+    line = {
+        "metric": P5_METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0, 0.02^2) bf16 weights of Qwen3-4B's shapes, N(0,1) inputs",
+        "config": {"workload": "p5 decode-step projections", "B": B, "layers": L,
+                   "shapes": {"qkv": [NQKV, H], "o": [H, NATT], "gate_up": [2 * I, H],
+                              "down": [H, I], "lm_head": [V, H]},
+                   "parallelism": "replicas" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2: {wbytes / 1e9:.2f} GB of weights per step",
+                   "launch": "one CUDA graph per step" + ("" if args.no_overlap else
+                             ", programmatic dependent launch between projections"),
+                   "grids": {k: op.grid for k, op in G.items()}},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": launches * args.steps, "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------------------------- c5: the engine
 def run_engine(args):
     """BASELINE config c5: random-init Qwen3-4B (std 0.02, seeded), B=32 prompts of 1024 uniform
@@ -563,7 +735,14 @@ def run_engine(args):
 
 def main():
     args = parse_args()
-    if args.workload == "c5" and args.impl == "ours":
+    if args.workload == "p5" and args.impl == "ours":
+        run_proj(args)
+    elif args.workload == "p5":
+        if dist_env()[1] == 0:
+            print(json.dumps({"impl": "reference", "unavailable": (
+                "the reference arm times the headline decode step (c2); the projections have no "
+                "separate CPU arm (their oracle is timed in the p5 line's cpu_baseline)")}), flush=True)
+    elif args.workload == "c5" and args.impl == "ours":
         run_engine(args)
     elif args.workload == "c5":
         if dist_env()[1] == 0:
