@@ -507,7 +507,8 @@ def run_proj(args):
     """Workload p5: the projections of one Qwen3-4B decode step at B = 32 rows, on the skinny-GEMM
     kernel with the reference's epilogues (engine.py:259-263): per layer QKV (bf16 out), o_proj
     (residual add), gate|up (SwiGLU) and down_proj (residual add), 36 layers with their own
-    weights, then the LM head with the greedy argmax. Random weights (std 0.02, seeded), random
+    weights, then the LM head with the greedy argmax (the RMSNorm row kernels between them, as in
+    the engine, are not part of this workload). Random weights (std 0.02, seeded), random
     inputs; the step is one CUDA graph of its 145 launches, replayed; consecutive launches overlap
     by programmatic dependent launch. value: weight + activation bytes per step / device time.
     N > 1: independent replicas (the projections are replicated in the sharded engine)."""

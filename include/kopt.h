@@ -225,8 +225,7 @@ KOPT_API int kopt_decode_attn_fused_noalloc(const kopt_plan* plan, const void* q
  * each weight read once for all rows, on the tcgen05 tensor cores (weight rows as the MMA's M = 128,
  * decode rows as its N, fp32 accumulators in tensor memory). Replaces Gemv
  * (engine/kernels/gemv.py:109-150) and the
- * epilogues of its kernel (gemv.py:29-106); the NORM prologue stays a row kernel
- * (kopt_add_rms_norm), which normalises x once instead of once per weight tile. */
+ * epilogues of its kernel (gemv.py:29-106), with its NORM prologue (kopt_gemv_fused). */
 #define KOPT_GEMV_F32 0     /* y: float [M, N], the fp32 sums */
 #define KOPT_GEMV_BF16 1    /* y: bf16 [M, N] = bf16(sum) */
 #define KOPT_GEMV_RESID 2   /* y: the residual h, bf16 [M, N], updated in place: h = bf16(h + bf16(sum)) */
@@ -266,6 +265,28 @@ KOPT_API int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int t
  * row-major; all 16-byte aligned; ws: plan->ws_bytes, 256-byte aligned, zero before first use. */
 KOPT_API int kopt_gemv(const kopt_gemv_plan* plan, const void* x, const void* w, void* y, void* ws,
                        void* stream);
+/* Fusions around a projection (gemv.py:1-20, 66-79, 95-98): the RMSNorm of x applied in shared
+ * memory as the x tiles arrive, bf16(norm_weight * bf16(x * rstd)) with rstd = rsqrt(ss / K + eps),
+ * and, for KOPT_GEMV_RESID, the row sums of squares of the new residual that the next projection's
+ * norm needs. Sums of squares travel as per-tile partials, added in tile order by the consumer, so
+ * results never depend on timing (the reference adds them with atomics). */
+typedef struct kopt_gemv_fuse {
+  const void* norm_weight;   /* bf16 [K], 16-byte aligned; NULL: no norm (x used as it is) */
+  const float* ss_in;        /* fp32 [ss_tiles][M] row sums of squares of x (a RESID projection's
+                                ss_out, or kopt_row_sumsq); NULL: every CTA sums the x rows
+                                itself (correct, but a latency-bound pass of several µs) */
+  int32_t ss_tiles;
+  float eps;
+  float* ss_out;             /* KOPT_GEMV_RESID only: fp32 [plan->tiles][M]; NULL: not written */
+} kopt_gemv_fuse;
+/* out[m] = sum over k of x[m][k]^2 (x bf16 [M, K] row-major, 16-byte aligned, K a multiple of 8;
+ * out fp32 [M]), one CTA per row, sums in a fixed order: the ss_in of a fused RMSNorm when no
+ * residual projection wrote it (the reference's embed_ss, engine/kernels/gemv.py:202-217). */
+KOPT_API int kopt_row_sumsq(const void* x, int M, int K, float* out, void* stream);
+/* kopt_gemv with the fusions above (fuse may be NULL). Replaces Gemv.__call__ with norm=True and
+ * the ss / ss_out hand-off of engine/kernels/gemv.py:140-150. */
+KOPT_API int kopt_gemv_fused(const kopt_gemv_plan* plan, const void* x, const void* w, void* y,
+                             void* ws, const kopt_gemv_fuse* fuse, void* stream);
 /* Copy the workspace error word (KOPT_DEV_ERR_TIMEOUT) to *err_out and clear it. Synchronises. */
 KOPT_API int kopt_gemv_read_error(const kopt_gemv_plan* plan, void* ws, int* err_out, void* stream);
 

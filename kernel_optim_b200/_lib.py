@@ -47,6 +47,8 @@ EXPORTED = (
     "kopt_silu_mul",
     "kopt_gemv_plan_make",
     "kopt_gemv",
+    "kopt_gemv_fused",
+    "kopt_row_sumsq",
     "kopt_gemv_read_error",
 )
 
@@ -128,6 +130,18 @@ class GemvPlan(ctypes.Structure):
     ]
 
 
+class GemvFuse(ctypes.Structure):
+    """Mirror of struct kopt_gemv_fuse."""
+
+    _fields_ = [
+        ("norm_weight", ctypes.c_void_p),
+        ("ss_in", ctypes.c_void_p),
+        ("ss_tiles", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("ss_out", ctypes.c_void_p),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -160,6 +174,9 @@ _SIGS = {
     "kopt_silu_mul": (_i32, [_vp, _vp, _i32, _i32, _vp]),
     "kopt_gemv_plan_make": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(GemvPlan)]),
     "kopt_gemv": (_i32, [ctypes.POINTER(GemvPlan), _vp, _vp, _vp, _vp, _vp]),
+    "kopt_gemv_fused": (_i32, [ctypes.POINTER(GemvPlan), _vp, _vp, _vp, _vp,
+                               ctypes.POINTER(GemvFuse), _vp]),
+    "kopt_row_sumsq": (_i32, [_vp, _i32, _i32, _vp, _vp]),
     "kopt_gemv_read_error": (_i32, [ctypes.POINTER(GemvPlan), _vp, ctypes.POINTER(ctypes.c_int),
                                     _vp]),
 }

@@ -1501,10 +1501,12 @@ __global__ void add_rms_norm_kernel(bf16* __restrict__ res, const bf16* __restri
   bf16* x = res + row * n;
   float ss = 0.f;
   uint4 keep[4];   // up to 4 vectors per thread (n <= 32 * blockDim)
+  uint4 wkeep[4];  // their weights, loaded with them: no second memory round trip after the sum
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int v = threadIdx.x + i * blockDim.x;
     if (v >= nv) break;
+    wkeep[i] = __ldg(reinterpret_cast<const uint4*>(w + v * 8));
     uint4 a = *reinterpret_cast<const uint4*>(x + v * 8);
     if (delta != nullptr) {
       const uint4 d = *reinterpret_cast<const uint4*>(delta + row * n + v * 8);
@@ -1545,7 +1547,7 @@ __global__ void add_rms_norm_kernel(bf16* __restrict__ res, const bf16* __restri
   for (int i = 0; i < 4; ++i) {
     const int v = threadIdx.x + i * blockDim.x;
     if (v >= nv) break;
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + v * 8);
+    const uint4 wv = wkeep[i];
     const uint32_t* pa = reinterpret_cast<const uint32_t*>(&keep[i]);
     const uint32_t* pw = reinterpret_cast<const uint32_t*>(&wv);
     uint4 y;
@@ -1581,6 +1583,37 @@ __global__ void silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ 
   *reinterpret_cast<uint4*>(out + m * I + v * 8) = y;
 }
 
+// out[m] = sum over the row of x[m]^2 (bf16 x, fp32 sums), one CTA per row: each thread its 8-element
+// vectors in order, then a warp xor tree and the warps in order. The row sums of squares a fused
+// RMSNorm needs when no residual projection has produced them (the embedded rows of layer 0).
+__global__ void row_sumsq_kernel(const bf16* __restrict__ x, int n, float* __restrict__ out) {
+  __shared__ float part[32];
+  griddep_wait();
+  const long long row = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * n);
+  float ss = 0.f;
+  for (int v = threadIdx.x; v < n / 8; v += blockDim.x) {
+    const uint4 a = xr[v];
+    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = bf2f(pa[e]);
+      ss = __fadd_rn(ss, __fadd_rn(__fmul_rn(f.x, f.x), __fmul_rn(f.y, f.y)));
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) part[warp] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t = __fadd_rn(t, part[w]);
+    out[row] = t;
+  }
+  griddep_launch_dependents();
+}
+
 // ============================================================= decode-step skinny GEMM (GEMV)
 // y[M, N] = x[M, K] . W[N, K]^T for M <= 64 rows (the decode batch), fp32 accumulation, with the
 // reference's epilogues (gemv.py:1-20, 29-106): F32 (fp32 store), BF16 (rounded store), RESID
@@ -1612,7 +1645,10 @@ __global__ void silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ 
 constexpr int kGEpiWarps = 4;            // epilogue warps: tensor-memory lanes 0-127
 constexpr int kGProducerWarp = 4;
 constexpr int kGMmaWarp = 5;
-constexpr int kGThreads = 6 * 32;
+constexpr int kGNormWarp0 = 6;           // warps 6-9: RMSNorm of x in shared memory (when fused)
+constexpr int kGNormThreads = 128;
+constexpr int kGNormSmemK = 4096;        // norm weights up to this K are staged in shared memory
+constexpr int kGThreads = 10 * 32;
 constexpr int kGRows = 128;              // weight rows per tile = the MMA's M
 constexpr int kGBK = 64;                 // k per chunk (one ring stage: 4 MMAs of K = 16)
 constexpr int kGLd = kGRows + 4;         // fp32 tile row stride in shared memory (floats)
@@ -1633,6 +1669,12 @@ struct GemvParams {
   int* cnt;                              // arrivals per tile, then tiles done (zero between launches)
   unsigned long long* keys;              // ARGMAX: per row, the best (bf16 logit, -index) so far
   int* err;
+  const bf16* xg;                        // x in global memory (the norm's own sums of squares)
+  const bf16* nw;                        // RMSNorm weight [K] applied to x; NULL: x used as it is
+  const float* ss_in;                    // row sums of squares of x, [ss_tiles][M]; NULL: from x
+  float* ss_out;                         // RESID: row sums of squares of the new h, [tiles][M]
+  float eps;
+  int ss_tiles;
   long long units;                       // tiles x nchunks
   int M, N, K, nchunks, tiles, per;      // per: units per CTA
 };
@@ -1643,7 +1685,9 @@ struct __align__(1024) GSmem {
   bf16 w[S][kGRows * kGBK];              // 16 KB per stage
   bf16 x[S][16 * MT * kGBK];             // 2 KB per 16 decode rows per stage
   float ct[16 * MT][kGLd];               // a finished segment's fp32 sums, [decode row][weight row]
-  unsigned long long full[S], empty[S], tfull[2], tempty[2], fin;
+  unsigned long long full[S], empty[S], xready[S], tfull[2], tempty[2], fin, mrg;
+  float rstd[64];                        // fused RMSNorm: 1 / rms of each row of x
+  alignas(16) bf16 nws[kGNormSmemK];     // fused RMSNorm: its weight, when K <= kGNormSmemK
   uint32_t tmem;                         // tensor-memory base from tcgen05.alloc
   int last;
   int last_all;
@@ -1656,6 +1700,15 @@ static_assert(gsmem_bytes<1>() <= 232448 && gsmem_bytes<2>() <= 232448 && gsmem_
 
 __device__ __forceinline__ float silu_bf16(float g) {   // bf16(g / (1 + exp(-g))), g a bf16 value
   return bf16r(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+}
+
+// Bulk copy global -> shared (no tensor map, no multicast), completion counted on an mbarrier.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
 }
 
 // ---- tcgen05 (tensor memory + 5th-generation MMA) helpers
@@ -1724,6 +1777,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* r) {
 template <int MT, int EPI>
 __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
   constexpr int S = gemv_stages<MT>();
+  const bool norm = p.nw != nullptr;   // x is normalised in shared memory before the MMAs read it
   constexpr int NM = 16 * MT;                  // the MMA's N: decode rows, padded
   constexpr uint32_t kCols = 2 * NM;           // two accumulators (32, 64 or 128 columns)
   extern __shared__ unsigned char smem_raw[];
@@ -1737,12 +1791,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constan
     for (int i = 0; i < S; ++i) {
       mbar_init(smem_u32(&s.full[i]), 1);
       mbar_init(smem_u32(&s.empty[i]), 1);
+      mbar_init(smem_u32(&s.xready[i]), kGNormThreads);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&s.tfull[b]), 1);
       mbar_init(smem_u32(&s.tempty[b]), kGEpiWarps);
     }
     mbar_init(smem_u32(&s.fin), 1);
+    mbar_init(smem_u32(&s.mrg), 1);
     s.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1820,7 +1876,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constan
         const uint32_t d = tmem + static_cast<uint32_t>(buf * NM);
         for (int c = a; c < b; ++c, ++i) {
           const int st = i % S;
-          if (!mbar_wait(smem_u32(&s.full[st]), (i / S) & 1, s, p.err, true)) {
+          if (!mbar_wait(smem_u32(norm ? &s.xready[st] : &s.full[st]), (i / S) & 1, s, p.err, true)) {
             ok = false;
             break;
           }
@@ -1840,6 +1896,76 @@ __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constan
       mbar_wait(smem_u32(&s.fin), 0, s, p.err, false);
     }
     __syncwarp();
+    griddep_launch_dependents();
+  } else if (warp >= kGNormWarp0) {   // ------------------------------------- RMSNorm of x (fused)
+    griddep_wait();
+    if (norm) {
+      const int t = threadIdx.x - kGNormWarp0 * 32;   // 0 .. 127
+      // rstd of each row: from the producer's per-tile sums in tile order, or from x itself
+      // (tpr threads per row, each a contiguous K range, then a fixed shuffle tree)
+      constexpr int tpr = kGNormThreads / NM;        // 8, 4 or 2
+      const int m = t / tpr, part = t % tpr;
+      float ss = 0.f;
+      if (m < p.M) {
+        if (p.ss_in != nullptr) {   // the row's threads take contiguous runs of tiles, in order
+          const int per_t = (p.ss_tiles + tpr - 1) / tpr;
+          const int t0 = part * per_t, t1 = min(p.ss_tiles, t0 + per_t);
+#pragma unroll 8
+          for (int tt = t0; tt < t1; ++tt) ss = __fadd_rn(ss, __ldcg(p.ss_in + tt * p.M + m));
+        } else {
+          const int kv = p.K / 8, per_t = (kv + tpr - 1) / tpr;
+          const int v0 = part * per_t, v1 = min(kv, v0 + per_t);
+          const uint4* row = reinterpret_cast<const uint4*>(p.xg + static_cast<long long>(m) * p.K);
+#pragma unroll 8
+          for (int v = v0; v < v1; ++v) {
+            const uint4 a = __ldg(row + v);
+            const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = bf2f(pa[e]);
+              ss = __fadd_rn(ss, __fadd_rn(__fmul_rn(f.x, f.x), __fmul_rn(f.y, f.y)));
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 1; off < tpr; off <<= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+      if (part == 0) s.rstd[m] = m < p.M ? rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(p.K)), p.eps)) : 0.f;
+      const bool wsm = p.K <= kGNormSmemK;   // the weight read once into shared memory
+      if (wsm)
+        for (int v = t; v < p.K / 8; v += kGNormThreads)
+          reinterpret_cast<uint4*>(s.nws)[v] = __ldg(reinterpret_cast<const uint4*>(p.nw) + v);
+      named_bar(2, kGNormThreads);
+      // every stage: x <- bf16(w * bf16(x * rstd)) in place (fused.py:39-46's cast order), in the
+      // 128-byte-swizzled layout TMA wrote (16-byte chunk c of row r sits at chunk c ^ (r % 8))
+      for (int i = 0; i < n; ++i) {
+        const int st = i % S;
+        if (!mbar_wait(smem_u32(&s.full[st]), (i / S) & 1, s, p.err, true)) break;
+        const int kb = static_cast<int>((u0 + i) % p.nchunks) * kGBK;
+        unsigned char* xs = reinterpret_cast<unsigned char*>(&s.x[st][0]);
+        for (int c = t; c < NM * 8; c += kGNormThreads) {
+          const int r = c >> 3, pc = c & 7;
+          const int k0 = kb + 8 * (pc ^ (r & 7));
+          uint4* cp = reinterpret_cast<uint4*>(xs + r * 128 + pc * 16);
+          uint4 a = *cp;
+          const uint4 wv = k0 >= p.K ? make_uint4(0, 0, 0, 0)
+                           : wsm ? *reinterpret_cast<const uint4*>(s.nws + k0)
+                                 : __ldg(reinterpret_cast<const uint4*>(p.nw + k0));
+          const float rs = s.rstd[r];
+          uint32_t* pa = reinterpret_cast<uint32_t*>(&a);
+          const uint32_t* pw = reinterpret_cast<const uint32_t*>(&wv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = bf2f(pa[e]), fw = bf2f(pw[e]);
+            pa[e] = pack_bf16(__fmul_rn(fw.x, bf16r(__fmul_rn(f.x, rs))),
+                              __fmul_rn(fw.y, bf16r(__fmul_rn(f.y, rs))));
+          }
+          *cp = a;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> MMA reads
+        mbar_arrive(smem_u32(&s.xready[st]));
+      }
+    }
     griddep_launch_dependents();
   } else {   // ------------------------------------------------------------- epilogue warps 0-3
     griddep_wait();
@@ -1898,14 +2024,44 @@ __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constan
         float4 acc4[kR];
 #pragma unroll
         for (int r = 0; r < kR; ++r) acc4[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-        // segments in a fixed order (the tile's first CTA first), KP of them per round so that
-        // KP x kR loads are in flight together
-        constexpr int KP = kR <= 8 ? 2 : 1;
         auto seg_src = [&](int k) {
           const bool kfirst_seg = static_cast<long long>(k) * p.per >= tu0;
           return reinterpret_cast<const float4*>(
               p.part + static_cast<long long>(2 * k + (kfirst_seg ? 0 : 1)) * p.M * kGRows);
         };
+        const int nseg = klast - kfirst + 1;
+        const uint32_t seg_bytes = static_cast<uint32_t>(p.M) * kGRows * 4;
+        if (u >= u1 && static_cast<long long>(nseg) * seg_bytes <= static_cast<long long>(sizeof(s.w))) {
+          // this CTA's last segment: the ring is idle (every stage has been read by the MMAs), so
+          // all the tile's partials come in at once by bulk copies, one L2 round trip, and are
+          // added from shared memory in the same fixed order
+          const float4* stage = reinterpret_cast<const float4*>(&s.w[0][0]);
+          if (tid == 0) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");   // generic writes -> bulk reads
+            const uint32_t mb = smem_u32(&s.mrg);
+            mbar_arrive_expect_tx(mb, static_cast<uint32_t>(nseg) * seg_bytes);
+            for (int j = 0; j < nseg; ++j)
+              bulk_g2s(smem_u32(&s.w[0][0]) + static_cast<uint32_t>(j) * seg_bytes, seg_src(kfirst + j),
+                       seg_bytes, mb);
+          }
+          mbar_wait(smem_u32(&s.mrg), 0, s, p.err, true);   // once per launch: phase 0
+          __syncwarp();
+          for (int j = 0; j < nseg; ++j)
+#pragma unroll
+            for (int r = 0; r < kR; ++r) {
+              const int m = warp + kGEpiWarps * r;
+              if (m < rows) {
+                const float4 x = stage[(j * p.M + m) * (kGRows / 4) + lane];
+                acc4[r].x += x.x;
+                acc4[r].y += x.y;
+                acc4[r].z += x.z;
+                acc4[r].w += x.w;
+              }
+            }
+        } else {
+        // segments in a fixed order (the tile's first CTA first), KP of them per round so that
+        // KP x kR loads are in flight together
+        constexpr int KP = kR <= 8 ? 2 : 1;
         for (int k = kfirst; k <= klast; k += KP) {
           float4 x4[KP][kR];
 #pragma unroll
@@ -1930,6 +2086,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constan
               acc4[r].w += x4[j][r].w;
             }
         }
+        }
 #pragma unroll
         for (int r = 0; r < kR; ++r) {
           const int m = warp + kGEpiWarps * r;
@@ -1945,7 +2102,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constan
       for (int r0 = 0; r0 < NM; r0 += 32) {
         const int m = r0 + (tid >> 2);
         const bool act = m < NM && m < p.M;
-        if (EPI != GEMV_ARGMAX && !act) continue;   // ARGMAX: every lane takes part in the shuffles
+        // ARGMAX and RESID: every lane takes part in the shuffles
+        if (EPI != GEMV_ARGMAX && EPI != GEMV_RESID && !act) continue;
         float v[32];
         if (!act) {
 #pragma unroll
@@ -1986,9 +2144,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constan
           }
         } else if (EPI == GEMV_RESID) {   // h <- bf16(h + bf16(acc)) (gemv.py:95-97)
           bf16* h = static_cast<bf16*>(p.y) + row;
+          float sq = 0.f;   // sum of squares of this thread's new h values (gemv.py:97-98)
 #pragma unroll
           for (int seg2 = 0; seg2 < 2; ++seg2) {
-            if (!(seg2 == 0 ? va : vb)) continue;
+            if (!act || !(seg2 == 0 ? va : vb)) continue;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
               bf16* hp = h + (seg2 == 0 ? sa : sb) + 8 * half;
@@ -1999,10 +2158,17 @@ __global__ void __launch_bounds__(kGThreads, 1) gemv_kernel(const __grid_constan
                 const float2 f = bf2f(ph[e]);
                 const int j = 16 * seg2 + 8 * half + 2 * e;
                 ph[e] = pack_bf16(__fadd_rn(f.x, bf16r(v[j])), __fadd_rn(f.y, bf16r(v[j + 1])));
+                const float2 hn = bf2f(ph[e]);
+                sq = __fadd_rn(sq, __fadd_rn(__fmul_rn(hn.x, hn.x), __fmul_rn(hn.y, hn.y)));
               }
               *reinterpret_cast<uint4*>(hp) = hv;
             }
           }
+          // the row's 4 threads, then one partial per (tile, row): the next projection's norm adds
+          // the tiles in order, so the result does not depend on timing
+          sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, 1));
+          sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, 2));
+          if (p.ss_out != nullptr && act && q == 0) p.ss_out[static_cast<long long>(tile) * p.M + m] = sq;
         } else if (EPI == GEMV_ARGMAX) {
           // this thread's 32 columns, then the row's 4 threads, then all tiles through one 64-bit
           // atomicMax per row: key = (order-preserving bits of the bf16 logit) << 32 | ~index, so
@@ -2338,7 +2504,8 @@ int gemv_launch_t(const kopt_gemv_plan* plan, GemvParams& p, void* stream) {
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(plan->grid);
-  cfg.blockDim = dim3(kGThreads);
+  // the four RMSNorm warps exist only when the norm is fused
+  cfg.blockDim = dim3(p.nw != nullptr ? kGThreads : kGThreads - kGNormThreads);
   cfg.dynamicSmemBytes = gsmem_bytes<MT>();
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
@@ -2379,9 +2546,10 @@ int kopt_add_rms_norm(void* res, const void* delta, const void* weight, void* ou
       (delta != nullptr && !aligned16(delta)))
     return KOPT_ERR_ARG;
   const int nv = N / 8;
-  int threads = (nv + 3) / 4;                         // at most 4 vectors per thread
-  threads = threads < 32 ? 32 : (threads + 31) / 32 * 32;
-  if (threads > 1024) return KOPT_ERR_ARG;
+  // one vector per thread up to 1024 threads (all loads of a row in one round), at most 4
+  int threads = (nv + 31) / 32 * 32;
+  if (threads > 1024) threads = 1024;
+  if (nv > 4 * threads) return KOPT_ERR_ARG;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M);
   cfg.blockDim = dim3(threads);
@@ -2398,6 +2566,13 @@ int kopt_add_rms_norm(void* res, const void* delta, const void* weight, void* ou
     return KOPT_ERR_CUDA;
   }
   return KOPT_OK;
+}
+
+int kopt_row_sumsq(const void* x, int M, int K, float* out, void* stream) {
+  if (x == nullptr || out == nullptr || M < 1 || K < 8 || K % 8 != 0 || !aligned16(x))
+    return KOPT_ERR_ARG;
+  row_sumsq_kernel<<<M, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const bf16*>(x), K, out);
+  return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
 }
 
 int kopt_silu_mul(const void* gate_up, void* out, int M, int I, void* stream) {
@@ -2449,10 +2624,16 @@ int kopt_gemv_plan_make(int device, int M, int N, int K, int epi, int target_cta
   return KOPT_OK;
 }
 
-int kopt_gemv(const kopt_gemv_plan* plan, const void* x, const void* w, void* y, void* ws,
-              void* stream) {
+int kopt_gemv_fused(const kopt_gemv_plan* plan, const void* x, const void* w, void* y, void* ws,
+                    const kopt_gemv_fuse* fuse, void* stream) {
   if (plan == nullptr || x == nullptr || w == nullptr || y == nullptr || ws == nullptr)
     return KOPT_ERR_ARG;
+  if (fuse != nullptr) {
+    if ((fuse->norm_weight != nullptr && !aligned16(fuse->norm_weight)) ||
+        (fuse->ss_in != nullptr && (fuse->norm_weight == nullptr || fuse->ss_tiles < 1)) ||
+        (fuse->ss_out != nullptr && plan->epi != GEMV_RESID))
+      return KOPT_ERR_ARG;
+  }
   if (!aligned16(x) || !aligned16(w) || !aligned16(y)) return KOPT_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return KOPT_ERR_WORKSPACE;
   int rc = set_device(plan->device);
@@ -2485,6 +2666,14 @@ int kopt_gemv(const kopt_gemv_plan* plan, const void* x, const void* w, void* y,
   if (lay.total != plan->ws_bytes) return KOPT_ERR_WORKSPACE;
   char* base = static_cast<char*>(ws);
   p.y = y;
+  p.xg = static_cast<const bf16*>(x);
+  if (fuse != nullptr) {
+    p.nw = static_cast<const bf16*>(fuse->norm_weight);
+    p.ss_in = fuse->ss_in;
+    p.ss_tiles = fuse->ss_tiles;
+    p.ss_out = fuse->ss_out;
+    p.eps = fuse->eps;
+  }
   p.err = reinterpret_cast<int*>(base);
   p.cnt = reinterpret_cast<int*>(base + lay.cnt);
   p.part = reinterpret_cast<float*>(base + lay.part);
@@ -2498,6 +2687,11 @@ int kopt_gemv(const kopt_gemv_plan* plan, const void* x, const void* w, void* y,
   p.per = plan->units_per_cta;
   return mt == 1 ? gemv_launch_epi<1>(plan, p, stream)
                  : mt == 2 ? gemv_launch_epi<2>(plan, p, stream) : gemv_launch_epi<4>(plan, p, stream);
+}
+
+int kopt_gemv(const kopt_gemv_plan* plan, const void* x, const void* w, void* y, void* ws,
+              void* stream) {
+  return kopt_gemv_fused(plan, x, w, y, ws, nullptr, stream);
 }
 
 int kopt_gemv_read_error(const kopt_gemv_plan* plan, void* ws, int* err_out, void* stream) {

@@ -11,10 +11,11 @@ Keeps the reference engine's surface (GodRishUniverse/kernel_optim engine/engine
 What changes is the decode step (engine.py:313-341, 388-401): the per-layer ``qk_norm_rope`` +
 ``attn1`` pair becomes one ``PagedDecodeAttention`` launch over a paged KV cache, and the whole step
 is captured once per shape in a CUDA graph and replayed, pipelined one step ahead of the host as in
-engine.py:509-533. Around it the layer runs as engine.py:325-340 does: the residual add and RMSNorm
-in one kernel (``add_rms_norm``), the projections as skinny GEMMs against fused weights (q/k/v; gate
-and up; ``Gemv``, engine.py:259-262) with the residual add and SwiGLU as their epilogues, all in
-Transformers' cast order (batches above 64 rows: cuBLAS GEMMs and ``silu_mul``). Prefill is the
+engine.py:509-533. Around it the layer runs as engine.py:325-340 does, on the tcgen05 skinny GEMM
+(``Gemv``, engine.py:259-263) against fused weights (q/k/v; gate and up): each RMSNorm a row kernel
+(``add_rms_norm``), the residual adds, SwiGLU and the LM head's greedy pick as epilogues, all in
+Transformers' cast order (batches above 64 rows: cuBLAS GEMMs, ``add_rms_norm`` and
+``silu_mul``). Prefill is the
 native Transformers forward with its DynamicCache, whose K/V are copied into the pages (prefill is
 not the optimised path).
 
@@ -138,6 +139,8 @@ class Engine:
             nqkv = self.layers[0]["qkv"].shape[0]
             ov = self.overlap
             self.qkv = torch.zeros(B, nqkv, dtype=bf, device=dev)
+            # each RMSNorm is a row kernel writing the normalised rows once; the projections read
+            # them (normalising inside the projection, kopt_gemv_fused, measured slower here)
             self.gemv = dict(
                 qkv=Gemv(B, nqkv, H, EPI_BF16, device=dev, overlap_prev=ov),
                 o=Gemv(B, H, self.nq * self.d, EPI_RESID, device=dev, overlap_prev=ov),
@@ -187,9 +190,10 @@ class Engine:
 
     def _step(self):
         """One decode step at positions pos[b]; argmax feeds ids, positions advance. The layer
-        loop of engine.py:325-340. With the skinny-GEMM kernels (B <= 64) the residual adds and
-        SwiGLU are the projections' epilogues (gemv.py:86-105), as in the reference's decode
-        step; otherwise cuBLAS GEMMs with the residual add fused into the next RMSNorm."""
+        loop of engine.py:325-340. With the skinny-GEMM kernels (B <= 64) the residual adds,
+        SwiGLU and the greedy pick are the projections' epilogues (gemv.py:86-105) and each
+        RMSNorm a row kernel; otherwise cuBLAS GEMMs with the residual add fused into the next
+        RMSNorm."""
         h, n = self.hid, self.normed
         torch.index_select(self.embed, 0, self.ids, out=h)
         gv = self.gemv

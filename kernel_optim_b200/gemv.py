@@ -15,13 +15,17 @@ y[M, N] = x[M, K] . w[N, K]^T with fp32 sums and one epilogue (gemv.py:86-105):
   the LM head and greedy pick of the reference's decode step (engine.py:263 logits, then argmax)
   in one kernel that never writes the logits.
 
-``norm=True`` normalises x first, bf16(nw * bf16(x * rstd)) (gemv.py:66-79), with a row kernel that
-writes the normalised rows once: re-normalising x inside every weight tile would repeat the work
-once per tile (96 to 600 times for Qwen3-4B's projections). The row sums of squares are recomputed
-from x there, so ``ss`` and ``ss_out`` (the reference's hand-off of those sums between kernels) are
-neither read nor written. The kernel splits K wherever a tile's chunks fall to several CTAs, for
-every epilogue (their fp32 partials are added in CTA order), so ``allow_split`` is accepted for
-the signature and does not restrict the split.
+``norm=True`` normalises x first, bf16(nw * bf16(x * rstd)) with rstd = rsqrt(mean(x^2) + eps)
+(gemv.py:66-79). By default a row kernel (``kopt_add_rms_norm``) writes the normalised rows once
+and the projection reads them: on B200 that is faster than normalising inside the projection. With
+``fuse_norm=True`` the kernel does it itself (``kopt_gemv_fused``): four warps rewrite each x tile
+in shared memory between its TMA copy and the MMAs, rstd from ``ss``, the row sums of squares the
+RESID projection before wrote into its ``ss_out`` — float32 ``[T, M]``, one partial per weight tile
+of that projection (``Gemv.ss_tiles``), added in tile order, so nothing depends on timing where the
+reference adds them with atomics; a ``[M]`` tensor of whole sums works too; without ``ss`` a row
+kernel (``kopt_row_sumsq``, the reference's ``embed_ss``) computes them first. The kernel splits K wherever a tile's chunks fall to several CTAs, for every epilogue
+(their fp32 partials are added in CTA order), so ``allow_split`` is accepted for the signature and
+does not restrict the split.
 
 Launches go to the current torch stream of the tensors' device; a missing library raises KoptError.
 """
@@ -34,7 +38,7 @@ import time
 import torch
 
 from . import _lib
-from ._lib import GemvPlan, KoptError, check
+from ._lib import GemvFuse, GemvPlan, KoptError, check
 from .fused import _ptr, _require_cuda, _stream, add_rms_norm
 
 EPI_F32, EPI_BF16, EPI_RESID, EPI_SWIGLU, EPI_ARGMAX = (
@@ -49,14 +53,17 @@ class Gemv:
     kernel before it on the stream drains)."""
 
     def __init__(self, M, N, K, epi, norm=False, allow_split=False, eps=1e-6, device=None,
-                 ctas=0, overlap_prev=False):
+                 ctas=0, overlap_prev=False, fuse_norm=False):
         self.M, self.N, self.K, self.epi, self.norm, self.eps = M, N, K, epi, norm, eps
         self.allow_split = allow_split
         dev = torch.device(device) if device is not None else torch.device("cuda")
         self.device = dev if dev.index is not None else torch.device("cuda", torch.cuda.current_device())
         self.overlap_prev = overlap_prev
-        self._xn = torch.empty(M, K, dtype=torch.bfloat16, device=self.device) if norm else None
         self._plans: dict[int, tuple[GemvPlan, torch.Tensor]] = {}
+        self._ss = None   # row sums of squares of x, when the caller gives none
+        self.fuse_norm = fuse_norm
+        self._xn = (torch.empty(M, K, dtype=torch.bfloat16, device=self.device)
+                    if norm and not fuse_norm else None)
         self.cfg = self._plan(ctas).grid
 
     def _plan(self, ctas: int) -> GemvPlan:
@@ -79,6 +86,11 @@ class Gemv:
     @property
     def grid(self) -> int:
         return self.cfg
+
+    @property
+    def ss_tiles(self) -> int:
+        """Rows of the ``ss_out`` partials a RESID call writes: one per weight tile."""
+        return self._plan(self.cfg).tiles
 
     def __call__(self, x, w, y=None, nw=None, ss=None, h=None, ss_out=None, cfg=None):
         key = self.cfg if cfg is None else cfg
@@ -106,13 +118,44 @@ class Gemv:
             _require_cuda(out, "y", torch.float32 if self.epi == EPI_F32 else torch.bfloat16)
             if out.shape != (M, N) or not out.is_contiguous():
                 raise KoptError(f"Gemv: output must be [{M}, {N}] contiguous")
-        if self.norm:
+        fuse = None
+        if self.norm and not self.fuse_norm:
             if nw is None:
                 raise KoptError("Gemv(norm=True) needs nw")
             add_rms_norm(x, None, nw, self._xn, self.eps)
             x = self._xn
-        check(_lib.lib().kopt_gemv(ctypes.byref(plan), _ptr(x), _ptr(w), _ptr(out), _ptr(ws),
-                                   _stream(x.device)), "kopt_gemv")
+        if (self.norm and self.fuse_norm) or ss_out is not None:
+            fuse = GemvFuse()
+            fuse.eps = self.eps
+            if self.norm and self.fuse_norm:
+                if nw is None:
+                    raise KoptError("Gemv(norm=True) needs nw")
+                _require_cuda(nw, "nw")
+                if nw.shape != (K,) or not nw.is_contiguous():
+                    raise KoptError(f"Gemv: nw must be [{K}] contiguous")
+                fuse.norm_weight = nw.data_ptr()
+                if ss is None:   # no residual projection wrote them: one row pass first
+                    if self._ss is None:
+                        self._ss = torch.empty(1, M, dtype=torch.float32, device=self.device)
+                    check(_lib.lib().kopt_row_sumsq(_ptr(x), M, K, _ptr(self._ss), _stream(x.device)),
+                          "kopt_row_sumsq")
+                    ss = self._ss
+                if ss is not None:
+                    _require_cuda(ss, "ss", torch.float32)
+                    if ss.numel() % M or not ss.is_contiguous() or ss.shape[-1] != M:
+                        raise KoptError(f"Gemv: ss must be float32 [T, {M}] (or [{M}]) contiguous")
+                    fuse.ss_in = ss.data_ptr()
+                    fuse.ss_tiles = ss.numel() // M
+            if ss_out is not None:
+                if self.epi != EPI_RESID:
+                    raise KoptError("Gemv: ss_out is written by EPI_RESID only")
+                _require_cuda(ss_out, "ss_out", torch.float32)
+                if ss_out.shape != (plan.tiles, M) or not ss_out.is_contiguous():
+                    raise KoptError(f"Gemv: ss_out must be float32 [{plan.tiles}, {M}] contiguous")
+                fuse.ss_out = ss_out.data_ptr()
+        check(_lib.lib().kopt_gemv_fused(ctypes.byref(plan), _ptr(x), _ptr(w), _ptr(out), _ptr(ws),
+                                         ctypes.byref(fuse) if fuse is not None else None,
+                                         _stream(x.device)), "kopt_gemv_fused")
 
     def read_error(self) -> int:
         """KOPT_DEV_ERR_* bits of past calls (synchronises); clears them."""

@@ -48,6 +48,8 @@ def test_struct_layouts_match_header():
     assert ctypes.sizeof(_lib.Gather) == 152
     # kopt_gemv_plan: 10 int32, int64 -> 48 bytes
     assert ctypes.sizeof(_lib.GemvPlan) == 48
+    # kopt_gemv_fuse: 2 pointers, int32, float, pointer -> 32 bytes
+    assert ctypes.sizeof(_lib.GemvFuse) == 32
 
 
 @pytest.mark.parametrize("args", [
@@ -98,5 +100,6 @@ def test_gemv_rejects_null_arguments(lib):
     plan = _lib.GemvPlan()
     assert lib.kopt_gemv(None, None, None, None, None, None) == _lib.KOPT_ERR_ARG
     assert lib.kopt_gemv(ctypes.byref(plan), None, None, None, None, None) == _lib.KOPT_ERR_ARG
+    assert lib.kopt_gemv_fused(ctypes.byref(plan), None, None, None, None, None, None) == _lib.KOPT_ERR_ARG
     err = ctypes.c_int(0)
     assert lib.kopt_gemv_read_error(None, None, ctypes.byref(err), None) == _lib.KOPT_ERR_ARG
