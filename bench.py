@@ -66,6 +66,8 @@ def parse_args():
     ap.add_argument("--p5-layers", type=int, default=36,
                     help="p5: transformer layers in the step (36 = Qwen3-4B; fewer for a small "
                          "profiling case)")
+    ap.add_argument("--prefill", choices=["native", "transformers"], default="native",
+                    help="c5: prefill on the row kernels + SDPA, or the Transformers forward")
     ap.add_argument("--no-gemv", action="store_true",
                     help="c5: cuBLAS GEMMs + separate SwiGLU / residual kernels instead of the "
                          "tcgen05 skinny-GEMM projections with fused epilogues (kopt_gemv)")
@@ -682,7 +684,8 @@ def run_engine(args):
     model = random_model(QWEN3_4B["layers"], QWEN3_4B["hidden"], QWEN3_4B["intermediate"],
                          QWEN3_4B["vocab"], seed=0, device=dev)
     eng = Engine.from_model(model, dev, group=dist.group.WORLD if dist is not None else None,
-                            overlap=not args.no_overlap, gemv=not args.no_gemv)
+                            overlap=not args.no_overlap, gemv=not args.no_gemv,
+                            prefill=args.prefill)
     g = torch.Generator().manual_seed(5)
     prompts = torch.randint(0, QWEN3_4B["vocab"], (B, S), generator=g).tolist()
     for _ in range(max(1, args.warmup)):
@@ -720,6 +723,7 @@ def run_engine(args):
         "config": {"workload": "c5 engine generate", "B": B, "prompt": S, "new_tokens": N,
                    "overlap_prev": not args.no_overlap,
                    "projections": "cuBLAS" if eng.gemv is None else "kopt_gemv (fused epilogues)",
+                   "prefill": args.prefill,
                    "parallelism": (f"kv-head shard x{world}, all-gather fused into the attention "
                                    "kernel (NVLink stores)" if world > 1 else "single GPU")},
         "decode_tokens_s": round(B / (step_ms * 1e-3), 1), "decode_step_ms": round(step_ms, 4),

@@ -15,9 +15,9 @@ engine.py:509-533. Around it the layer runs as engine.py:325-340 does, on the tc
 (``Gemv``, engine.py:259-263) against fused weights (q/k/v; gate and up): each RMSNorm a row kernel
 (``add_rms_norm``), the residual adds, SwiGLU and the LM head's greedy pick as epilogues, all in
 Transformers' cast order (batches above 64 rows: cuBLAS GEMMs, ``add_rms_norm`` and
-``silu_mul``). Prefill is the
-native Transformers forward with its DynamicCache, whose K/V are copied into the pages (prefill is
-not the optimised path).
+``silu_mul``). Prefill (``prefill="native"``) runs the same row kernels over the whole prompt with
+cuBLAS GEMMs and torch SDPA for the causal attention, the prologue kernel writing the prompt's K/V,
+which are copied into the pages; ``prefill="transformers"`` uses the native Transformers forward.
 
 Multi-GPU (``group`` = a torch.distributed process group of G ranks, one GPU each, one node): rank r
 keeps kv heads [r*nkv/G, (r+1)*nkv/G) — their QKV weight rows and their pages — and runs attention
@@ -32,7 +32,7 @@ import torch
 
 from ._lib import KoptError
 from .paged import PAGE, PagedDecodeAttention, PagedKVCache
-from .fused import add_rms_norm, silu_mul
+from .fused import add_rms_norm, qk_norm_rope, silu_mul
 from .gather import PeerGather, slot_of
 from .gemv import EPI_ARGMAX, EPI_BF16, EPI_RESID, EPI_SWIGLU, Gemv
 from .shard import head_range, shard_qkv_weight
@@ -40,22 +40,25 @@ from .shard import head_range, shard_qkv_weight
 
 class Engine:
     def __init__(self, model_path: str, device: str = "cuda:0", group=None, overlap: bool = True,
-                 gemv: bool = True):
+                 gemv: bool = True, prefill: str = "native"):
         from transformers import AutoModelForCausalLM
         model = AutoModelForCausalLM.from_pretrained(
             model_path, dtype=torch.bfloat16, attn_implementation="sdpa", local_files_only=True)
-        self._init(model.eval().to(device), device, group, overlap, gemv)
+        self._init(model.eval().to(device), device, group, overlap, gemv, prefill)
 
     @classmethod
     def from_model(cls, model, device: str = "cuda:0", group=None,
-                   overlap: bool = True, gemv: bool = True) -> "Engine":
+                   overlap: bool = True, gemv: bool = True, prefill: str = "native") -> "Engine":
         """Wrap an already loaded Qwen3ForCausalLM (bf16, sdpa) instead of reading a checkpoint."""
         self = cls.__new__(cls)
-        self._init(model.eval().to(device), device, group, overlap, gemv)
+        self._init(model.eval().to(device), device, group, overlap, gemv, prefill)
         return self
 
     # ------------------------------------------------------------------ construction
-    def _init(self, model, device, group, overlap=True, gemv=True):
+    def _init(self, model, device, group, overlap=True, gemv=True, prefill="native"):
+        if prefill not in ("native", "transformers"):
+            raise KoptError("prefill must be 'native' or 'transformers'")
+        self.prefill = prefill
         torch.backends.cuda.matmul.allow_tf32 = False
         self.device = torch.device(device)
         if self.device.type != "cuda":
@@ -224,7 +227,60 @@ class Engine:
         torch.argmax(logits, dim=-1, out=self.ids)
         self.pos.add_(1)
 
+    def _qkv_full(self, i):
+        """Layer i's QKV weight for all heads (prefill attends with every head on every rank)."""
+        lw = self.layers[i]
+        if self.world == 1:
+            return lw["qkv"]
+        if "qkv_full" not in lw:
+            a = lw["mod"].self_attn
+            lw["qkv_full"] = torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0).contiguous()
+        return lw["qkv_full"]
+
     def _prefill(self, prompt):
+        if self.prefill == "native":
+            self._prefill_native(prompt)
+        else:
+            self._prefill_transformers(prompt)
+
+    def _prefill_native(self, prompt):
+        """Prefill on the row kernels of the decode step, Qwen3DecoderLayer's cast order: per layer
+        the residual add + input RMSNorm (add_rms_norm), one QKV GEMM, the q/k RMSNorm + RoPE
+        prologue (kopt_qk_norm_rope) writing the prompt's K/V, causal GQA attention (torch SDPA),
+        o_proj, residual add + post-attention RMSNorm, gate|up GEMM, SwiGLU (silu_mul), down_proj;
+        this rank's K/V heads go into the pages. Only the last position goes through the final
+        norm and the LM head (the reference's prefill keeps only its logits too)."""
+        B, S = prompt.shape
+        H, nq, nkv, d = self.embed.shape[1], self.nq, self.nkv, self.d
+        dev, bf, M = self.device, torch.bfloat16, B * S
+        h = torch.index_select(self.embed, 0, prompt.reshape(-1))
+        n = torch.empty_like(h)
+        q = torch.empty(M, nq * d, dtype=bf, device=dev)
+        k = torch.empty(B, nkv, S, d, dtype=bf, device=dev)
+        v = torch.empty_like(k)
+        act = torch.empty(M, self.inter, dtype=bf, device=dev)
+        pos0 = torch.zeros(B, dtype=torch.int32, device=dev)
+        h0 = self.h0
+        delta = None
+        for i, lw in enumerate(self.layers):
+            add_rms_norm(h, delta, lw["w_in"], n, self.eps)
+            qkv = torch.mm(n, self._qkv_full(i).t())
+            qk_norm_rope(qkv, lw["q_norm"], lw["k_norm"], self.cos, self.sin, pos0, q, k, v, S,
+                         self.eps, nq, nkv, d)
+            a = torch.nn.functional.scaled_dot_product_attention(
+                q.view(B, S, nq, d).transpose(1, 2), k, v, is_causal=True, enable_gqa=True)
+            o = torch.mm(a.transpose(1, 2).reshape(M, nq * d), lw["o"].t())
+            add_rms_norm(h, o, lw["w_post"], n, self.eps)
+            silu_mul(torch.mm(n, lw["gu"].t()), act)
+            delta = torch.mm(act, lw["down"].t())
+            self.cache.write_prefix(i, k[:, h0:h0 + self.nkv_l], v[:, h0:h0 + self.nkv_l])
+        last = h.view(B, S, H)[:, -1].contiguous()
+        nl = torch.empty_like(last)
+        add_rms_norm(last, delta.view(B, S, H)[:, -1].contiguous(), self.final_norm, nl, self.eps)
+        self.ids.copy_(self.model.lm_head(nl).argmax(dim=-1))
+        self.pos.fill_(S)
+
+    def _prefill_transformers(self, prompt):
         """The native forward over the prompt; its K/V (this rank's heads) go into the pages."""
         out = self.model(input_ids=prompt, use_cache=True)
         self.ids.copy_(out.logits[:, -1, :].argmax(dim=-1))
