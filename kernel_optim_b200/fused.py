@@ -119,7 +119,10 @@ class _DevErr:
         idx = device.index if device.index is not None else torch.cuda.current_device()
         w = cls._words.get(idx)
         if w is None:
-            w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+            # a normal tensor even when first asked for under torch.inference_mode (the engine's
+            # generate), so that callers outside it can still clear it in place
+            with torch.inference_mode(False):
+                w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
             cls._words[idx] = w
         return w
 
