@@ -23,9 +23,11 @@ in shared memory between its TMA copy and the MMAs, rstd from ``ss``, the row su
 RESID projection before wrote into its ``ss_out`` — float32 ``[T, M]``, one partial per weight tile
 of that projection (``Gemv.ss_tiles``), added in tile order, so nothing depends on timing where the
 reference adds them with atomics; a ``[M]`` tensor of whole sums works too; without ``ss`` a row
-kernel (``kopt_row_sumsq``, the reference's ``embed_ss``) computes them first. The kernel splits K wherever a tile's chunks fall to several CTAs, for every epilogue
-(their fp32 partials are added in CTA order), so ``allow_split`` is accepted for the signature and
-does not restrict the split.
+kernel (``kopt_row_sumsq``, the reference's ``embed_ss``) computes them first.
+
+The kernel splits K wherever a tile's chunks fall to several CTAs, for every epilogue (their fp32
+partials are added in CTA order), so ``allow_split`` is accepted for the signature and does not
+restrict the split.
 
 Launches go to the current torch stream of the tensors' device; a missing library raises KoptError.
 """
