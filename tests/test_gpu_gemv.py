@@ -277,3 +277,15 @@ def test_argmax_ties_take_the_first_index():
     Gemv(M, N, K, EPI_ARGMAX, device=DEV)(x, w, ids)
     torch.cuda.synchronize()
     assert ids.tolist() == [0] * M
+
+
+@pytest.mark.parametrize("N,K,epi", [(6144, 2560, EPI_BF16), (2560, 9728, EPI_RESID),
+                                     (9728, 2560, EPI_SWIGLU), (151936, 2560, EPI_ARGMAX)])
+def test_plan_matches_host_mirror(N, K, epi):
+    """kopt_gemv_plan_make's split equals the host restatement that tests/test_gemv_plan.py checks."""
+    from kernel_optim_b200.gemv_plan import gemv_split
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    op = Gemv(32, N, K, epi, device=DEV)
+    plan = op._plans[op.grid][0]
+    want = gemv_split(N, K, swiglu=epi == EPI_SWIGLU, ctas=sms)
+    assert (plan.tiles, plan.units_per_cta, plan.grid) == (want.tiles, want.per, want.grid)
