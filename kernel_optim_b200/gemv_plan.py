@@ -6,7 +6,8 @@ restates that arithmetic so the split can be inspected and property-tested witho
 * the weight is cut into tiles of 128 rows (SWIGLU: 64 gate rows and their 64 up rows, so
   N / 64 tiles; otherwise ceil(N / 128)) and K into ceil(K / 64) chunks; a unit is one (tile,
   chunk), numbered tile-major: u = tile * nchunks + chunk;
-* with C requested CTAs (the SM count by default, at most one per unit), every CTA takes
+* with C requested CTAs (by default the SM count times the resident CTAs per SM, one with this
+  kernel's shared memory; at most one per unit), every CTA takes
   per = ceil(units / C) consecutive units; the grid is ceil(units / per) CTAs;
 * CTA c's run [c per, min((c+1) per, units)) falls into segments, one per tile it touches; a
   segment that is not a whole tile writes its fp32 partial to workspace slot 2c (the CTA's first

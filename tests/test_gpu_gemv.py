@@ -287,5 +287,5 @@ def test_plan_matches_host_mirror(N, K, epi):
     sms = torch.cuda.get_device_properties(DEV).multi_processor_count
     op = Gemv(32, N, K, epi, device=DEV)
     plan = op._plans[op.grid][0]
-    want = gemv_split(N, K, swiglu=epi == EPI_SWIGLU, ctas=sms)
+    want = gemv_split(N, K, swiglu=epi == EPI_SWIGLU, ctas=sms * plan.ctas_per_sm)
     assert (plan.tiles, plan.units_per_cta, plan.grid) == (want.tiles, want.per, want.grid)
