@@ -1456,7 +1456,26 @@ int encode_kv_maps(Params& p, int B, int nkv) {
   return KOPT_OK;
 }
 
+// A plan is a plain struct that the caller may have edited or kept from another shape: its
+// fields must agree with each other before they size a launch. The kernels index the workspace by
+// chunk + pair (T = 1; chunks < grid + ceil(pages / 32)) or by CTA (T > 1), so grid, max_units and
+// the shape must be those kopt_decode_attn_plan would give together.
+int check_plan(const kopt_plan* plan) {
+  if (plan->B < 1 || plan->B > kMaxB || plan->T < 1 || plan->T > kVMaxT || plan->nkv < 1 ||
+      plan->grid < 1 || plan->max_len < 1 || plan->max_units < 1)
+    return KOPT_ERR_ARG;
+  const long long pairs = static_cast<long long>(plan->B) * plan->nkv;
+  if (plan->T > 1) {
+    if (plan->grid % pairs != 0 || plan->grid > plan->max_units) return KOPT_ERR_ARG;
+    return KOPT_OK;
+  }
+  const long long pages = pairs * ((static_cast<long long>(plan->max_len) + kPage - 1) / kPage);
+  const long long units = plan->grid + (pages + kChunkPages - 1) / kChunkPages + pairs;
+  return units <= plan->max_units ? KOPT_OK : KOPT_ERR_ARG;
+}
+
 int fill_ws(Params& p, const kopt_plan* plan, void* ws) {
+  if (check_plan(plan) != KOPT_OK) return KOPT_ERR_ARG;
   if (ws == nullptr || (reinterpret_cast<uintptr_t>(ws) & 255) != 0) return KOPT_ERR_WORKSPACE;
   const WsLayout w = ws_layout(plan);
   if (w.total != plan->ws_bytes) return KOPT_ERR_WORKSPACE;
@@ -1701,11 +1720,12 @@ namespace {
 int fused_launch(const kopt_plan* plan, const void* qkv, const void* q_norm_w, const void* k_norm_w,
                  const void* cos, const void* sin, int rope_len, const kopt_kv_cache* cache,
                  const int32_t* pos, void* out, const kopt_gather* g, void* q_out, void* ws,
-                 float scale, float eps, void* stream) {
+                 float scale, float eps, void* stream, size_t clear_bytes = 0) {
   if (plan == nullptr || qkv == nullptr || q_norm_w == nullptr || k_norm_w == nullptr ||
       cos == nullptr || sin == nullptr || pos == nullptr || (g == nullptr && out == nullptr) ||
       rope_len < 1 || plan->T != 1)   // the fused prologue appends one token per sequence
     return KOPT_ERR_ARG;
+  if (plan->flags & ~KOPT_PLAN_OVERLAP_PREV) return KOPT_ERR_ARG;
   if (!aligned16(qkv) || (out && !aligned16(out)) || (q_out && !aligned16(q_out)) ||
       !aligned16(cos) || !aligned16(sin) || (reinterpret_cast<uintptr_t>(q_norm_w) & 7) ||
       (reinterpret_cast<uintptr_t>(k_norm_w) & 7))
@@ -1758,6 +1778,10 @@ int fused_launch(const kopt_plan* plan, const void* qkv, const void* q_norm_w, c
   if (rc) return rc;
   rc = encode_kv_maps(p, plan->B, plan->nkv);
   if (rc) return rc;
+  // every argument is checked: only now may a clear of the workspace header go on the stream
+  if (clear_bytes > 0 &&
+      cudaMemsetAsync(ws, 0, clear_bytes, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return KOPT_ERR_CUDA;
   return p.bt ? launch_attn<true, true>(plan, p, stream) : launch_attn<false, true>(plan, p, stream);
 }
 }  // namespace
@@ -1898,7 +1922,13 @@ extern "C" int kopt_decode_attn_fused_noalloc(
     const int32_t* pos, void* out, void* q_out, float scale, float eps, int* dev_err,
     void* stream) {
   if (plan == nullptr) return KOPT_ERR_ARG;
-  if (plan->ws_bytes > static_cast<int64_t>(kStaticScratchBytes)) return KOPT_ERR_SCRATCH;
+  // The plan is a plain struct the caller may have edited: its shape fields, not only ws_bytes,
+  // decide how much of the buffer the kernel and the clear below touch, so they are checked
+  // against each other and against the buffer before anything is queued.
+  if (plan->T != 1 || check_plan(plan) != KOPT_OK) return KOPT_ERR_ARG;
+  const WsLayout w = ws_layout(plan);
+  if (w.total != plan->ws_bytes) return KOPT_ERR_WORKSPACE;
+  if (w.total > static_cast<int64_t>(kStaticScratchBytes)) return KOPT_ERR_SCRATCH;
   int rc = set_device(plan->device);
   if (rc) return rc;
   void* ws = nullptr;
@@ -1906,11 +1936,10 @@ extern "C" int kopt_decode_attn_fused_noalloc(
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // The buffer keeps the previous call's contents: the error word and the split counters must
-  // start at zero (the partial-result slots need no initial value).
-  const WsLayout w = ws_layout(plan->B, plan->nkv, plan->max_units);
-  if (cudaMemsetAsync(ws, 0, static_cast<size_t>(w.ml), st) != cudaSuccess) return KOPT_ERR_CUDA;
-  rc = kopt_decode_attn_fused(plan, qkv, q_norm_w, k_norm_w, cos, sin, rope_len, cache, pos, out,
-                              q_out, ws, scale, eps, stream);
+  // start at zero (the partial-result slots need no initial value). The clear is queued by the
+  // launch itself, after every argument has been checked, right before the kernel.
+  rc = fused_launch(plan, qkv, q_norm_w, k_norm_w, cos, sin, rope_len, cache, pos, out, nullptr,
+                    q_out, ws, scale, eps, stream, static_cast<size_t>(w.ml));
   if (rc) return rc;
   if (dev_err != nullptr &&
       cudaMemcpyAsync(dev_err, ws, sizeof(int), cudaMemcpyDeviceToDevice, st) != cudaSuccess)

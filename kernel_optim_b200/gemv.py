@@ -170,7 +170,8 @@ class Gemv:
     def candidates(self) -> list[int]:
         """Grid sizes worth timing: the library's one resident wave first, then fractions of it."""
         auto = self._plan(0)
-        sms = auto.grid // max(auto.ctas_per_sm, 1)
+        # the device's SM count: auto.grid is clipped to the unit count for small projections
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         out = [auto.grid] + [self._plan(c).grid for c in (sms, 3 * sms // 2, 3 * sms) if c > 0]
         return list(dict.fromkeys(out))
 

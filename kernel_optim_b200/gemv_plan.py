@@ -1,7 +1,13 @@
 """Host mirror of the work split of the skinny-GEMM kernel (csrc/gemv.cu).
 
 kopt_gemv_plan_make and gemv_kernel divide a projection between CTAs as follows; this module
-restates that arithmetic so the split can be inspected and property-tested without a GPU:
+restates that arithmetic so the split can be inspected and property-tested without a GPU. The
+lines of csrc/gemv.cu restated here (a change there must be mirrored here):
+
+* gemv_split       <- kopt_gemv_plan_make, gemv.cu:897-930 (tiles, units, per, grid)
+* GemvSplit.run    <- gemv_kernel, gemv.cu:312-314 (a CTA's unit run)
+* write_slot       <- gemv.cu:529-542 (a split segment's partial slot and the tile counter)
+* holders, read_slot <- gemv.cu:548-590 (the merge's CTAs kfirst .. klast and kfirst_seg)
 
 * the weight is cut into tiles of 128 rows (SWIGLU: 64 gate rows and their 64 up rows, so
   N / 64 tiles; otherwise ceil(N / 128)) and K into ceil(K / 64) chunks; a unit is one (tile,

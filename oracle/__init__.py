@@ -11,7 +11,8 @@ Contents
                 summation order, and the Transformers Qwen3 modules it must agree with.
 * attention.py  fp32 SDPA decode-attention oracle (the north-star tolerance target), and a numpy
                 restatement of the reference's split-K kernel + LSE combine (fused.py:138-234).
-* inputs.py     seeded synthetic inputs for the five BASELINE configurations.
+* epilogue.py   restatement of the decode step's row kernels and projection epilogues (add +
+                RMSNorm, SwiGLU, residual, LM-head argmax) in the reference's cast order.
 * cpu_path.py   the reference's CPU path (Transformers' sdpa attention, repeat_kv and enable_gqa
                 forms) used as the timed CPU baseline.
 

@@ -103,3 +103,64 @@ def test_gemv_rejects_null_arguments(lib):
     assert lib.kopt_gemv_fused(ctypes.byref(plan), None, None, None, None, None, None) == _lib.KOPT_ERR_ARG
     err = ctypes.c_int(0)
     assert lib.kopt_gemv_read_error(None, None, ctypes.byref(err), None) == _lib.KOPT_ERR_ARG
+
+
+def _hand_plan(B=4, nkv=8, grid=148, max_len=2048, T=1):
+    """A T = 1 plan filled by hand the way kopt_decode_attn_plan fills it (no GPU needed):
+    max_units = grid + ceil(pages / 32) + B * nkv, and the workspace layout of decode_attn.cu
+    (256-byte header, counters, (m, l) pairs and 4 x 128 fp32 partials per unit slot)."""
+    plan = _lib.Plan()
+    pages = B * nkv * ((max_len + 15) // 16)
+    plan.B, plan.T, plan.nkv, plan.grid, plan.max_len = B, T, nkv, grid, max_len
+    plan.max_units = grid + (pages + 31) // 32 + B * nkv
+    plan.ctas_per_sm, plan.device, plan.static_pct = 1, 0, 100
+    plan.ws_bytes = _ws_bytes(B, nkv, plan.max_units)
+    return plan
+
+
+def _ws_bytes(B, nkv, units, rows=4):
+    a256 = lambda x: (x + 255) & ~255
+    return 256 + a256(B * nkv * 4) + a256(units * rows * 8) + units * rows * 128 * 4
+
+
+def _noalloc(lib, plan):
+    cache = _lib.KvCache()
+    return lib.kopt_decode_attn_fused_noalloc(ctypes.byref(plan), None, None, None, None, None, 1,
+                                              ctypes.byref(cache), None, None, None, 1.0, 1e-6,
+                                              None, None)
+
+
+def test_noalloc_rejects_edited_plans_before_queuing_anything(lib):
+    """The allocation-free entry point clears part of its built-in buffer before the launch; a
+    plan whose fields disagree must be turned away before that (and before any CUDA call, which is
+    why this runs without a GPU)."""
+    plan = _hand_plan()
+    plan.B = 64                      # batch edited, slots and workspace left as they were
+    assert _noalloc(lib, plan) == _lib.KOPT_ERR_ARG
+    plan = _hand_plan()
+    plan.max_units *= 4              # more slots than ws_bytes pays for
+    assert _noalloc(lib, plan) == _lib.KOPT_ERR_WORKSPACE
+    plan = _hand_plan()
+    plan.T = 2                       # the fused prologue appends one token per sequence
+    assert _noalloc(lib, plan) == _lib.KOPT_ERR_ARG
+    plan = _hand_plan()
+    plan.grid = 4 * plan.grid        # more CTAs than the unit slots were sized for
+    assert _noalloc(lib, plan) == _lib.KOPT_ERR_ARG
+    big = _hand_plan(B=4, max_len=131072)   # consistent, but above the 8 MiB buffer
+    assert big.ws_bytes > 8 << 20
+    assert _noalloc(lib, big) == _lib.KOPT_ERR_SCRATCH
+
+
+def test_workspace_launchers_reject_inconsistent_plans(lib):
+    """The same consistency check guards the entry points that take a caller's workspace: an
+    edited grid would index unit slots past the end of the workspace."""
+    buf = ctypes.create_string_buffer(1024)
+    base = (ctypes.addressof(buf) + 255) & ~255      # host addresses: never dereferenced here
+    cache = _lib.KvCache()
+    cache.k = cache.v = base
+    cache.cap = 16
+    for grid, expect in ((148, _lib.KOPT_ERR_CUDA), (4 * 148, _lib.KOPT_ERR_ARG)):
+        plan = _hand_plan()
+        plan.grid = grid             # 148: consistent, so the call gets as far as the device query
+        assert lib.kopt_decode_attn(ctypes.byref(plan), base, ctypes.byref(cache), base, base,
+                                    base, 1.0, None) == expect
