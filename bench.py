@@ -22,6 +22,10 @@ on the same config, rank 0 only.
 
 Other workloads: c3/c4 (longer contexts), v3/v5/v7 (the T > 1 verify step), c5 (the engine end to
 end, tokens/s) and p5 (the projections of one decode step on the skinny-GEMM kernel, TB/s).
+
+The c2 line also carries `c4_strong`: config c4 (B=4, 131072 keys) strong-scaled over the N GPUs,
+each keeping 8/N kv heads of every sequence, with the head outputs all-gathered in the kernel; its
+`value` is the whole job's algorithmic bytes per call over the device time (max over ranks).
 """
 
 from __future__ import annotations
@@ -73,6 +77,8 @@ def parse_args():
                          "tcgen05 skinny-GEMM projections with fused epilogues (kopt_gemv)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="c2: skip the extra c4 strong-scaling measurement (key c4_strong)")
     ap.add_argument("--soak-ms", type=float, default=600.0,
                     help="untimed launches before the timed region, for the clock samples")
     return ap.parse_args()
@@ -320,6 +326,9 @@ def run_ours(args):
                 "algorithmic_bytes_per_launch": bytes_rank}
 
     e2e = None if args.no_e2e else run_e2e(args, case, attn, out, gathered, pg, dist, bytes_job)
+    strong = None
+    if args.workload == "c2" and not args.no_strong and args.layout == "paged":
+        strong = run_strong_c4(args, dist, n, rank, dev)
     cpu = None
     if n == 1 and rank == 0 and not args.no_cpu_baseline and args.layout == "paged" and case.fused:
         cpu = cpu_baseline(case, bytes_rank)
@@ -351,6 +360,8 @@ def run_ours(args):
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
+    if strong is not None:
+        line["c4_strong"] = strong
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:
@@ -358,6 +369,57 @@ def run_ours(args):
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_strong_c4(args, dist, n, rank, dev):
+    """Config c4 strong-scaled over the N ranks: B = 4 sequences of 131072 keys in total, rank r
+    keeping kv heads [r 8/N, (r+1) 8/N) of every sequence (and their query heads), the head outputs
+    all-gathered inside the kernel over NVLink (N > 1). Back-to-back calls over two layer caches,
+    CUDA events on the launching stream, max over ranks; value = the job's algorithmic bytes
+    (2 GiB of K/V per call, whatever N) over that time."""
+    from kernel_optim_b200.paged import PagedDecodeAttention
+    from kernel_optim_b200.workloads import build_case
+    layers = 2
+    case = build_case("c4", dev, seed=0, paged=True, batch_scale=1, kv_shard=n, kv_rank=rank,
+                      layers=layers)
+    t = case.tensors
+    attn = PagedDecodeAttention(case.B, case.nq, case.nkv, 128, dev, t["cache"].capacity,
+                                overlap_prev=not args.no_overlap)
+    out = torch.empty(case.B, case.nq * 128, dtype=torch.bfloat16, device=dev)
+    pg = None
+    if n > 1:
+        from kernel_optim_b200.gather import PeerGather
+        pg = PeerGather(case.B, n * case.nq * 128, dev)
+    try:
+        launch = StepLauncher(case, attn, layers, out, gather=pg)
+        steps = max(4, min(args.steps, 40))
+        for i in range(max(args.warmup, 3)):
+            launch(i)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            launch(i)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(dist, e0.elapsed_time(e1)) / steps
+        err = attn.read_error()
+        if err:
+            raise RuntimeError(f"device error word {err} in the c4 strong-scaling run")
+        bytes_job = case.algorithmic_bytes() * n
+        return {"workload": "c4 strong-scaled: B=4 sequences of 131072 keys in total, kv heads "
+                            "sharded 8/N per GPU, head outputs all-gathered in the kernel",
+                "kv_heads_per_gpu": case.nkv, "us_per_call": round(ms * 1e3, 2),
+                "value": round(bytes_job / (ms * 1e-3) / 1e12, 4), "unit": "TB/s",
+                "steps": steps, "algorithmic_bytes_per_call": bytes_job}
+    finally:
+        if pg is not None:
+            if dist is not None:
+                dist.barrier()
+            pg.close()
 
 
 def run_e2e(args, case, attn, out, gathered, pg, dist, bytes_job):

@@ -42,7 +42,7 @@ extern "C" {
  * a bad page id or length is recorded here and the access is skipped or clamped. */
 #define KOPT_DEV_ERR_PAGE 1    /* block-table entry outside [0, num_pages) */
 #define KOPT_DEV_ERR_LEN 2     /* pos[b] + T outside [1, cap] (clamped) */
-#define KOPT_DEV_ERR_TIMEOUT 4 /* an mbarrier wait ran past its time limit */
+#define KOPT_DEV_ERR_TIMEOUT 4 /* an mbarrier wait or the gather's flag wait ran past its limit */
 #define KOPT_DEV_ERR_ROPE 8    /* pos[b] + t outside the RoPE table (clamped) */
 #define KOPT_DEV_ERR_PLAN 16   /* internal work-split invariant violated (work skipped) */
 
@@ -167,7 +167,8 @@ KOPT_API int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, cons
  * output row straight into every rank's gathered buffer (plain stores over NVLink through CUDA IPC
  * mappings), at column offset r * nq_local * 128. When all its CTAs are done, the last one raises
  * flags[w][r] = epoch + 1 on every rank w, then waits until every rank's flag in its own array has
- * reached epoch + 1 (bounded, 1 s; KOPT_DEV_ERR_TIMEOUT in the workspace error word on expiry) and
+ * reached epoch + 1 (bounded by wait_ns, 1 s by default; KOPT_DEV_ERR_TIMEOUT in the workspace
+ * error word on expiry, after which the call still completes and its own rows are in place) and
  * advances the epoch: once the call completes on a stream, the gathered rows of all ranks are in
  * this rank's buffer. Every rank must make the same calls in the same order. This takes the place
  * of a separate all-gather (NCCL) of the head outputs between attention and o_proj, which the
@@ -182,6 +183,8 @@ typedef struct kopt_gather {
   int32_t rank;
   int32_t world;               /* 1 .. KOPT_MAX_RANKS */
   int64_t row_elems;           /* elements per gathered row: nq_total * 128 */
+  int64_t wait_ns;             /* bound of the last CTA's wait for the peers' flags, in ns:
+                                  0 = the default 1 s; at most 10 s (KOPT_ERR_ARG above) */
 } kopt_gather;
 
 /* kopt_decode_attn_fused whose output goes to every rank's gathered buffer (see above); plan->T 1. */

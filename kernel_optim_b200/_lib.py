@@ -109,6 +109,7 @@ class Gather(ctypes.Structure):
         ("rank", ctypes.c_int32),
         ("world", ctypes.c_int32),
         ("row_elems", ctypes.c_int64),
+        ("wait_ns", ctypes.c_int64),
     ]
 
 

@@ -86,6 +86,7 @@ struct Params {
   int* flag_peer[kMaxRanks];
   int* epoch;            // this rank's call counter, advanced by the last CTA
   long long out_row;     // elements per output row
+  unsigned long long wait_ns;   // bound of the gather's flag wait
   int out_col;           // this rank's first column
   int rank, world;       // world == 0: no gather, write `out`
   float* ws_o;           // [max_units, 4, 128]
@@ -342,7 +343,7 @@ __device__ __forceinline__ long long row_offset(const Params& p, int b, int kvh,
 // Fused gather, run by the last CTA of this rank once every CTA's rows are out: raise this rank's
 // flag on every rank (release at system scope, after a system fence covering the rows that the
 // other CTAs ordered before their counter increment), then wait until every rank's flag for this
-// call is up here (acquire; bounded at 1 s, KOPT_DEV_ERR_TIMEOUT on expiry), so that this
+// call is up here (acquire; bounded by p.wait_ns, KOPT_DEV_ERR_TIMEOUT on expiry), so that this
 // kernel's completion means the whole gathered row block has landed in local memory. The peers are
 // other GPUs running the same kernel; nothing here waits on work of this GPU.
 __device__ __noinline__ void gather_signal_and_wait(const Params& p) {
@@ -358,7 +359,7 @@ __device__ __noinline__ void gather_signal_and_wait(const Params& p) {
       int f;
       asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(f) : "l"(mine + w) : "memory");
       if (f >= e) break;
-      if (globaltimer() - t0 > kTimeoutNs) {
+      if (globaltimer() - t0 > p.wait_ns) {
         atomicOr(p.ws_err, KOPT_DEV_ERR_TIMEOUT);
         break;
       }
@@ -1563,7 +1564,7 @@ using namespace kopt;
 
 extern "C" {
 
-int kopt_abi_version(void) { return 1; }
+int kopt_abi_version(void) { return 2; }
 
 const char* kopt_strerror(int status) {
   switch (status) {
@@ -1753,7 +1754,7 @@ int fused_launch(const kopt_plan* plan, const void* qkv, const void* q_norm_w, c
   } else {
     if (g->world < 1 || g->world > kMaxRanks || g->rank < 0 || g->rank >= g->world ||
         g->epoch == nullptr || g->row_elems < (g->rank + 1) * heads || g->row_elems % 8 != 0 ||
-        plan->T != 1)
+        plan->T != 1 || g->wait_ns < 0 || g->wait_ns > 10 * static_cast<long long>(kTimeoutNs))
       return KOPT_ERR_ARG;
     for (int w = 0; w < g->world; ++w) {
       if (g->out[w] == nullptr || g->flags[w] == nullptr || !aligned16(g->out[w]))
@@ -1767,6 +1768,7 @@ int fused_launch(const kopt_plan* plan, const void* qkv, const void* q_norm_w, c
     p.world = g->world;
     p.out_row = g->row_elems;
     p.out_col = static_cast<int>(g->rank * heads);
+    p.wait_ns = g->wait_ns > 0 ? static_cast<unsigned long long>(g->wait_ns) : kTimeoutNs;
   }
   p.B = plan->B;
   p.T = plan->T;

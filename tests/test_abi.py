@@ -34,7 +34,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_strerror(lib):
-    assert lib.kopt_abi_version() == 1
+    assert lib.kopt_abi_version() == 2
     assert lib.kopt_strerror(0) == b"ok"
     assert b"argument" in lib.kopt_strerror(_lib.KOPT_ERR_ARG)
     assert lib.kopt_strerror(999) == b"unknown kopt status"
@@ -44,8 +44,8 @@ def test_struct_layouts_match_header():
     # kopt_kv_cache: 2 pointers, 2 int64, 2 int32, pointer, 2 int32 -> 56 bytes on LP64
     assert ctypes.sizeof(_lib.KvCache) == 56
     assert ctypes.sizeof(_lib.Plan) == 56
-    # kopt_gather: 8 + 8 pointers, pointer, 2 int32, int64 -> 152 bytes
-    assert ctypes.sizeof(_lib.Gather) == 152
+    # kopt_gather: 8 + 8 pointers, pointer, 2 int32, 2 int64 -> 160 bytes
+    assert ctypes.sizeof(_lib.Gather) == 160
     # kopt_gemv_plan: 10 int32, int64 -> 48 bytes
     assert ctypes.sizeof(_lib.GemvPlan) == 48
     # kopt_gemv_fuse: 2 pointers, int32, float, pointer -> 32 bytes
@@ -154,13 +154,19 @@ def test_noalloc_rejects_edited_plans_before_queuing_anything(lib):
 def test_workspace_launchers_reject_inconsistent_plans(lib):
     """The same consistency check guards the entry points that take a caller's workspace: an
     edited grid would index unit slots past the end of the workspace."""
+    # Host addresses stand in for device buffers: the plan check must turn the call away before
+    # anything reaches the device (only an inconsistent plan is ever passed with them, so nothing
+    # is launched on a machine with a GPU either).
     buf = ctypes.create_string_buffer(1024)
-    base = (ctypes.addressof(buf) + 255) & ~255      # host addresses: never dereferenced here
+    base = (ctypes.addressof(buf) + 255) & ~255
     cache = _lib.KvCache()
     cache.k = cache.v = base
     cache.cap = 16
-    for grid, expect in ((148, _lib.KOPT_ERR_CUDA), (4 * 148, _lib.KOPT_ERR_ARG)):
-        plan = _hand_plan()
-        plan.grid = grid             # 148: consistent, so the call gets as far as the device query
-        assert lib.kopt_decode_attn(ctypes.byref(plan), base, ctypes.byref(cache), base, base,
-                                    base, 1.0, None) == expect
+    plan = _hand_plan()
+    plan.grid = 4 * plan.grid
+    assert lib.kopt_decode_attn(ctypes.byref(plan), base, ctypes.byref(cache), base, base,
+                                base, 1.0, None) == _lib.KOPT_ERR_ARG
+    plan = _hand_plan()
+    plan.max_units -= 1              # one slot short of what the grid and the batch need
+    assert lib.kopt_decode_attn(ctypes.byref(plan), base, ctypes.byref(cache), base, base,
+                                base, 1.0, None) == _lib.KOPT_ERR_ARG

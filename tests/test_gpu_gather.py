@@ -165,3 +165,60 @@ def test_fused_gather_two_ranks_over_nvlink():
     results = {r: ([_tensor(a) for a in e], [[_tensor(a) for a in x] for x in g],
                    [_tensor(a) for a in lo], err) for r, (e, g, lo, err) in results.items()}
     _check(results, world, _unsharded(torch.device("cuda:0")))
+
+
+def test_gather_flag_wait_runs_out_on_one_gpu():
+    """The fused gather's bounded flag wait, made to run out on purpose without a second GPU: a
+    world-2 descriptor whose "peer" buffers are a second local allocation that no kernel ever
+    signals. The call must complete, set KOPT_DEV_ERR_TIMEOUT (and nothing else), still store this
+    rank's rows into both buffers and raise its flag in both flag arrays; after the error word is
+    read and cleared, a world-1 call on the same workspace is correct again. Nothing hangs: the
+    wait is bounded at 5 ms here (the descriptor's wait_ns)."""
+    import ctypes
+
+    from kernel_optim_b200 import _lib
+    from kernel_optim_b200.fused import _ptr, _stream
+    from kernel_optim_b200.paged import PagedDecodeAttention
+    from kernel_optim_b200.workloads import build_case
+
+    dev = torch.device("cuda:0")
+    case = build_case("c2", dev, seed=5, paged=True, kv_shard=2, kv_rank=0, layers=1)
+    t = case.tensors
+    B, nq_l, nkv_l = case.B, case.nq, case.nkv
+    cache = t["cache"]
+    attn = PagedDecodeAttention(B, nq_l, nkv_l, 128, dev, cache.capacity)
+    args = (t["qkv"], t["q_norm_w"], t["k_norm_w"], t["cos"], t["sin"], cache)
+    plain = torch.empty(B, nq_l * 128, dtype=torch.bfloat16, device=dev)
+    attn(*args, 0, t["pos"], plain)
+    torch.cuda.synchronize(dev)
+    assert attn.read_error() == 0
+    row = 2 * nq_l * 128
+    outs = [torch.zeros(B, row, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    flags = [torch.zeros(64, dtype=torch.int32, device=dev) for _ in range(2)]
+    epoch = torch.zeros(64, dtype=torch.int32, device=dev)
+
+    def call(world, wait_ns):
+        g = _lib.Gather()
+        for w in range(world):
+            g.out[w], g.flags[w] = outs[w].data_ptr(), flags[w].data_ptr()
+        g.epoch, g.rank, g.world, g.row_elems, g.wait_ns = epoch.data_ptr(), 0, world, row, wait_ns
+        _lib.check(_lib.lib().kopt_decode_attn_fused_gather(
+            ctypes.byref(attn.plan), _ptr(t["qkv"]), _ptr(t["q_norm_w"]), _ptr(t["k_norm_w"]),
+            _ptr(t["cos"]), _ptr(t["sin"]), t["cos"].shape[0], ctypes.byref(attn._cache(cache, 0)),
+            _ptr(t["pos"]), ctypes.byref(g), None, _ptr(attn.ws), ctypes.c_float(attn.scale),
+            ctypes.c_float(attn.eps), _stream(dev)), "kopt_decode_attn_fused_gather")
+
+    call(2, 5_000_000)
+    torch.cuda.synchronize(dev)
+    assert attn.read_error() == _lib.DEV_ERR_TIMEOUT   # read_error also clears the word
+    for w in range(2):
+        assert torch.equal(outs[w][:, : nq_l * 128], plain), f"rows missing in buffer {w}"
+        assert int(flags[w][0]) == 1, f"flag not raised in array {w}"
+    assert int(flags[0][1]) == 0 and int(epoch[0]) == 1
+    outs[0].zero_()
+    flags[0].zero_()
+    epoch.zero_()
+    call(1, 0)   # default bound; its own flag is the only one it waits for
+    torch.cuda.synchronize(dev)
+    assert attn.read_error() == 0
+    assert torch.equal(outs[0][:, : nq_l * 128], plain)
