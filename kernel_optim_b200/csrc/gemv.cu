@@ -227,76 +227,11 @@ __device__ __forceinline__ float silu_bf16(float g) {   // bf16(g / (1 + exp(-g)
   return bf16r(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
 }
 
-// Bulk copy global -> shared (no tensor map, no multicast), completion counted on an mbarrier.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst),
-      "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
-}
-
-// ---- tcgen05 (tensor memory + 5th-generation MMA) helpers
-__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// Shared-memory matrix descriptor: K-major tile written by TMA with the 128-byte swizzle, rows of
-// 128 bytes, 8-row groups 1024 bytes apart (stride byte offset); the leading byte offset is not
-// used by swizzled K-major layouts; version 1 (bits 46-47); layout 2 = 128-byte swizzle (61-63).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
-         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
-         (static_cast<uint64_t>(2) << 61);
-}
 // Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), A and B bf16 (7-9, 10-12 =
 // 1), both K-major (15, 16 = 0), N >> 3 (17-22), M >> 4 (24-28).
 __host__ __device__ constexpr uint32_t gemv_idesc(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(kGRows >> 4) << 24);
-}
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                          uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive once on the mbarrier when every tcgen05.mma this thread issued so far has completed.
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
-}
-// 16 consecutive fp32 columns of this thread's tensor-memory lane; the wait is in the same
-// statement, so the registers are complete when the statement ends.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* r) {
-  uint32_t v[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15}, [%16];\n\ttcgen05.wait::ld.sync.aligned;"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-        "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr)
-      : "memory");
-#pragma unroll
-  for (int j = 0; j < 16; ++j) r[j] = __uint_as_float(v[j]);
 }
 
 template <int MT, int EPI>
