@@ -202,6 +202,21 @@ KOPT_API int kopt_ipc_get_handle(const void* ptr, void* handle /* KOPT_IPC_HANDL
 KOPT_API int kopt_ipc_open(int device, const void* handle, void** peer_ptr);
 KOPT_API int kopt_ipc_close(int device, void* peer_ptr);
 
+/* ---- prefill: causal GQA attention over the prompt --------------------------------------- *
+ * out[b*S + s, h] = softmax over keys 0 .. s of (q[b*S + s, h] . K[b, h/4, key] * scale), times
+ * V[b, h/4, key], for B prompts of S tokens each. q, out: [B*S, nq*128] bf16 row-major, 16-byte
+ * aligned; q as kopt_qk_norm_rope writes it (normed, roped). The prompt's K/V are read from
+ * positions 0 .. S-1 of `cache` (paged or contiguous), where kopt_qk_norm_rope writes them when
+ * called with pos = 0 and T = S. dev_err: device int, KOPT_DEV_ERR_* bits OR-ed in (a bad page id
+ * is recorded and page 0 read instead; a wait that runs out records KOPT_DEV_ERR_TIMEOUT). On the
+ * tcgen05 tensor cores: S = Q K^T and O += P V in tensor memory, K/V tiles fed by TMA, fp32 online
+ * softmax. Allocates nothing; not for use while another launch holds this GPU's tensor memory.
+ * Replaces F.scaled_dot_product_attention(q, k, v, is_causal=True) with GQA in Engine._prefill
+ * (engine/engine.py:376-377). */
+KOPT_API int kopt_prefill_attn(const void* q, const kopt_kv_cache* cache, void* out, int B, int S,
+                               int nq, int nkv, int d, float scale, int* dev_err, int device,
+                               void* stream);
+
 /* kopt_decode_attn_fused without a workspace argument, for callers that cannot allocate device
  * memory for it (an engine that owns the whole memory budget and hands out only fixed buffers, a
  * process whose allocator must not grow after start-up, a plugin host without a device allocator

@@ -37,6 +37,7 @@ EXPORTED = (
     "kopt_qk_norm_rope",
     "kopt_decode_attn_fused",
     "kopt_decode_attn_fused_noalloc",
+    "kopt_prefill_attn",
     "kopt_decode_attn_fused_gather",
     "kopt_ipc_alloc",
     "kopt_ipc_free",
@@ -160,6 +161,8 @@ _SIGS = {
                                  _i32, _i32, _i32, _i32, _i32, _f32, _vp, _i32, _vp]),
     "kopt_decode_attn_fused": (_i32, [ctypes.POINTER(Plan), _vp, _vp, _vp, _vp, _vp, _i32,
                                       ctypes.POINTER(KvCache), _vp, _vp, _vp, _vp, _f32, _f32, _vp]),
+    "kopt_prefill_attn": (_i32, [_vp, ctypes.POINTER(KvCache), _vp, _i32, _i32, _i32, _i32, _i32,
+                                 ctypes.c_float, _vp, _i32, _vp]),
     "kopt_decode_attn_fused_noalloc": (_i32, [ctypes.POINTER(Plan), _vp, _vp, _vp, _vp, _vp, _i32,
                                               ctypes.POINTER(KvCache), _vp, _vp, _vp, _f32, _f32,
                                               _vp, _vp]),

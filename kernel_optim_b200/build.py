@@ -20,7 +20,7 @@ INCLUDE = ROOT / "include"
 LIB = PKG / "libkopt.so"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["decode_attn.cu", "gemv.cu"]
+SOURCES = ["decode_attn.cu", "gemv.cu", "prefill_attn.cu"]
 
 
 def nvcc_path() -> str:

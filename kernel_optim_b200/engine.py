@@ -31,8 +31,9 @@ from __future__ import annotations
 import torch
 
 from ._lib import KoptError
-from .paged import PAGE, PagedDecodeAttention, PagedKVCache
+from .paged import PAGE, PagedDecodeAttention, PagedKVCache, qk_norm_rope_paged
 from .fused import add_rms_norm, qk_norm_rope, silu_mul
+from .prefill import prefill_attention
 from .gather import PeerGather, slot_of
 from .gemv import EPI_ARGMAX, EPI_BF16, EPI_RESID, EPI_SWIGLU, Gemv
 from .shard import head_range, shard_qkv_weight
@@ -246,34 +247,45 @@ class Engine:
     def _prefill_native(self, prompt):
         """Prefill on the row kernels of the decode step, Qwen3DecoderLayer's cast order: per layer
         the residual add + input RMSNorm (add_rms_norm), one QKV GEMM, the q/k RMSNorm + RoPE
-        prologue (kopt_qk_norm_rope) writing the prompt's K/V, causal GQA attention (torch SDPA),
-        o_proj, residual add + post-attention RMSNorm, gate|up GEMM, SwiGLU (silu_mul), down_proj;
-        this rank's K/V heads go into the pages. Only the last position goes through the final
-        norm and the LM head (the reference's prefill keeps only its logits too)."""
+        prologue (kopt_qk_norm_rope), causal GQA attention, o_proj, residual add +
+        post-attention RMSNorm, gate|up GEMM, SwiGLU (silu_mul), down_proj. On one GPU the prologue
+        writes the prompt's K/V straight into the pages and the attention is the tcgen05 prefill
+        kernel reading them there (kopt_prefill_attn); sharded, every rank attends with all heads
+        (torch SDPA on the prologue's K/V) and keeps its own kv heads' K/V in its pages. Only the
+        last position goes through the final norm and the LM head (the reference's prefill keeps
+        only its logits too)."""
         B, S = prompt.shape
         H, nq, nkv, d = self.embed.shape[1], self.nq, self.nkv, self.d
         dev, bf, M = self.device, torch.bfloat16, B * S
         h = torch.index_select(self.embed, 0, prompt.reshape(-1))
         n = torch.empty_like(h)
         q = torch.empty(M, nq * d, dtype=bf, device=dev)
-        k = torch.empty(B, nkv, S, d, dtype=bf, device=dev)
-        v = torch.empty_like(k)
+        if self.world > 1:   # sharded: every head's K/V, for the all-head attention
+            k = torch.empty(B, nkv, S, d, dtype=bf, device=dev)
+            v = torch.empty_like(k)
         act = torch.empty(M, self.inter, dtype=bf, device=dev)
         pos0 = torch.zeros(B, dtype=torch.int32, device=dev)
         h0 = self.h0
         delta = None
+        attn = torch.empty(M, nq * d, dtype=bf, device=dev) if self.world == 1 else None
         for i, lw in enumerate(self.layers):
             add_rms_norm(h, delta, lw["w_in"], n, self.eps)
             qkv = torch.mm(n, self._qkv_full(i).t())
-            qk_norm_rope(qkv, lw["q_norm"], lw["k_norm"], self.cos, self.sin, pos0, q, k, v, S,
-                         self.eps, nq, nkv, d)
-            a = torch.nn.functional.scaled_dot_product_attention(
-                q.view(B, S, nq, d).transpose(1, 2), k, v, is_causal=True, enable_gqa=True)
-            o = torch.mm(a.transpose(1, 2).reshape(M, nq * d), lw["o"].t())
+            if self.world == 1:
+                qk_norm_rope_paged(qkv, lw["q_norm"], lw["k_norm"], self.cos, self.sin, pos0, q,
+                                   self.cache, i, S, self.eps, nq, nkv, d)
+                prefill_attention(q, self.cache, i, attn, B, S, nq, nkv, d)
+                o = torch.mm(attn, lw["o"].t())
+            else:
+                qk_norm_rope(qkv, lw["q_norm"], lw["k_norm"], self.cos, self.sin, pos0, q, k, v, S,
+                             self.eps, nq, nkv, d)
+                a = torch.nn.functional.scaled_dot_product_attention(
+                    q.view(B, S, nq, d).transpose(1, 2), k, v, is_causal=True, enable_gqa=True)
+                o = torch.mm(a.transpose(1, 2).reshape(M, nq * d), lw["o"].t())
+                self.cache.write_prefix(i, k[:, h0:h0 + self.nkv_l], v[:, h0:h0 + self.nkv_l])
             add_rms_norm(h, o, lw["w_post"], n, self.eps)
             silu_mul(torch.mm(n, lw["gu"].t()), act)
             delta = torch.mm(act, lw["down"].t())
-            self.cache.write_prefix(i, k[:, h0:h0 + self.nkv_l], v[:, h0:h0 + self.nkv_l])
         last = h.view(B, S, H)[:, -1].contiguous()
         nl = torch.empty_like(last)
         add_rms_norm(last, delta.view(B, S, H)[:, -1].contiguous(), self.final_norm, nl, self.eps)
