@@ -21,7 +21,8 @@ qkv and positions from pinned host memory, runs the step and copies the output b
 on the same config, rank 0 only.
 
 Other workloads: c3/c4 (longer contexts), v3/v5/v7 (the T > 1 verify step), c5 (the engine end to
-end, tokens/s) and p5 (the projections of one decode step on the skinny-GEMM kernel, TB/s).
+end, tokens/s), p5 (the projections of one decode step on the skinny-GEMM kernel, TB/s) and f5
+(the prefill attention of c5's prompts on the tcgen05 kernel, TFLOP/s).
 
 The c2 line also carries `c4_strong`: config c4 (B=4, 131072 keys) strong-scaled over the N GPUs,
 each keeping 8/N kv heads of every sequence, with the head outputs all-gathered in the kernel; its
@@ -58,7 +59,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "v3", "v5", "v7", "p5"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "v3", "v5", "v7", "p5", "f5"],
+                    default="c2",
                     help="c2-c4: one decode-attention call per step; c5: the engine end to end")
     ap.add_argument("--layers", type=int, default=8, help="layer caches rotated across steps")
     ap.add_argument("--layout", choices=["paged", "contiguous"], default="paged")
@@ -108,6 +110,15 @@ def max_over_ranks(dist, x: float) -> float:
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def tensor_peak():
+    """Dense bf16 tensor peak: the measured cuBLAS burst figure (a kernel timed alone)."""
+    try:
+        p = json.loads(PEAKS_FILE.read_text())
+        return float(p["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, cuBLAS burst)"
+    except Exception:
+        return 1590.0, "fallback 1.59 PFLOP/s (no MEASURED_PEAKS.json)"
 
 
 def peaks():
@@ -730,6 +741,135 @@ def run_proj(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------ f5: prefill attention (tcgen05)
+F5_METRIC = "prefill attention TFLOP/s (causal GQA, c5 prompts), us/call"
+
+
+def run_prefill(args):
+    """Workload f5: the attention of config c5's prefill, one call per layer: B = 32 prompts of
+    S = 1024 tokens, 32 query / 8 kv heads, d = 128, causal, on the tcgen05 kernel
+    (kopt_prefill_attn) over a paged cache (random page permutation) as the engine's prefill runs
+    it; four layers' q and K/V rotated (1.6 GB, far above L2). value: algorithmic FLOPs per call,
+    4 d per (query, key) pair with key <= query (S (S + 1) / 2 pairs per sequence and query
+    head: Q K^T and P V), over the device time. torch SDPA (its fastest backend for these
+    shapes, enable_gqa) on the same inputs is timed beside it as the library reference."""
+    from kernel_optim_b200.fused import qk_norm_rope_error
+    from kernel_optim_b200.paged import PagedKVCache
+    from kernel_optim_b200.prefill import prefill_attention
+    world, rank, local = dist_env()
+    dist = init_dist(world, local)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, S, NQ, NKV, D, L = 32, 1024, 32, 8, 128, 4
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(0)
+    cache = PagedKVCache(L, B * S // 16, NKV, D, B, S, dev)
+    cache.assign_permuted([S] * B, torch.Generator().manual_seed(1))
+    cache.k.normal_(generator=g)
+    cache.v.normal_(generator=g)
+    qs = [torch.randn(B * S, NQ * D, generator=g, device=dev).to(bf) for _ in range(L)]
+    out = torch.empty(B * S, NQ * D, dtype=bf, device=dev)
+    flops = B * NQ * 4 * D * S * (S + 1) // 2
+
+    def step(i):
+        prefill_attention(qs[i % L], cache, i % L, out, B, S, NQ, NKV, D)
+
+    def timed(fn, n):
+        for i in range(max(3, args.warmup)):
+            fn(i)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(n):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(dist, e0.elapsed_time(e1)) / n
+
+    sampler = ClockSampler(local)
+    t_end = time.perf_counter() + args.soak_ms / 1e3
+    i = 0
+    while time.perf_counter() < t_end:
+        step(i)
+        i += 1
+        if i % 16 == 0:
+            torch.cuda.synchronize()
+    ms = timed(step, args.steps)
+    clocks = sampler.stop()
+    err = qk_norm_rope_error(dev)
+    if err:
+        raise RuntimeError(f"device error word {err}")
+    # the library reference on the same inputs: contiguous [B, H, S, D] views for SDPA
+    kk = [torch.stack([cache.gather(j, b, S)[0] for b in range(B)]) for j in range(L)]
+    vv = [torch.stack([cache.gather(j, b, S)[1] for b in range(B)]) for j in range(L)]
+    qh = [q.view(B, S, NQ, D).transpose(1, 2) for q in qs]
+
+    def sdpa(i):
+        torch.nn.functional.scaled_dot_product_attention(qh[i % L], kk[i % L], vv[i % L],
+                                                         is_causal=True, enable_gqa=True)
+    ms_sdpa = timed(sdpa, max(4, args.steps // 2))
+    bf16_peak, peak_src = tensor_peak()
+    achieved = flops / (ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": bf16_peak,
+                "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 4), "traffic": ncu_traffic("f5"),
+                "peak_source": peak_src, "kernel": "prefill_attn_kernel<PAGED=1>",
+                "kernel_us": round(ms * 1e3, 2), "algorithmic_flops_per_launch": flops}
+
+    e2e = None
+    if not args.no_e2e:
+        # through the public call with host buffers: q from pinned memory in, the output back
+        host_q = torch.empty(B * S, NQ * D, dtype=bf, pin_memory=True)
+        host_q.copy_(qs[0].cpu())
+        host_o = torch.empty_like(host_q, pin_memory=True)
+        n_e2e = max(2, min(args.steps, 6))
+
+        def e2e_step(i):
+            qs[0].copy_(host_q, non_blocking=True)
+            prefill_attention(qs[0], cache, 0, out, B, S, NQ, NKV, D)
+            host_o.copy_(out, non_blocking=True)
+        ms_e2e = timed(e2e_step, n_e2e)
+        e2e = {"value": round(world * flops / (ms_e2e * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+               "us_per_call": round(ms_e2e * 1e3, 1), "h2d_bytes_per_step": host_q.numel() * 2,
+               "d2h_bytes_per_step": host_o.numel() * 2, "steps": n_e2e}
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        # the reference's CPU path for the same attention (torch SDPA, causal, GQA) on one sequence
+        qc, kc, vc = qh[0][:1].cpu(), kk[0][:1].cpu(), vv[0][:1].cpu()
+        t0 = time.perf_counter()
+        reps = 0
+        while reps < 1 or time.perf_counter() - t0 < 10.0:
+            torch.nn.functional.scaled_dot_product_attention(qc, kc, vc, is_causal=True, enable_gqa=True)
+            reps += 1
+        secs = (time.perf_counter() - t0) / reps
+        cpu = {"value": round(flops / B / secs / 1e12, 5), "unit": "TFLOP/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"one of the 32 sequences (bf16 torch SDPA, causal, enable_gqa, host) x{reps}, "
+                         f"{secs * 1e3:.1f} ms per sequence"}
+    line = {
+        "metric": F5_METRIC, "value": round(world * achieved, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "us_per_call": round(ms * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) bf16 q and K/V cache, paged with a random page permutation",
+        "config": {"workload": "f5 prefill attention (c5 prompts)", "B": B, "S": S, "q_heads": NQ,
+                   "kv_heads": NKV, "head_dim": D, "causal": True, "paged": True, "layers_rotated": L,
+                   "parallelism": "replicas" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2: {L} layers' q and K/V in rotation"},
+        "roofline": roofline,
+        "library_reference": {"impl": "torch.nn.functional.scaled_dot_product_attention (enable_gqa, "
+                                      "is_causal) on contiguous copies", "us_per_call": round(ms_sdpa * 1e3, 1),
+                              "value": round(flops / (ms_sdpa * 1e-3) / 1e12, 2), "unit": "TFLOP/s"},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------------------------- c5: the engine
 def run_engine(args):
     """BASELINE config c5: random-init Qwen3-4B (std 0.02, seeded), B=32 prompts of 1024 uniform
@@ -804,6 +944,13 @@ def main():
     args = parse_args()
     if args.workload == "p5" and args.impl == "ours":
         run_proj(args)
+    elif args.workload == "f5" and args.impl == "ours":
+        run_prefill(args)
+    elif args.workload == "f5":
+        if dist_env()[1] == 0:
+            print(json.dumps({"impl": "reference", "unavailable": (
+                "the reference arm times the headline decode step (c2); the prefill attention's "
+                "CPU reference is timed in the f5 line's cpu_baseline")}), flush=True)
     elif args.workload == "p5":
         if dist_env()[1] == 0:
             print(json.dumps({"impl": "reference", "unavailable": (

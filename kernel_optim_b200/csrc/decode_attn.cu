@@ -1007,21 +1007,25 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(const __grid_constant
 // engine.py:403-415). Their K/V are already in the cache (qk_norm_rope appends all T). One CTA
 // takes one (pair, split of the keys) and all 4 T query rows of the pair (T tokens x the 4 heads
 // of the GQA group) on MT m16 MMA tiles (MT = 1 for T <= 4, 2 for T <= 8), so every key is read
-// once; 4 warps stream the split's pages round-robin through private 3-deep TMA rings, and the
-// split that finishes last merges the partials.
-constexpr int kVW = 4;                       // warps per verify CTA
-constexpr int kVThreads = kVW * 32;
+// once. 4 page streams go round-robin over the split's pages through 3-deep TMA rings; each stream
+// is consumed by MT warps, warp w taking row tile w / 4 of stream w % 4, so a warp carries one
+// tile's state whatever T is. A ring slot is refilled once all its consumers are done with it.
+// The split that finishes last merges the partials.
+constexpr int kVW = 4;                       // page streams per verify CTA
 constexpr int kVStages = 3;
 constexpr int kVMaxT = 8;
+template <int MT>
+__host__ __device__ constexpr int verify_threads() { return kVW * MT * 32; }
 
 template <int MT>
 struct __align__(1024) VSmem {
-  bf16 k[kVStages][kVW][2][kPage * kHalf];   // per warp and stage: one page, two 64-dim boxes
+  bf16 k[kVStages][kVW][2][kPage * kHalf];   // per stream and stage: one page, two 64-dim boxes
   bf16 v[kVStages][kVW][2][kPage * kHalf];
   alignas(16) bf16 q[16 * MT][kD + 8];       // query rows (padded rows: no ldmatrix conflicts)
   float red_m[kVW][16 * MT];
   float red_l[kVW][16 * MT];
-  unsigned long long full[kVStages][kVW];
+  unsigned long long full[kVStages][kVW];    // slot filled by the stream's TMA
+  unsigned long long empty[kVStages][kVW];   // slot consumed by the stream's MT warps
   int last;                                  // this CTA merges the splits of its pair
   volatile int abort;
 };
@@ -1039,8 +1043,9 @@ __device__ __forceinline__ void mma16816_full(float (&d)[4], uint32_t a0, uint32
 }
 
 template <bool PAGED, int MT>
-__global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(verify_threads<MT>()) verify_attn_kernel(const __grid_constant__ Params p) {
   constexpr int R = 16 * MT;                 // query rows
+  constexpr int NT = verify_threads<MT>();
   // the warps' partial outputs reuse the rings once every page is consumed
   static_assert(sizeof(float) * kVW * R * (kD + 4) <= sizeof(bf16) * 2 * kVStages * kVW * 2 * kPage * kHalf,
                 "verify partials do not fit in the rings");
@@ -1048,6 +1053,9 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
   VSmem<MT>& s = *reinterpret_cast<VSmem<MT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sw = warp % kVW;                 // this warp's page stream
+  const int mt = warp / kVW;                 // and its row tile
+  const bool issuer = mt == 0;               // the stream's first warp issues its copies
   const int nq = p.nkv * kGroup;
   const int split = blockIdx.x % p.nsplit;
   const int pair = blockIdx.x / p.nsplit;
@@ -1063,29 +1071,32 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
   const int s0 = split * per, s1 = min(Lb, s0 + per);   // this split's keys (s0 on a page edge)
   const int pg0 = s0 / kPage;
   const int npg = s1 > s0 ? ceil_div_i(s1, kPage) - pg0 : 0;
-  const int mine = npg > warp ? ceil_div_i(npg - warp, kVW) : 0;   // pages of this warp
+  const int mine = npg > sw ? ceil_div_i(npg - sw, kVW) : 0;   // pages of this stream
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kVStages; ++i)
-      for (int w = 0; w < kVW; ++w) mbar_init(smem_u32(&s.full[i][w]), 1);
+      for (int w = 0; w < kVW; ++w) {
+        mbar_init(smem_u32(&s.full[i][w]), 1);
+        mbar_init(smem_u32(&s.empty[i][w]), MT);
+      }
     s.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   const uint64_t pol = evict_first_policy();
 
-  // page ids of this warp's pages k = base + lane, 32 at a time
+  // page ids of this stream's pages k = base + lane, 32 at a time
   const int* bt_row = PAGED ? p.bt + static_cast<long long>(b) * p.bt_stride : nullptr;
   int win = 0, win_base = -32;
   auto issue = [&](int k) {
-    const int pg = pg0 + warp + k * kVW;
+    const int pg = pg0 + sw + k * kVW;
     int row = 0;
     bool ok = true;
     if (PAGED) {
       if (k >= win_base + 32) {
         win_base = k - (k & 31);
         const int kk = win_base + lane;
-        win = kk < mine ? bt_row[pg0 + warp + kk * kVW] : 0;
+        win = kk < mine ? bt_row[pg0 + sw + kk * kVW] : 0;
       }
       const int pid = __shfl_sync(0xffffffffu, win, k - win_base);
       if (pid < 0 || pid >= p.num_pages) ok = false;
@@ -1093,7 +1104,7 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
     }
     if (lane == 0) {
       const int slot = k % kVStages;
-      const uint32_t fb = smem_u32(&s.full[slot][warp]);
+      const uint32_t fb = smem_u32(&s.full[slot][sw]);
       if (!ok) {
         atomicOr(p.ws_err, KOPT_DEV_ERR_PAGE);
         mbar_arrive_expect_tx(fb, 0);
@@ -1103,8 +1114,8 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
       mbar_arrive_expect_tx(fb, 4u * kBoxBytes);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint32_t dk = smem_u32(&s.k[slot][warp][h][0]);
-        const uint32_t dv = smem_u32(&s.v[slot][warp][h][0]);
+        const uint32_t dk = smem_u32(&s.k[slot][sw][h][0]);
+        const uint32_t dv = smem_u32(&s.v[slot][sw][h][0]);
         if (PAGED) {
           tma_load_2d(dk, &p.tmk, h * kHalf, row, fb, pol);
           tma_load_2d(dv, &p.tmv, h * kHalf, row, fb, pol);
@@ -1117,10 +1128,11 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
   };
   // the first copies go out before the query rows are read
   int issued = 0;
-  for (; issued < min(mine, kVStages) && !__shfl_sync(0xffffffffu, s.abort, 0); ++issued) issue(issued);
+  if (issuer)
+    for (; issued < min(mine, kVStages) && !__shfl_sync(0xffffffffu, s.abort, 0); ++issued) issue(issued);
 
   // query rows r = 4 j + g: token j, head kvh * 4 + g (rows of tokens past T are zero)
-  for (int i = threadIdx.x; i < R * (kD / 8); i += kVThreads) {
+  for (int i = threadIdx.x; i < R * (kD / 8); i += NT) {
     const int r = i / (kD / 8), c = i % (kD / 8);
     const int j = r / kGroup, g = r % kGroup;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -1131,152 +1143,142 @@ __global__ void __launch_bounds__(kVThreads) verify_attn_kernel(const __grid_con
   }
   __syncthreads();
 
-  // lane: in tile mt, rows 16 mt + lane / 4 (h = 0) and + 8 (h = 1), columns 2 (lane % 4) + {0, 1}
-  float m[MT][2], l[MT][2];
-  int lim[MT][2];            // last key each row sees (-1: a row past the T tokens)
+  // lane: in this warp's tile, rows 16 mt + lane / 4 (h = 0) and + 8 (h = 1), columns 2 (lane % 4) + {0, 1}
+  float m[2], l[2];
+  int lim[2];            // last key each row sees (-1: a row past the T tokens)
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
+  for (int h = 0; h < 2; ++h) {
+    const int r = 16 * mt + 8 * h + (lane >> 2);
+    m[h] = kNegBig;
+    l[h] = 0.f;
+    lim[h] = r / kGroup < T ? p0 + r / kGroup : -1;
+  }
+  float o[16][4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = 16 * mt + 8 * h + (lane >> 2);
-      m[mt][h] = kNegBig;
-      l[mt][h] = 0.f;
-      lim[mt][h] = r / kGroup < T ? p0 + r / kGroup : -1;
-    }
-  float o[MT][16][4];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int j = 0; j < 16; ++j) o[mt][j][0] = o[mt][j][1] = o[mt][j][2] = o[mt][j][3] = 0.f;
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   const int mi = lane >> 3, ri = lane & 7;
+  const uint32_t qaddr = smem_u32(&s.q[16 * mt + (lane & 15)][(lane >> 4) * 8]);
 
   for (int k = 0; k < mine; ++k) {
     const int slot = k % kVStages;
-    mbar_wait(smem_u32(&s.full[slot][warp]), (k / kVStages) & 1, s, p.ws_err, true);
+    mbar_wait(smem_u32(&s.full[slot][sw]), (k / kVStages) & 1, s, p.ws_err, true);
     __syncwarp();   // reconverge after the per-lane spin before ldmatrix / mma.sync
-    const int key0 = (pg0 + warp + k * kVW) * kPage;
-    const uint32_t kbase = smem_u32(&s.k[slot][warp][0][0]);
-    const uint32_t vbase = smem_u32(&s.v[slot][warp][0][0]);
-    // ---- S = Q K^T, R rows x 16 keys
-    float c0[MT][4], c1[MT][4];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) c0[mt][e] = c1[mt][e] = 0.f;
+    const int key0 = (pg0 + sw + k * kVW) * kPage;
+    const uint32_t kbase = smem_u32(&s.k[slot][sw][0][0]);
+    const uint32_t vbase = smem_u32(&s.v[slot][sw][0][0]);
+    // ---- S = Q K^T, this tile's 16 rows x 16 keys
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
     {
       const int tok = 8 * (mi >> 1) + ri;
       const uint32_t krow = kbase + tok * 128;
-      const uint32_t qaddr = smem_u32(&s.q[lane & 15][(lane >> 4) * 8]);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const int h = ks >> 2, c = 2 * (ks & 3) + (mi & 1);
-        uint32_t b00, b01, b10, b11;
+        uint32_t b00, b01, b10, b11, a0, a1, a2, a3;
         ldsm_x4(krow + h * kBoxBytes + ((c ^ ri) << 4), b00, b01, b10, b11);
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(qaddr + mt * 16 * (kD + 8) * 2 + ks * 32, a0, a1, a2, a3);
-          mma16816_full(c0[mt], a0, a1, a2, a3, b00, b01);
-          mma16816_full(c1[mt], a0, a1, a2, a3, b10, b11);
-        }
+        ldsm_x4(qaddr + ks * 32, a0, a1, a2, a3);
+        mma16816_full(c0, a0, a1, a2, a3, b00, b01);
+        mma16816_full(c1, a0, a1, a2, a3, b10, b11);
       }
     }
     const int kc = key0 + 2 * (lane & 3);
-    // rows of the page past the split's keys may hold anything: zero them so 0 * V stays 0
+    // rows of the page past the split's keys may hold anything: zero them so 0 * V stays 0 (the
+    // stream's first warp does it; its partner waits for it below)
     const int ntok = min(s1 - key0, kPage);
     if (ntok < kPage) {
-      for (int i = lane; i < (kPage - ntok) * 16; i += 32) {
-        const int r = ntok + (i >> 4), part = i & 15;
-        const uint32_t a = vbase + (part >> 3) * kBoxBytes + r * 128 + ((part & 7) << 4);
-        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+      if (issuer) {
+        for (int i = lane; i < (kPage - ntok) * 16; i += 32) {
+          const int r = ntok + (i >> 4), part = i & 15;
+          const uint32_t a = vbase + (part >> 3) * kBoxBytes + r * 128 + ((part & 7) << 4);
+          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+        }
       }
-      __syncwarp();
+      if (MT > 1) named_bar(2 + sw, 32 * MT);   // the stream's warps: zeroed rows visible
+      else __syncwarp();
     }
     const int tok = 8 * (mi & 1) + ri;
     const uint32_t vrow = vbase + tok * 128;
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      // ---- online softmax, rows h = 0 / 1 of this tile (4 lanes share a row)
-      uint32_t pa[4];
-      float al[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int lm = lim[mt][h];
-        float sv[4];
-        sv[0] = (kc < s1 && kc <= lm) ? c0[mt][2 * h] * p.scale_log2 : -INFINITY;
-        sv[1] = (kc + 1 < s1 && kc + 1 <= lm) ? c0[mt][2 * h + 1] * p.scale_log2 : -INFINITY;
-        sv[2] = (kc + 8 < s1 && kc + 8 <= lm) ? c1[mt][2 * h] * p.scale_log2 : -INFINITY;
-        sv[3] = (kc + 9 < s1 && kc + 9 <= lm) ? c1[mt][2 * h + 1] * p.scale_log2 : -INFINITY;
-        float x = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
-        x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
-        x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
-        const float mn = fmaxf(m[mt][h], x);
-        al[h] = exp2f(m[mt][h] - mn);
-        float pr[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) pr[e] = exp2f(sv[e] - mn);
-        l[mt][h] = l[mt][h] * al[h] + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
-        m[mt][h] = mn;
-        // P as the A operand: a0 / a1 rows h = 0 / 1 keys 0-7, a2 / a3 keys 8-15
-        pa[h] = pack_bf16(pr[0], pr[1]);
-        pa[2 + h] = pack_bf16(pr[2], pr[3]);
-      }
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        o[mt][j][0] *= al[0];
-        o[mt][j][1] *= al[0];
-        o[mt][j][2] *= al[1];
-        o[mt][j][3] *= al[1];
-      }
-      // ---- O += P V
-#pragma unroll
-      for (int j = 0; j < 16; j += 2) {
-        const int c = j + (mi >> 1);
-        uint32_t b0a, b1a, b0b, b1b;
-        ldsm_x4_t(vrow + (c >> 3) * kBoxBytes + (((c & 7) ^ ri) << 4), b0a, b1a, b0b, b1b);
-        mma16816_full(o[mt][j], pa[0], pa[1], pa[2], pa[3], b0a, b1a);
-        mma16816_full(o[mt][j + 1], pa[0], pa[1], pa[2], pa[3], b0b, b1b);
-      }
-    }
-    __syncwarp();
-    if (issued < mine && !__shfl_sync(0xffffffffu, s.abort, 0)) issue(issued++);
-  }
-  // every copy this warp issued has landed (waited above, or drained here after an abort)
-  if (lane == 0)
-    for (int k = max(issued - kVStages, 0); k < issued; ++k)
-      mbar_wait(smem_u32(&s.full[k % kVStages][warp]), (k / kVStages) & 1, s, p.ws_err, false);
-
-  // ---- merge the 4 warps (partials in the ring memory), then the splits of this pair
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
+    // ---- online softmax, rows h = 0 / 1 of this tile (4 lanes share a row)
+    uint32_t pa[4];
+    float al[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      l[mt][h] += __shfl_xor_sync(0xffffffffu, l[mt][h], 1);
-      l[mt][h] += __shfl_xor_sync(0xffffffffu, l[mt][h], 2);
+      const int lm = lim[h];
+      float sv[4];
+      sv[0] = (kc < s1 && kc <= lm) ? c0[2 * h] * p.scale_log2 : -INFINITY;
+      sv[1] = (kc + 1 < s1 && kc + 1 <= lm) ? c0[2 * h + 1] * p.scale_log2 : -INFINITY;
+      sv[2] = (kc + 8 < s1 && kc + 8 <= lm) ? c1[2 * h] * p.scale_log2 : -INFINITY;
+      sv[3] = (kc + 9 < s1 && kc + 9 <= lm) ? c1[2 * h + 1] * p.scale_log2 : -INFINITY;
+      float x = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+      x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
+      x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+      const float mn = fmaxf(m[h], x);
+      al[h] = exp2f(m[h] - mn);
+      float pr[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pr[e] = exp2f(sv[e] - mn);
+      l[h] = l[h] * al[h] + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
+      m[h] = mn;
+      // P as the A operand: a0 / a1 rows h = 0 / 1 keys 0-7, a2 / a3 keys 8-15
+      pa[h] = pack_bf16(pr[0], pr[1]);
+      pa[2 + h] = pack_bf16(pr[2], pr[3]);
     }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= al[0];
+      o[j][1] *= al[0];
+      o[j][2] *= al[1];
+      o[j][3] *= al[1];
+    }
+    // ---- O += P V
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      const int c = j + (mi >> 1);
+      uint32_t b0a, b1a, b0b, b1b;
+      ldsm_x4_t(vrow + (c >> 3) * kBoxBytes + (((c & 7) ^ ri) << 4), b0a, b1a, b0b, b1b);
+      mma16816_full(o[j], pa[0], pa[1], pa[2], pa[3], b0a, b1a);
+      mma16816_full(o[j + 1], pa[0], pa[1], pa[2], pa[3], b0b, b1b);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&s.empty[slot][sw]));   // this warp is done with the slot
+    if (issuer && issued < mine && !__shfl_sync(0xffffffffu, s.abort, 0)) {
+      // refill the slot once every consumer of the stream has left it
+      const bool ok = mbar_wait(smem_u32(&s.empty[slot][sw]), (k / kVStages) & 1, s, p.ws_err, true);
+      __syncwarp();
+      if (ok) issue(issued++);
+    }
+  }
+  // every copy this stream issued has landed (waited above, or drained here after an abort)
+  if (issuer && lane == 0)
+    for (int k = max(issued - kVStages, 0); k < issued; ++k)
+      mbar_wait(smem_u32(&s.full[k % kVStages][sw]), (k / kVStages) & 1, s, p.ws_err, false);
+
+  // ---- merge the streams (partials in the ring memory), then the splits of this pair
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l[h] += __shfl_xor_sync(0xffffffffu, l[h], 1);
+    l[h] += __shfl_xor_sync(0xffffffffu, l[h], 2);
+  }
   __syncthreads();   // every warp is done with the rings
   float* ob = reinterpret_cast<float*>(&s.k[0][0][0][0]);   // [kVW][R][kD + 4]
   {
     const int c = 2 * (lane & 3);
+    const int rA = 16 * mt + (lane >> 2), rB = rA + 8;
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      const int rA = 16 * mt + (lane >> 2), rB = rA + 8;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        *reinterpret_cast<float2*>(&ob[(warp * R + rA) * (kD + 4) + 8 * j + c]) = make_float2(o[mt][j][0], o[mt][j][1]);
-        *reinterpret_cast<float2*>(&ob[(warp * R + rB) * (kD + 4) + 8 * j + c]) = make_float2(o[mt][j][2], o[mt][j][3]);
-      }
-      if ((lane & 3) == 0) {
-        s.red_m[warp][rA] = m[mt][0];
-        s.red_l[warp][rA] = l[mt][0];
-        s.red_m[warp][rB] = m[mt][1];
-        s.red_l[warp][rB] = l[mt][1];
-      }
+    for (int j = 0; j < 16; ++j) {
+      *reinterpret_cast<float2*>(&ob[(sw * R + rA) * (kD + 4) + 8 * j + c]) = make_float2(o[j][0], o[j][1]);
+      *reinterpret_cast<float2*>(&ob[(sw * R + rB) * (kD + 4) + 8 * j + c]) = make_float2(o[j][2], o[j][3]);
+    }
+    if ((lane & 3) == 0) {
+      s.red_m[sw][rA] = m[0];
+      s.red_l[sw][rA] = l[0];
+      s.red_m[sw][rB] = m[1];
+      s.red_l[sw][rB] = l[1];
     }
   }
   __syncthreads();
   // thread -> row r, dims d0 .. d0 + DPT - 1
-  constexpr int TPR = kVThreads / R, DPT = kD / TPR;
+  constexpr int TPR = NT / R, DPT = kD / TPR;
   const int r = threadIdx.x / TPR, d0 = (threadIdx.x % TPR) * DPT;
   const int j = r / kGroup, g = r % kGroup;
   float M = kNegBig;
@@ -1525,7 +1527,7 @@ int verify_occupancy(int device, int* blocks_per_sm) {
     configured[device] = 1;
   }
   if (blocks_per_sm &&
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kern, kVThreads,
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kern, verify_threads<MT>(),
                                                     vsmem_bytes<MT>()) != cudaSuccess)
     return KOPT_ERR_CUDA;
   return KOPT_OK;
@@ -1542,7 +1544,7 @@ template <bool PAGED, int MT>
 int launch_verify_t(const kopt_plan* plan, Params& p, void* stream) {
   int rc = verify_occupancy<PAGED, MT>(plan->device, nullptr);
   if (rc) return rc;
-  verify_attn_kernel<PAGED, MT><<<plan->grid, kVThreads, vsmem_bytes<MT>(),
+  verify_attn_kernel<PAGED, MT><<<plan->grid, verify_threads<MT>(), vsmem_bytes<MT>(),
                                   static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
 }
