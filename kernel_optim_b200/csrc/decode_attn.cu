@@ -125,6 +125,8 @@ struct __align__(1024) Smem {
   int static_pages;                     // P: pages of the line split into one piece per CTA
   int total_chunks;                     // grid static pieces + dynamic chunks
   int late;                             // the last kLateCtas pieces are shortened (see chunk_range)
+  int parts;                            // > 0: every pair has npg_eq pages and is cut into this
+  int npg_eq;                           //   many pieces of its own (see compute_plan)
   volatile int nclaimed;                // ring entries 0 .. nclaimed-1 are valid
   int npend;                            // partial units written, not yet released
   int pend[kMaxPend][5];                // their (pair, first chunk, chunks, sequence, kv head)
@@ -203,6 +205,14 @@ __device__ void compute_plan(const Params& p, Smem& s, int lane) {
   err = __reduce_or_sync(0xffffffffu, err);
   if (lane == 0) s.err_bits = err;
   __syncwarp();
+  // do all sequences stream the same number of pages?
+  int nmin = 1 << 30, nmax = 0;
+  for (int b = lane; b < p.B; b += 32) {
+    nmin = min(nmin, s.npages[b]);
+    nmax = max(nmax, s.npages[b]);
+  }
+  nmin = __reduce_min_sync(0xffffffffu, nmin);
+  nmax = __reduce_max_sync(0xffffffffu, nmax);
   int carry = 0;
   for (int base = 0; base < p.B; base += 32) {
     const int b = base + lane;
@@ -225,6 +235,22 @@ __device__ void compute_plan(const Params& p, Smem& s, int lane) {
     s.static_pages = P;
     s.total_chunks = G + ceil_div_i(carry - P, kChunkPages);
     s.late = p.late_skew && G > 2 * kLateCtas && P / G >= 4 * kLateMax;
+    // Pairs of equal length, no more of them than CTAs: cut each pair into the same number k of
+    // pieces (CTA c takes part c % k of pair c / k) instead of one line cut into G pieces. Every
+    // CTA then holds one unit, with no unit boundary inside its piece (measured on c2: 48.4 ->
+    // 45.6 us; c4, k = 4: 347 -> 318 us). Only when the CTAs so used are >= 80% of the grid, a
+    // part has at least one page, and the whole line is split statically; the CTAs beyond
+    // pairs * k (the last ones, which start last under programmatic launch) get no pages.
+    s.parts = 0;
+    s.npg_eq = nmin;
+    const int pairs = p.B * p.nkv;
+    if (nmin == nmax && pairs <= G && P == carry) {
+      const int k = min(G / pairs, nmin);
+      if (5 * pairs * k >= 4 * G) {
+        s.parts = k;
+        s.late = 0;
+      }
+    }
   }
 }
 
@@ -245,6 +271,16 @@ __device__ __forceinline__ int late_front(const Smem& s) {   // pages of the fir
 __device__ __forceinline__ void chunk_range(const Smem& s, int k, int& x0, int& x1) {
   const int G = gridDim.x;
   const long long P = s.static_pages;
+  if (s.parts > 0) {   // part k % parts of pair k / parts, or nothing past the last pair's part
+    const int q = k / s.parts, i = k - q * s.parts, np = s.npg_eq;
+    if (static_cast<long long>(q) * np >= s.total_pages) {
+      x0 = x1 = s.total_pages;
+    } else {
+      x0 = q * np + static_cast<int>(static_cast<long long>(i) * np / s.parts);
+      x1 = q * np + static_cast<int>(static_cast<long long>(i + 1) * np / s.parts);
+    }
+    return;
+  }
   if (k < G && s.late) {
     const int G4 = G - kLateCtas, F = late_front(s), q = s.static_pages / G;
     if (k < G4) {
@@ -268,6 +304,11 @@ __device__ __forceinline__ void chunk_range(const Smem& s, int k, int& x0, int& 
 __device__ __forceinline__ int chunk_of(const Smem& s, int y) {
   const long long G = gridDim.x;
   const long long P = s.static_pages;
+  if (s.parts > 0) {   // the part of its pair holding page y
+    const int q = y / s.npg_eq, off = y - q * s.npg_eq;
+    return q * s.parts +
+           static_cast<int>((static_cast<long long>(off + 1) * s.parts - 1) / s.npg_eq);
+  }
   if (y < P && s.late) {
     const int G4 = static_cast<int>(G) - kLateCtas, F = late_front(s);
     const int q = s.static_pages / static_cast<int>(G);

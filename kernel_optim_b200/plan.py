@@ -14,7 +14,11 @@ without a GPU:
 * with overlapped launches (skew) and long enough pieces, the last LATE_CTAS pieces are shorter by
   LATE_PAGES (the last CTA's most) and the first grid - LATE_CTAS pieces share the difference;
 * a unit is a chunk's intersection with one pair; its partial result goes to workspace slot k + q,
-  and the last of the pair's n units to finish merges slots c + q for c in c0 .. c0 + n - 1.
+  and the last of the pair's n units to finish merges slots c + q for c in c0 .. c0 + n - 1;
+* when every pair has the same page count np, there are no more pairs than CTAs and the whole line
+  is static, each pair is cut into k = min(grid // pairs, np) parts of its own instead (piece c =
+  part c % k of pair c // k, [floor(i np / k), floor((i + 1) np / k)) within it), provided
+  pairs * k >= 0.8 grid; the CTAs past pairs * k get nothing and the late-start allowance is off.
 """
 
 from __future__ import annotations
@@ -54,6 +58,8 @@ class Plan:
     total_chunks: int
     grid: int
     late: bool = False
+    parts: int = 0       # > 0: pair-aligned pieces, `parts` per pair of npg_eq pages
+    npg_eq: int = 0
 
     def _late_front(self) -> int:
         q = self.static_pages // self.grid
@@ -61,6 +67,12 @@ class Plan:
 
     def chunk_range(self, k: int):
         G, P = self.grid, self.static_pages
+        if self.parts:
+            q, i = divmod(k, self.parts)
+            np_ = self.npg_eq
+            if q * np_ >= self.total_pages:
+                return self.total_pages, self.total_pages
+            return q * np_ + i * np_ // self.parts, q * np_ + (i + 1) * np_ // self.parts
         if k < G and self.late:
             G4, F, q = G - LATE_CTAS, self._late_front(), P // G
             if k < G4:
@@ -74,6 +86,9 @@ class Plan:
 
     def chunk_of(self, y: int) -> int:
         G, P = self.grid, self.static_pages
+        if self.parts:
+            q, off = divmod(y, self.npg_eq)
+            return q * self.parts + ((off + 1) * self.parts - 1) // self.npg_eq
         if y < P and self.late:
             G4, F, q = G - LATE_CTAS, self._late_front(), P // G
             if y < F:
@@ -98,7 +113,13 @@ def plan(lengths, nkv: int, grid: int, fused: bool, static_pct: int = STATIC_PCT
     if P < grid:
         P = 0
     late = skew and grid > 2 * LATE_CTAS and P // grid >= 4 * LATE_PAGES[0]
-    return Plan(npages, pstart, T, P, grid + -(-(T - P) // CHUNK_PAGES), grid, late)
+    parts, pairs = 0, len(lengths) * nkv
+    if min(npages) == max(npages) and pairs <= grid and P == T:
+        k = min(grid // pairs, npages[0])
+        if 5 * pairs * k >= 4 * grid:
+            parts, late = k, False
+    return Plan(npages, pstart, T, P, grid + -(-(T - P) // CHUNK_PAGES), grid, late, parts,
+                npages[0])
 
 
 def units_of_chunk(pl: Plan, lengths, nkv: int, fused: bool, k: int) -> list[Unit]:
