@@ -988,9 +988,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(const __grid_c
       mbar_wait(smem_u32(&s.full[k % kStages][warp]), (k / kStages) & 1, s, p.ws_err, false);
   }
   // The last CTA to finish (all claims made) resets the chunk counter for the next call; with the
-  // fused gather it also tells every rank that all of this rank's rows have landed there.
+  // fused gather it also tells every rank that all of this rank's rows have landed there. A call
+  // split statically only (no chunk is claimed) and without the gather needs neither, so its
+  // CTAs skip the fence and the count (the whole grid takes the same branch: total_chunks is
+  // the same in every CTA) and leave the SM sooner.
   if (p.world > 0) named_bar(1, kNW * 32);   // every output store of this CTA is issued
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && p.world == 0 && s.total_chunks == static_cast<int>(gridDim.x)) {
+    if (s.err_bits) atomicOr(p.ws_err, s.err_bits);
+  } else if (threadIdx.x == 0) {
     if (s.err_bits) atomicOr(p.ws_err, s.err_bits);
     if (p.world > 0) __threadfence_system();   // this CTA's rows visible to the peers
     else __threadfence();
