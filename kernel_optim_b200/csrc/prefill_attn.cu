@@ -6,23 +6,29 @@
 // GQA (engine.py:376-377), then the prompt's K/V go to the cache. Here the prologue writes the
 // prompt's K/V straight into the (paged) cache and this kernel reads them from there.
 //
-// One CTA per (sequence, query head, 128-row query tile), the longest tiles first. For key tile j
-// (128 keys) of the tiles 0 .. qt the tile needs (causal):
-//   warp 4   TMA producer: the query tile once, then K and V tiles into a 2-deep ring (128-byte
-//            swizzle; paged caches arrive as 16-row page boxes);
-//   warp 5   allocates tensor memory and one thread issues the MMAs:
-//            S_j = Q K_j^T into one of two fp32 S buffers in tensor memory (M = 128 query rows,
-//            N = 128 keys, K-major operands), then O += P_j V_j (P from shared memory, V as an
-//            MN-major operand) into the fp32 O accumulator in tensor memory;
-//   warps 0-3 one thread per query row (tensor-memory lane): read the row of S_j with tcgen05.ld,
-//            mask the diagonal tile, online softmax in fp32 in the exp2 domain, write P_j to shared
-//            memory as bf16 (the K-major layout the MMA reads). The running maximum only moves
-//            when a row's maximum grows by more than 2^8, so O (in tensor memory) is rescaled
-//            rarely, by the warp that needs it, between the two MMAs that touch it; at the end
-//            O / l goes to the output as bf16.
-// S_{j+1} is computed while the softmax works on S_j. Every wait is bounded in time; on expiry
-// the kernel records KOPT_DEV_ERR_TIMEOUT, stops, waits (bounded) for what it issued and frees
-// its tensor memory.
+// Persistent grid, one CTA per SM. A work item is one sequence, one kv head, one 128-row query
+// tile and two of the kv head's four query heads (A and B): both query tiles sit at the same
+// positions, so they need the same key tiles 0 .. qt (causal) and every K/V tile loaded serves
+// both. Items are dealt round-robin, the longest (last query tiles) first. Per key tile j:
+//   warp 8   TMA producer: the item's two query tiles, then K_j and V_j into a 2-deep ring
+//            (128-byte swizzle; paged caches arrive as 16-row page boxes);
+//   warp 9   allocates all 512 tensor-memory columns (S_A, S_B, O_A, O_B, fp32) and one thread
+//            issues the MMAs in the order S_A(0) S_B(0), then per j: O_A += P_A(j) V_j,
+//            S_A(j+1), O_B += P_B(j) V_j, S_B(j+1): while one softmax group works on its scores,
+//            the tensor core computes the other group's. S = Q K^T has M = 128 query rows,
+//            N = 128 keys, K-major operands from shared memory; P V takes P from tensor memory
+//            (the A operand) and V from shared memory as an MN-major operand;
+//   warps 0-3 / 4-7: the softmax of tile A / B, one thread per query row (tensor-memory lane):
+//            the row of S_j by tcgen05.ld, the diagonal tile masked, online softmax in fp32 in the
+//            exp2 domain, and P_j written back as bf16 pairs over the first 64 columns of its S
+//            buffer by tcgen05.st. The running maximum only moves when a row's maximum grows by
+//            more than 2^8, so O is rescaled rarely, by the thread that needs it; at the end of
+//            the item O / l goes to the output as bf16.
+// The MMAs of one thread execute in issue order, and a commit tracks every MMA issued before it:
+// S_x(j+1) is issued after O_x += P_x(j) V_j, so when a softmax thread sees S_x(j+1) complete, the
+// P V that read P_x(j) (same columns) is complete too, and O_x may be rescaled. Every wait is
+// bounded in time; on expiry the kernel records KOPT_DEV_ERR_TIMEOUT, stops, waits (bounded) for
+// what it issued and frees its tensor memory.
 
 #include "common.cuh"
 
@@ -31,19 +37,21 @@ namespace {
 
 constexpr int kPD = 128;                    // head dim
 constexpr int kPGroup = 4;                  // query heads per kv head
+constexpr int kPHeads = 2;                  // query heads (tiles A, B) per work item
 constexpr int kPRows = 128;                 // query rows per tile: the MMAs' M
 constexpr int kPKeys = 128;                 // keys per tile
 constexpr int kPPage = 16;                  // tokens per cache page
 constexpr int kPStages = 2;                 // K/V ring depth
-constexpr int kPSoftWarps = 4;              // warps 0-3: one thread per query row
-constexpr int kPProducer = 4;
-constexpr int kPMma = 5;
-constexpr int kPThreads = 6 * 32;
-constexpr uint32_t kPCols = 512;            // tensor memory: S double buffer + O
-constexpr uint32_t kPColO = 256;
+constexpr int kPSoftWarps = 8;              // warps 0-3: rows of tile A, warps 4-7: rows of tile B
+constexpr int kPProducer = 8;
+constexpr int kPMma = 9;
+constexpr int kPThreads = 10 * 32;
+constexpr uint32_t kPCols = 512;            // tensor memory: S_A, S_B, O_A, O_B (128 columns each)
 constexpr int kPHalf = kPRows * 64;         // elements of one 64-column half tile
 constexpr uint32_t kPHalfBytes = kPHalf * 2;   // 16 KiB
 constexpr float kPRescale = 8.f;            // log2 growth of a row's max that moves its running max
+__host__ __device__ constexpr uint32_t col_s(int x) { return 128u * static_cast<uint32_t>(x); }
+__host__ __device__ constexpr uint32_t col_o(int x) { return 256u + 128u * static_cast<uint32_t>(x); }
 
 struct PrefillParams {
   CUtensorMap tmq;          // q [B*S, nq*128] as 4-D {128 dims, nq heads, S rows, B}: box {64, 1, 128, 1}
@@ -54,18 +62,17 @@ struct PrefillParams {
   int* err;                 // device error word
   int bt_stride, num_pages;
   int B, S, nq, nkv, nqt;
-  int items;                // B * nq * nqt (sequence, query head, query tile) work items
+  int items;                // nqt * B * nkv * 2 (query tile, sequence, kv head, head pair)
   float scale_log2;
 };
 
 struct __align__(1024) PSmem {
-  bf16 q[2][2][kPHalf];             // two query tiles, each [dims 0-63 | 64-127][128 rows][64]
+  bf16 q[kPHeads][2][kPHalf];       // the item's query tiles A, B: [dims 0-63 | 64-127][128 rows][64]
   bf16 k[kPStages][2][kPHalf];      // key tiles: [dims half][128 keys][64]
   bf16 v[kPStages][2][kPHalf];      // value tiles, same layout (read as an MN-major operand)
-  bf16 pm[2][kPHalf];               // P: [keys 0-63 | 64-127][128 rows][64], bf16
-  unsigned long long qfull[2], qempty[2];
+  unsigned long long qfull, qempty;
   unsigned long long kfull[kPStages], vfull[kPStages], kempty[kPStages], vempty[kPStages];
-  unsigned long long sfull[2], sempty[2], pfull, odone, drain;
+  unsigned long long sfull[kPHeads], pfull[kPHeads], odone[kPHeads], oempty[kPHeads], drain;
   uint32_t tmem;
   volatile int abort;
 };
@@ -160,21 +167,42 @@ __device__ __forceinline__ float ex2_fast(float x) {
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+// 16 consecutive 32-bit columns of this thread's tensor-memory lane from raw words (no wait).
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+// D (tensor memory) [+]= A (tensor memory, M rows = lanes, K along columns as bf16 pairs) x B
+// (shared-memory descriptor), kind::f16.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 // This CTA's work items: item w = blockIdx.x + i * gridDim.x of the list ordered longest first
-// (query tile qt = nqt - 1 down to 0; within a tile, sequence-major, head-minor, so the 4 heads of
-// a kv head are neighbours and share its K/V tiles in L2).
+// (query tile qt = nqt - 1 down to 0; within a tile sequence-major, then kv head, then head pair,
+// so neighbouring items share their K/V tiles in L2).
 struct Item {
-  int b, h, kvh, q0, nt;
+  int b, kvh, h0, q0, nt;   // query heads h0 (tile A) and h0 + 1 (tile B)
 };
 __device__ __forceinline__ Item item_of(const PrefillParams& p, int w) {
-  const int per_qt = p.B * p.nq;
+  const int per_qt = p.B * p.nkv * kPHeads;
   const int qt = p.nqt - 1 - w / per_qt;
   const int rem = w - (w / per_qt) * per_qt;
+  const int pairs_b = p.nkv * kPHeads;
   Item it;
-  it.b = rem / p.nq;
-  it.h = rem - it.b * p.nq;
-  it.kvh = it.h / kPGroup;
+  it.b = rem / pairs_b;
+  const int r2 = rem - it.b * pairs_b;
+  it.kvh = r2 / kPHeads;
+  it.h0 = it.kvh * kPGroup + (r2 - it.kvh * kPHeads) * kPHeads;
   it.q0 = qt * kPRows;
   it.nt = qt + 1;   // causal: key tiles 0 .. qt
   return it;
@@ -189,18 +217,20 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
   const int G = gridDim.x;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&s.qfull[i]), 1);
-      mbar_init(smem_u32(&s.qempty[i]), 1);
+    mbar_init(smem_u32(&s.qfull), 1);
+    mbar_init(smem_u32(&s.qempty), 1);
+    for (int i = 0; i < kPStages; ++i) {
       mbar_init(smem_u32(&s.kfull[i]), 1);
       mbar_init(smem_u32(&s.vfull[i]), 1);
       mbar_init(smem_u32(&s.kempty[i]), 1);
       mbar_init(smem_u32(&s.vempty[i]), 1);
-      mbar_init(smem_u32(&s.sfull[i]), 1);
-      mbar_init(smem_u32(&s.sempty[i]), kPSoftWarps * 32);
     }
-    mbar_init(smem_u32(&s.pfull), kPSoftWarps * 32);
-    mbar_init(smem_u32(&s.odone), 1);
+    for (int x = 0; x < kPHeads; ++x) {
+      mbar_init(smem_u32(&s.sfull[x]), 1);
+      mbar_init(smem_u32(&s.pfull[x]), kPRows);
+      mbar_init(smem_u32(&s.odone[x]), 1);
+      mbar_init(smem_u32(&s.oempty[x]), kPRows);
+    }
     mbar_init(smem_u32(&s.drain), 1);
     s.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -216,11 +246,10 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
 
   if (warp == kPProducer) {
     if (lane == 0) {
-      // ---- TMA producer: each item's query tile (two buffers, so the next item's arrives while
-      // this one computes), then its K and V tiles through the 2-deep ring; tiles are counted
-      // across items (t), so the ring never drains between items
-      // queries are read once (evict first); K/V tiles are read again by the other heads of the
-      // kv head and the later query tiles of the sequence (evict last)
+      // ---- TMA producer: each item's two query tiles, then its K and V tiles through the 2-deep
+      // ring; tiles are counted across items (t), so the ring never drains between items.
+      // Queries are read once (evict first); K/V tiles are read again by the other head pair of
+      // the kv head and the later query tiles of the sequence (evict last).
       const uint64_t pol_q = evict_first_policy();
       uint64_t pol;
       asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
@@ -249,11 +278,15 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
       };
       for (int w = blockIdx.x; ok && w < p.items; w += G, ++i) {
         const Item it = item_of(p, w);
-        const int qb = i & 1;
-        if (i >= 2 && !mbar_wait(smem_u32(&s.qempty[qb]), ((i >> 1) - 1) & 1, s, p.err, true)) break;
-        mbar_arrive_expect_tx(smem_u32(&s.qfull[qb]), 2 * kPHalfBytes);
-        tma_load_4d(smem_u32(&s.q[qb][0][0]), &p.tmq, 0, it.h, it.q0, it.b, smem_u32(&s.qfull[qb]), pol_q);
-        tma_load_4d(smem_u32(&s.q[qb][1][0]), &p.tmq, 64, it.h, it.q0, it.b, smem_u32(&s.qfull[qb]), pol_q);
+        // the previous item's last scores are computed: its query tiles may be replaced
+        if (i >= 1 && !mbar_wait(smem_u32(&s.qempty), (i - 1) & 1, s, p.err, true)) break;
+        mbar_arrive_expect_tx(smem_u32(&s.qfull), 4 * kPHalfBytes);
+#pragma unroll
+        for (int x = 0; x < kPHeads; ++x)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh)
+            tma_load_4d(smem_u32(&s.q[x][hh][0]), &p.tmq, 64 * hh, it.h0 + x, it.q0, it.b,
+                        smem_u32(&s.qfull), pol_q);
         for (int j = 0; j < it.nt; ++j) {
           const int st = t & 1, use = t >> 1;
           if (t >= kPStages && !mbar_wait(smem_u32(&s.kempty[st]), (use - 1) & 1, s, p.err, true)) {
@@ -271,8 +304,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
         }
       }
       // every copy issued has landed before the CTA ends (the newest phase of each barrier)
-      for (int k = max(i - 2, 0); k < i; ++k)
-        mbar_wait(smem_u32(&s.qfull[k & 1]), (k >> 1) & 1, s, p.err, false);
+      if (i > 0) mbar_wait(smem_u32(&s.qfull), (i - 1) & 1, s, p.err, false);
       for (int k = max(t - kPStages, 0); k < t; ++k) {
         mbar_wait(smem_u32(&s.kfull[k & 1]), (k >> 1) & 1, s, p.err, false);
         mbar_wait(smem_u32(&s.vfull[k & 1]), (k >> 1) & 1, s, p.err, false);
@@ -280,61 +312,80 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
     }
   } else if (warp == kPMma) {
     if (lane == 0) {
-      // ---- MMA issuer, one tile sequence across items: S of tile t + 1 is issued before P V of
-      // tile t, so the tensor core computes the next scores while the softmax works
-      int ntiles = 0;
-      for (int w = blockIdx.x; w < p.items; w += G) ntiles += item_of(p, w).nt;
-      int si = 0, sw = blockIdx.x, sj = 0, st_t = 0;   // next S: item si (index sw), its tile sj
-      Item sit = item_of(p, min(sw, p.items - 1));
-      auto issue_s = [&]() -> bool {
-        const int qb = si & 1, st = st_t & 1;
-        if (sj == 0 && !mbar_wait(smem_u32(&s.qfull[qb]), (si >> 1) & 1, s, p.err, true)) return false;
-        if (!mbar_wait(smem_u32(&s.kfull[st]), (st_t >> 1) & 1, s, p.err, true)) return false;
-        if (st_t >= 2 && !mbar_wait(smem_u32(&s.sempty[st]), ((st_t >> 1) - 1) & 1, s, p.err, true))
-          return false;
-        tc_fence_after();
-        const uint32_t qa = smem_u32(&s.q[qb][0][0]), ka = smem_u32(&s.k[st][0][0]);
+      // ---- MMA issuer. Per item: S_A(0), S_B(0); then per key tile j: O_A += P_A(j) V_j,
+      // S_A(j+1), O_B += P_B(j) V_j, S_B(j+1). Tiles are counted across items (T).
+      auto issue_s = [&](int x, int st) {   // S_x = Q_x K^T
+        const uint32_t qa = smem_u32(&s.q[x][0][0]), ka = smem_u32(&s.k[st][0][0]);
 #pragma unroll
         for (int kk = 0; kk < kPD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kPHalfBytes + (kk & 3) * 32;
-          umma_bf16(tmem + st * kPKeys, sw128_desc(qa + off), sw128_desc(ka + off), kIdescS, kk > 0);
+          umma_bf16(tmem + col_s(x), sw128_desc(qa + off), sw128_desc(ka + off), kIdescS, kk > 0);
         }
-        umma_commit(smem_u32(&s.sfull[st]));
-        umma_commit(smem_u32(&s.kempty[st]));
-        if (sj == sit.nt - 1) {   // the item's last scores: its query buffer may take item si + 2
-          umma_commit(smem_u32(&s.qempty[qb]));
-          ++si;
-          sw += G;
-          sj = 0;
-          if (sw < p.items) sit = item_of(p, sw);
-        } else {
-          ++sj;
-        }
-        ++st_t;
-        return true;
       };
-      bool ok = ntiles == 0 || issue_s();
-      int pj = 0, pnt = item_of(p, min(static_cast<int>(blockIdx.x), p.items - 1)).nt, pw = blockIdx.x;
-      for (int t = 0; ok && t < ntiles; ++t) {
-        if (t + 1 < ntiles && !issue_s()) break;
-        const int st = t & 1;
-        if (!mbar_wait(smem_u32(&s.pfull), t & 1, s, p.err, true)) break;
-        if (!mbar_wait(smem_u32(&s.vfull[st]), (t >> 1) & 1, s, p.err, true)) break;
-        tc_fence_after();
-        const uint32_t pa = smem_u32(&s.pm[0][0]), va = smem_u32(&s.v[st][0][0]);
+      auto issue_pv = [&](int x, int st, bool acc) {   // O_x (+)= P_x V, P_x from tensor memory
+        const uint32_t va = smem_u32(&s.v[st][0][0]);
 #pragma unroll
         for (int kk = 0; kk < kPKeys / 16; ++kk) {
-          const uint64_t adesc = sw128_desc(pa + (kk >> 2) * kPHalfBytes + (kk & 3) * 32);
           const uint64_t bdesc = sw128_mn_desc(va + kk * 16 * 128, kPHalfBytes, 1024);
-          umma_bf16(tmem + kPColO, adesc, bdesc, kIdescO, (pj > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + col_o(x), tmem + col_s(x) + 8 * kk, bdesc, kIdescO,
+                       (acc || kk > 0) ? 1u : 0u);
         }
-        umma_commit(smem_u32(&s.odone));
-        umma_commit(smem_u32(&s.vempty[st]));
-        if (++pj == pnt) {   // next item: its first P V overwrites O
-          pj = 0;
-          pw += G;
-          if (pw < p.items) pnt = item_of(p, pw).nt;
+      };
+      bool ok = true;
+      int t0 = 0, i = 0;
+      for (int w = blockIdx.x; ok && w < p.items; w += G, ++i) {
+        const int nt = item_of(p, w).nt;
+        ok = mbar_wait(smem_u32(&s.qfull), i & 1, s, p.err, true) &&
+             mbar_wait(smem_u32(&s.kfull[t0 & 1]), (t0 >> 1) & 1, s, p.err, true);
+        if (!ok) break;
+        tc_fence_after();
+        issue_s(0, t0 & 1);
+        umma_commit(smem_u32(&s.sfull[0]));
+        issue_s(1, t0 & 1);
+        umma_commit(smem_u32(&s.sfull[1]));
+        umma_commit(smem_u32(&s.kempty[t0 & 1]));
+        if (nt == 1) umma_commit(smem_u32(&s.qempty));
+        for (int j = 0; j < nt; ++j) {
+          const int T = t0 + j, st = T & 1, st1 = (T + 1) & 1;
+          const bool more = j + 1 < nt;
+          // O_A += P_A(j) V_j (the first P V of an item overwrites O_A, once the previous item's
+          // output has been read out of it)
+          if (!mbar_wait(smem_u32(&s.pfull[0]), T & 1, s, p.err, true) ||
+              !mbar_wait(smem_u32(&s.vfull[st]), (T >> 1) & 1, s, p.err, true) ||
+              (j == 0 && i > 0 && !mbar_wait(smem_u32(&s.oempty[0]), (i - 1) & 1, s, p.err, true))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(0, st, j > 0);
+          if (!more) umma_commit(smem_u32(&s.odone[0]));
+          if (more) {   // S_A(j+1): after the P V that read P_A(j) from the same columns
+            if (!mbar_wait(smem_u32(&s.kfull[st1]), ((T + 1) >> 1) & 1, s, p.err, true)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(0, st1);
+            umma_commit(smem_u32(&s.sfull[0]));
+          }
+          // O_B += P_B(j) V_j
+          if (!mbar_wait(smem_u32(&s.pfull[1]), T & 1, s, p.err, true) ||
+              (j == 0 && i > 0 && !mbar_wait(smem_u32(&s.oempty[1]), (i - 1) & 1, s, p.err, true))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(1, st, j > 0);
+          umma_commit(smem_u32(&s.vempty[st]));
+          if (!more) umma_commit(smem_u32(&s.odone[1]));
+          if (more) {   // S_B(j+1); then K_{j+1} has been read by both
+            issue_s(1, st1);
+            umma_commit(smem_u32(&s.sfull[1]));
+            umma_commit(smem_u32(&s.kempty[st1]));
+            if (j + 2 == nt) umma_commit(smem_u32(&s.qempty));   // the item's last scores
+          }
         }
+        t0 += nt;
       }
       // every MMA issued has completed before the tensor memory is released
       umma_commit(smem_u32(&s.drain));
@@ -342,24 +393,24 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
     }
     __syncwarp();
   } else {
-    // ---- softmax: thread r owns query row q0 + r (tensor-memory lane r) of every item
-    const int r = 32 * warp + lane;
-    const uint32_t lrow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+    // ---- softmax: warps 0-3 tile A, warps 4-7 tile B; thread r owns query row q0 + r (tensor
+    // memory lane r) of every item
+    const int x = warp >> 2;
+    const int r = 32 * (warp & 3) + lane;
+    const uint32_t lrow = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
     bool ok = true;
-    int t = 0;
-    for (int w = blockIdx.x; ok && w < p.items; w += G) {
+    int T = 0, i = 0;
+    for (int w = blockIdx.x; ok && w < p.items; w += G, ++i) {
       const Item it = item_of(p, w);
       const int row = it.q0 + r;
       float m = -INFINITY, l = 0.f;
-      for (int j = 0; j < it.nt; ++j, ++t) {
-        const int sb = t & 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.sfull[sb]), (t >> 1) & 1, s, p.err, true));
+      for (int j = 0; j < it.nt; ++j, ++T) {
+        // S_x(j) complete, and with it every MMA issued before (the P V that read P_x(j-1))
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.sfull[x]), T & 1, s, p.err, true));
         if (!ok) break;
         tc_fence_after();
         float sv[kPKeys];
-        tmem_ld128(lrow + sb * kPKeys, sv);
-        tc_fence_before();
-        mbar_arrive(smem_u32(&s.sempty[sb]));   // the S buffer may take S_{t+2}
+        tmem_ld128(lrow + col_s(x), sv);
         const bool diag = j == it.nt - 1;
         if (diag) {   // causal: key <= query position
           const int lim = row - j * kPKeys;
@@ -382,78 +433,66 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
           m = mx;
           l *= alpha;
         }
-        // P = 2^(s * scale * log2(e) - m), in registers (bf16 pairs) before waiting for the P
-        // buffer; l sums the fp32 p
-        uint32_t pk[kPKeys / 2];
+        // P = 2^(s * scale * log2(e) - m) as bf16 pairs, written over the first 64 columns of
+        // S_x 16 words at a time (word e holds keys 2e, 2e + 1; the scores are all in registers
+        // already); l sums the fp32 p
         float sum0 = 0.f, sum1 = 0.f;
         const float nm = -m;
 #pragma unroll
-        for (int e = 0; e < kPKeys / 2; ++e) {
-          const float p0 = ex2_fast(fmaf(sv[2 * e], p.scale_log2, nm));
-          const float p1 = ex2_fast(fmaf(sv[2 * e + 1], p.scale_log2, nm));
-          sum0 += p0;
-          sum1 += p1;
-          pk[e] = pack_bf16(p0, p1);
+        for (int ch = 0; ch < kPKeys / 32; ++ch) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = ex2_fast(fmaf(sv[32 * ch + 2 * e], p.scale_log2, nm));
+            const float p1 = ex2_fast(fmaf(sv[32 * ch + 2 * e + 1], p.scale_log2, nm));
+            sum0 += p0;
+            sum1 += p1;
+            pk[e] = pack_bf16(p0, p1);
+          }
+          tmem_st16u(lrow + col_s(x) + 16 * ch, pk);
         }
         l += sum0 + sum1;
-        const bool wresc = __any_sync(0xffffffffu, need) && j > 0;
-        if (t > 0) {   // P V of the previous tile done: P may be rewritten, O is stable
-          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.odone), (t - 1) & 1, s, p.err, true));
-          if (!ok) break;
-          tc_fence_after();
-        }
-        if (wresc) {
+        if (__any_sync(0xffffffffu, need) && j > 0) {   // O_x row *= alpha (1 where not needed)
 #pragma unroll
           for (int c = 0; c < kPD; c += 32) {
             float o[32];
-            tmem_ld32(lrow + kPColO + c, o);
+            tmem_ld32(lrow + col_o(x) + c, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(lrow + kPColO + c, o);
+            for (int q = 0; q < 32; ++q) o[q] *= alpha;
+            tmem_st32(lrow + col_o(x) + c, o);
           }
-          tmem_wait_st();
         }
-        if (diag && (j + 1) * kPKeys > p.S) {
-          // keys past the prompt: their P is 0, but their V rows may hold anything (0 * inf)
-          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.vfull[sb]), (t >> 1) & 1, s, p.err, true));
+        if (x == 0 && diag && (j + 1) * kPKeys > p.S) {
+          // keys past the prompt: their P is 0, but their V rows may hold anything (0 * inf);
+          // tile A's threads clear them before either P V of this tile is issued
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.vfull[T & 1]), (T >> 1) & 1, s, p.err, true));
           if (!ok) break;
           if (j * kPKeys + r >= p.S) {
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-              const uint32_t a = smem_u32(&s.v[sb][hh][r * 64]);
+              const uint32_t a = smem_u32(&s.v[T & 1][hh][r * 64]);
 #pragma unroll
               for (int c = 0; c < 8; ++c)
                 asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a + 16 * c), "r"(0u) : "memory");
             }
           }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the MMA
         }
-        // P row r in the 128-byte swizzled K-major layout (16-byte chunk c of row r at c ^ (r % 8))
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const uint32_t base = smem_u32(&s.pm[hh][r * 64]);
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            const int e = hh * 32 + cc * 4;
-            asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + ((cc ^ (r & 7)) << 4)),
-                         "r"(pk[e]), "r"(pk[e + 1]), "r"(pk[e + 2]), "r"(pk[e + 3])
-                         : "memory");
-          }
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // P visible to the MMA
+        tmem_wait_st();   // P_x(j) (and a rescaled O_x row) in tensor memory
         tc_fence_before();
-        mbar_arrive(smem_u32(&s.pfull));
+        mbar_arrive(smem_u32(&s.pfull[x]));
       }
       if (!ok) break;
-      // the item's output: O / l once its last P V is done
-      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.odone), (t - 1) & 1, s, p.err, true));
+      // the item's output: O_x / l once its last P V is done; then O_x is free for the next item
+      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.odone[x]), i & 1, s, p.err, true));
       if (!ok) break;
       tc_fence_after();
       const float inv = 1.0f / l;
-      bf16* dst = p.out + (static_cast<long long>(it.b) * p.S + row) * p.nq * kPD + it.h * kPD;
+      bf16* dst = p.out + (static_cast<long long>(it.b) * p.S + row) * p.nq * kPD + (it.h0 + x) * kPD;
 #pragma unroll
       for (int c = 0; c < kPD; c += 32) {
         float o[32];
-        tmem_ld32(lrow + kPColO + c, o);
+        tmem_ld32(lrow + col_o(x) + c, o);
         if (row < p.S) {
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
@@ -466,7 +505,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
           }
         }
       }
-      tc_fence_before();   // O read before the next item's first P V overwrites it
+      tc_fence_before();
+      mbar_arrive(smem_u32(&s.oempty[x]));
     }
   }
   tc_fence_before();
@@ -513,7 +553,7 @@ extern "C" int kopt_prefill_attn(const void* q, const kopt_kv_cache* cache, void
     return KOPT_ERR_ARG;
   }
   const long long nqt = (S + kPRows - 1) / kPRows;
-  const long long items = nqt * B * nq;
+  const long long items = nqt * B * nkv * kPHeads;
   if (items >= (1ll << 31)) return KOPT_ERR_ARG;
   int rc = set_device(device);
   if (rc) return rc;
