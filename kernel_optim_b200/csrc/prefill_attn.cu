@@ -256,19 +256,38 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
       const int npg_all = (p.S + kPPage - 1) / kPPage;
       int t = 0, i = 0;
       bool ok = true;
+      // A tile's page ids are read one tile ahead, all together (one memory round trip, not one
+      // per page, and off the path of the copies), and serve both its K and its V.
+      constexpr int kTilePages = kPKeys / kPPage;
+      int rows[kTilePages], nxt[kTilePages];
+      auto fetch_pids = [&](int b, int j) {
+        const int* bt = p.bt + static_cast<long long>(b) * p.bt_stride + j * kTilePages;
+        const int npg = min(kTilePages, npg_all - j * kTilePages);
+#pragma unroll
+        for (int pg = 0; pg < kTilePages; ++pg) nxt[pg] = pg < npg ? __ldg(bt + pg) : 0;
+      };
+      auto page_rows = [&](const Item& it) {   // rows of the fetched ids; nxt is free again
+#pragma unroll
+        for (int pg = 0; pg < kTilePages; ++pg) {
+          int pid = nxt[pg];
+          if (pid < 0 || pid >= p.num_pages) {   // recorded; a valid page keeps the byte count
+            atomicOr(p.err, KOPT_DEV_ERR_PAGE);
+            pid = 0;
+          }
+          rows[pg] = (pid * p.nkv + it.kvh) * kPPage;
+        }
+      };
+      if (PAGED && static_cast<int>(blockIdx.x) < p.items) fetch_pids(item_of(p, blockIdx.x).b, 0);
       auto load_tile = [&](const CUtensorMap* map, bf16 (*dst)[kPHalf], uint32_t bar, const Item& it, int j) {
         if (PAGED) {
-          const int npg = min(kPKeys / kPPage, npg_all - j * (kPKeys / kPPage));
+          const int npg = min(kTilePages, npg_all - j * kTilePages);
           mbar_arrive_expect_tx(bar, static_cast<uint32_t>(npg) * 2u * kPPage * 64u * 2u);
-          for (int pg = 0; pg < npg; ++pg) {
-            int pid = p.bt[static_cast<long long>(it.b) * p.bt_stride + j * (kPKeys / kPPage) + pg];
-            if (pid < 0 || pid >= p.num_pages) {   // recorded; a valid page keeps the byte count
-              atomicOr(p.err, KOPT_DEV_ERR_PAGE);
-              pid = 0;
+#pragma unroll
+          for (int pg = 0; pg < kTilePages; ++pg) {
+            if (pg < npg) {
+              tma_load_2d(smem_u32(&dst[0][pg * kPPage * 64]), map, 0, rows[pg], bar, pol);
+              tma_load_2d(smem_u32(&dst[1][pg * kPPage * 64]), map, 64, rows[pg], bar, pol);
             }
-            const int row = (pid * p.nkv + it.kvh) * kPPage;
-            tma_load_2d(smem_u32(&dst[0][pg * kPPage * 64]), map, 0, row, bar, pol);
-            tma_load_2d(smem_u32(&dst[1][pg * kPPage * 64]), map, 64, row, bar, pol);
           }
         } else {
           mbar_arrive_expect_tx(bar, 2 * kPHalfBytes);
@@ -289,6 +308,11 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
                         smem_u32(&s.qfull), pol_q);
         for (int j = 0; j < it.nt; ++j) {
           const int st = t & 1, use = t >> 1;
+          if (PAGED) {
+            page_rows(it);
+            if (j + 1 < it.nt) fetch_pids(it.b, j + 1);
+            else if (w + G < p.items) fetch_pids(item_of(p, w + G).b, 0);
+          }
           if (t >= kPStages && !mbar_wait(smem_u32(&s.kempty[st]), (use - 1) & 1, s, p.err, true)) {
             ok = false;
             break;
