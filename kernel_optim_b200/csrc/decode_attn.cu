@@ -1398,6 +1398,430 @@ __global__ void __launch_bounds__(verify_threads<MT>()) verify_attn_kernel(const
   if (threadIdx.x == 0) atomicExch(&p.ws_cnt[pair], 0);
 }
 
+// ------------------------------------------------- verify attention on tcgen05 (T = 5 .. 8)
+// The same work split as verify_attn_kernel (one CTA per pair and split of the keys), with the
+// arithmetic on the 5th-generation tensor cores. The pair's 4T query rows (row 4t + g: token t,
+// head kvh * 4 + g; rows 4T .. 31 zero) fill 32 rows of a 128-row query tile, four times: copy w
+// in rows 32w .. 32w + 31. S = Q K^T (M = 128, N = 128 keys) and O += P V (P from tensor memory)
+// run as full-size tcgen05 MMAs, and the four copies split the softmax: warp w (tensor-memory
+// lanes 32w ..) takes keys 32w .. 32w + 31 of each 128-key tile for its copy of the rows, with a
+// row maximum shared through shared memory, and writes P for those keys only (zero elsewhere), so
+// copy w's O and l are sums over its quarter of the keys; the four are added at the end. Keys go
+// in tiles of 128 (8 pages) through a 3-deep TMA ring; two S buffers, so the scores of tile j + 1
+// are ready when the softmax of tile j ends. Per tile j the MMA order is O += P(j) V_j, then
+// S(j + 2) into the buffer P(j) came from (the MMAs of one thread execute in issue order, and a
+// commit tracks every MMA issued before it). The running maximum moves only when a row's maximum
+// grows by more than 2^8. The epilogue writes the output when the pair has one split, else the
+// split's partial (m, l, O), and the split that finishes last merges them.
+//   warps 0-3  softmax, epilogue, merge;   warp 4  TMA producer;   warp 5  tensor memory + MMAs.
+constexpr int kTcKeys = 128;
+constexpr int kTcStages = 3;
+constexpr int kTcRows = 32;                  // query rows held (4 T <= 32)
+constexpr int kTcSoft = 4;                   // softmax warps = row copies
+constexpr int kTcThreads = 6 * 32;
+constexpr uint32_t kTcCols = 512;            // S0, S1, O: 128 fp32 columns each
+constexpr int kTcHalf = 128 * 64;            // elements of one 64-dim half of a 128-row tile
+constexpr uint32_t kTcHalfBytes = kTcHalf * 2;
+constexpr float kTcRescale = 8.f;
+// kind::f16: fp32 accumulator, bf16 A and B, A K-major; M = 128, N = 128; B K-major (S) or
+// MN-major (bit 16: V with dims contiguous)
+constexpr uint32_t kTcIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t kTcIdescO = kTcIdescS | (1u << 16);
+
+struct __align__(1024) TcSmem {
+  bf16 q[2][kTcHalf];                        // query tile: [dims half][128 rows][64], swizzled
+  bf16 k[kTcStages][2][kTcHalf];             // key tiles: [dims half][128 keys][64]
+  bf16 v[kTcStages][2][kTcHalf];             // value tiles, same layout (MN-major operand)
+  float red[2][kTcSoft][kTcRows];            // per tile parity: each copy's row maxima
+  float lsum[kTcSoft][kTcRows];              // each copy's row sums at the end
+  unsigned long long kfull[kTcStages], vfull[kTcStages], kempty[kTcStages], vempty[kTcStages];
+  unsigned long long sfull[2], pfull[2], pvdone[2], odone, drain;
+  unsigned long long redbar[2], epibar, partbar, lastbar;   // among the softmax warps (bounded)
+  uint32_t tmem;
+  int last;
+  volatile int abort;
+};
+constexpr size_t kTcSmemBytes = sizeof(TcSmem) + 1024;
+static_assert(kTcSmemBytes <= 232448, "verify (tcgen05) shared memory above the per-CTA limit");
+static_assert(sizeof(float) * kTcSoft * kTcRows * kD <= sizeof(bf16) * kTcStages * 2 * kTcHalf,
+              "the copies' outputs do not fit in the key ring");
+
+template <bool PAGED>
+__global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_constant__ Params p) {
+  extern __shared__ unsigned char smem_raw[];
+  TcSmem& s = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                         ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = p.nkv * kGroup;
+  const int split = blockIdx.x % p.nsplit;
+  const int pair = blockIdx.x / p.nsplit;
+  const int b = pair / p.nkv, kvh = pair % p.nkv;
+  const int T = p.T;                                    // 4 T <= kTcRows
+  int p0 = p.pos[b];
+  if (p0 < 0 || p0 + T > p.cap) {
+    if (threadIdx.x == 0 && split == 0 && kvh == 0) atomicOr(p.ws_err, KOPT_DEV_ERR_LEN);
+    p0 = min(max(p0, 0), p.cap - T);
+  }
+  const int Lb = p0 + T;                                // keys the last query sees
+  const int per = ceil_div_i(ceil_div_i(Lb, p.nsplit), kPage) * kPage;
+  const int s0 = split * per, s1 = min(Lb, s0 + per);   // this split's keys (s0 on a page edge)
+  const int pg0 = s0 / kPage;
+  const int pg1 = s1 > s0 ? ceil_div_i(s1, kPage) : pg0;   // pages [pg0, pg1)
+  const int nt = ceil_div_i(pg1 - pg0, kTcKeys / kPage);   // key tiles
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTcStages; ++i) {
+      mbar_init(smem_u32(&s.kfull[i]), 1);
+      mbar_init(smem_u32(&s.vfull[i]), 1);
+      mbar_init(smem_u32(&s.kempty[i]), 1);
+      mbar_init(smem_u32(&s.vempty[i]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&s.sfull[i]), 1);
+      mbar_init(smem_u32(&s.pfull[i]), 32 * kTcSoft);
+      mbar_init(smem_u32(&s.pvdone[i]), 1);
+    }
+    mbar_init(smem_u32(&s.odone), 1);
+    mbar_init(smem_u32(&s.drain), 1);
+    mbar_init(smem_u32(&s.redbar[0]), 32 * kTcSoft);
+    mbar_init(smem_u32(&s.redbar[1]), 32 * kTcSoft);
+    mbar_init(smem_u32(&s.epibar), 32 * kTcSoft);
+    mbar_init(smem_u32(&s.partbar), 32 * kTcSoft);
+    mbar_init(smem_u32(&s.lastbar), 1);
+    s.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(&s.tmem), kTcCols);
+    tmem_relinquish();
+  }
+  // the query tile in the 128-byte-swizzled K-major layout (16-byte chunk c of row r at
+  // c ^ (r % 8)): row r holds query row r % 32 (zero past 4 T)
+  for (int i = threadIdx.x; i < 128 * 16; i += kTcThreads) {
+    const int r = i >> 4, c = i & 15;              // row, 16-byte chunk of its 256 bytes
+    const int qr = r % kTcRows, t = qr / kGroup, g = qr % kGroup;
+    uint4 val = make_uint4(0u, 0u, 0u, 0u);
+    if (qr < kGroup * T)
+      val = *reinterpret_cast<const uint4*>(p.q + (static_cast<long long>(b) * T + t) * nq * kD +
+                                            (kvh * kGroup + g) * kD + c * 8);
+    const int h = c >> 3, cc = c & 7;
+    *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&s.q[h][0]) + r * 128 + ((cc ^ (r & 7)) << 4)) = val;
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the MMA reads it
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem;
+
+  if (warp == 4) {
+    // ---- producer warp: K and V tiles of 8 pages, lane i copying page i of the tile (its id read
+    // one tile ahead); lane 0 waits for the slots and sets the byte counts
+    const uint64_t pol = evict_first_policy();
+    constexpr int kTP = kTcKeys / kPage;
+    const int* bt_row = PAGED ? p.bt + static_cast<long long>(b) * p.bt_stride : nullptr;
+    auto fetch = [&](int j) {
+      const int pg = pg0 + j * kTP + lane;
+      return (PAGED && lane < kTP && pg < pg1) ? __ldg(bt_row + pg) : 0;
+    };
+    int nxt = nt > 0 ? fetch(0) : 0;
+    int t = 0;
+    bool ok = true;
+    for (; t < nt; ++t) {
+      const int st = t % kTcStages, use = t / kTcStages;
+      const int npg = min(kTP, pg1 - pg0 - t * kTP);
+      int row = 0;
+      if (PAGED) {
+        int pid = nxt;
+        if (lane < npg && (pid < 0 || pid >= p.num_pages)) {   // recorded; a valid page keeps the count
+          atomicOr(p.ws_err, KOPT_DEV_ERR_PAGE);
+          pid = 0;
+        }
+        row = (pid * p.nkv + kvh) * kPage;
+        if (t + 1 < nt) nxt = fetch(t + 1);
+      }
+      const int key = (pg0 + t * kTP + lane) * kPage;
+      for (int kv = 0; kv < 2; ++kv) {
+        unsigned long long* empty = kv == 0 ? s.kempty : s.vempty;
+        unsigned long long* full = kv == 0 ? s.kfull : s.vfull;
+        ok = __all_sync(0xffffffffu, t < kTcStages ||
+                        mbar_wait(smem_u32(&empty[st]), (use - 1) & 1, s, p.ws_err, true));
+        if (!ok) break;
+        if (lane == 0) mbar_arrive_expect_tx(smem_u32(&full[st]), static_cast<uint32_t>(npg) * 2u * kBoxBytes);
+        __syncwarp();
+        if (lane < npg) {
+          const CUtensorMap* map = kv == 0 ? &p.tmk : &p.tmv;
+          bf16 (*dst)[kTcHalf] = kv == 0 ? s.k[st] : s.v[st];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t d = smem_u32(&dst[h][lane * kPage * kHalf]);
+            if (PAGED) tma_load_2d(d, map, h * kHalf, row, smem_u32(&full[st]), pol);
+            else tma_load_4d(d, map, h * kHalf, key, kvh, b, smem_u32(&full[st]), pol);
+          }
+        }
+      }
+      if (!ok) break;
+    }
+    // every copy issued has landed (the newest phase of each slot; after an abort the tile whose
+    // V was not issued waits out its bound)
+    if (lane == 0) {
+      for (int k = max(t + (ok ? 0 : 1) - kTcStages, 0); k < t + (ok ? 0 : 1) && k < nt; ++k) {
+        mbar_wait(smem_u32(&s.kfull[k % kTcStages]), (k / kTcStages) & 1, s, p.ws_err, false);
+        mbar_wait(smem_u32(&s.vfull[k % kTcStages]), (k / kTcStages) & 1, s, p.ws_err, false);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ---- MMAs: S(0), S(1), then per tile j: O += P(j) V_j, S(j + 2)
+      auto issue_s = [&](int j) {
+        const uint32_t qa = smem_u32(&s.q[0][0]), ka = smem_u32(&s.k[j % kTcStages][0][0]);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kTcHalfBytes + (kk & 3) * 32;
+          umma_bf16(tmem + 128u * (j & 1), sw128_desc(qa + off), sw128_desc(ka + off), kTcIdescS, kk > 0);
+        }
+        umma_commit(smem_u32(&s.sfull[j & 1]));
+        umma_commit(smem_u32(&s.kempty[j % kTcStages]));
+      };
+      bool ok = true;
+      for (int j = 0; j < 2 && j < nt; ++j) {
+        if (!mbar_wait(smem_u32(&s.kfull[j]), 0, s, p.ws_err, true)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_s(j);
+      }
+      for (int j = 0; ok && j < nt; ++j) {
+        if (!mbar_wait(smem_u32(&s.pfull[j & 1]), (j >> 1) & 1, s, p.ws_err, true) ||
+            !mbar_wait(smem_u32(&s.vfull[j % kTcStages]), (j / kTcStages) & 1, s, p.ws_err, true))
+          break;
+        tc_fence_after();
+        const uint32_t va = smem_u32(&s.v[j % kTcStages][0][0]);
+#pragma unroll
+        for (int kk = 0; kk < kTcKeys / 16; ++kk)
+          umma_bf16_ts(tmem + 256u, tmem + 128u * (j & 1) + 8 * kk,
+                       sw128_mn_desc(va + kk * 16 * 128, kTcHalfBytes, 1024), kTcIdescO,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(smem_u32(&s.pvdone[j & 1]));
+        umma_commit(smem_u32(&s.vempty[j % kTcStages]));
+        if (j == nt - 1) umma_commit(smem_u32(&s.odone));
+        if (j + 2 < nt) {
+          if (!mbar_wait(smem_u32(&s.kfull[(j + 2) % kTcStages]), ((j + 2) / kTcStages) & 1, s, p.ws_err, true))
+            break;
+          tc_fence_after();
+          issue_s(j + 2);
+        }
+      }
+      umma_commit(smem_u32(&s.drain));
+      mbar_wait(smem_u32(&s.drain), 0, s, p.ws_err, false);
+    }
+    __syncwarp();
+  } else {
+    // ---- warps 0-3: warp w holds copy w of row r = lane (token r / 4, head kvh * 4 + r % 4) in
+    // tensor-memory lane 32 w + r and takes keys 32 w .. 32 w + 31 of each tile
+    const int w = warp, r = lane;
+    const uint32_t lq = tmem + (static_cast<uint32_t>(32 * w) << 16);
+    const int lim = r < kGroup * T ? p0 + r / kGroup : 0x7fffffff;   // last key the row sees
+    float m = kNegBig, l = 0.f;
+    bool ok = true;
+    uint32_t zero[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) zero[e] = 0u;
+    for (int j = 0; j < nt; ++j) {
+      const int bb = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.sfull[bb]), (j >> 1) & 1, s, p.ws_err, true));
+      if (!ok) break;
+      tc_fence_after();
+      float sv[32];
+      tmem_ld32(lq + 128u * bb + 32u * w, sv);
+      const int key0 = s0 + j * kTcKeys + 32 * w;   // this warp's first key in the tile
+      if (key0 + 32 > s1 || key0 + 31 > lim) {       // keys past the split or the row
+        const int cl = min(s1 - 1, lim) - key0;
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (c > cl) sv[c] = -INFINITY;
+      }
+      float mx0 = sv[0], mx1 = sv[1];
+#pragma unroll
+      for (int c = 2; c < 32; c += 2) {
+        mx0 = fmaxf(mx0, sv[c]);
+        mx1 = fmaxf(mx1, sv[c + 1]);
+      }
+      s.red[bb][w][r] = fmaxf(mx0, mx1);
+      mbar_arrive(smem_u32(&s.redbar[bb]));   // every copy's maximum of this tile is in
+      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.redbar[bb]), (j >> 1) & 1, s, p.ws_err, true));
+      if (!ok) break;
+      const float mx = fmaxf(fmaxf(s.red[bb][0][r], s.red[bb][1][r]), fmaxf(s.red[bb][2][r], s.red[bb][3][r])) *
+                       p.scale_log2;
+      const bool need = mx > m + kTcRescale;
+      float alpha = 1.f;
+      if (need) {
+        alpha = ex2_fast(m - mx);
+        m = mx;
+        l *= alpha;
+      }
+      uint32_t pk[16];
+      float sum0 = 0.f, sum1 = 0.f;
+      const float nm = -m;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float a0 = ex2_fast(fmaf(sv[2 * e], p.scale_log2, nm));
+        const float a1 = ex2_fast(fmaf(sv[2 * e + 1], p.scale_log2, nm));
+        sum0 += a0;
+        sum1 += a1;
+        pk[e] = pack_bf16(a0, a1);
+      }
+      l += sum0 + sum1;
+      // P of this copy over the first 64 columns: its keys' words 16 w .. 16 w + 15, zero elsewhere
+#pragma unroll
+      for (int q = 0; q < kTcSoft; ++q) tmem_st16u(lq + 128u * bb + 16u * q, q == w ? pk : zero);
+      if (__any_sync(0xffffffffu, need) && j > 0) {
+        // this copy's O row *= alpha, once the previous P V has completed
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.pvdone[bb ^ 1]), ((j - 1) >> 1) & 1, s, p.ws_err, true));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kD; c += 32) {
+          float o[32];
+          tmem_ld32(lq + 256u + c, o);
+#pragma unroll
+          for (int q = 0; q < 32; ++q) o[q] *= alpha;
+          tmem_st32(lq + 256u + c, o);
+        }
+      }
+      if (s0 + (j + 1) * kTcKeys > s1) {
+        // V rows past the split's keys may hold anything: zero them so 0 * V stays 0
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.vfull[j % kTcStages]), (j / kTcStages) & 1, s, p.ws_err, true));
+        if (!ok) break;
+        const int nv = s1 - (s0 + j * kTcKeys);
+        for (int i = nv * 16 + 32 * w + lane; i < kTcKeys * 16; i += 32 * kTcSoft) {
+          const int rr = i >> 4, part = i & 15;
+          const uint32_t a = smem_u32(&s.v[j % kTcStages][part >> 3][0]) + rr * 128 + ((part & 7) << 4);
+          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&s.pfull[bb]));
+    }
+    // ---- epilogue: add the four copies (through the key ring, free once the last P V is done);
+    // warp w then owns dims 32 w .. 32 w + 31 of row r
+    float* ob = reinterpret_cast<float*>(&s.k[0][0][0]);   // [copy][row][kD]
+    float O[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) O[c] = 0.f;
+    float L = 0.f;
+    const bool have = ok && nt > 0;
+    if (have) {
+      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.odone), 0, s, p.ws_err, true));
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kD; c += 32) {
+          float o[32];
+          tmem_ld32(lq + 256u + c, o);
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(&ob[(w * kTcRows + r) * kD + c + e]) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+        }
+        s.lsum[w][r] = l;
+      }
+    }
+    mbar_arrive(smem_u32(&s.epibar));
+    ok = __all_sync(0xffffffffu, ok && mbar_wait(smem_u32(&s.epibar), 0, s, p.ws_err, true));
+    const bool good = ok && have;
+    if (good) {
+#pragma unroll
+      for (int q = 0; q < kTcSoft; ++q) {
+        L += s.lsum[q][r];
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          const float4 x = *reinterpret_cast<const float4*>(&ob[(q * kTcRows + r) * kD + 32 * w + e]);
+          O[e] += x.x;
+          O[e + 1] += x.y;
+          O[e + 2] += x.z;
+          O[e + 3] += x.w;
+        }
+      }
+    }
+    const int t = r / kGroup, g = r % kGroup;
+    bf16* dst = p.out + ((static_cast<long long>(b) * T + t) * nq + kvh * kGroup + g) * kD + 32 * w;
+    if (p.nsplit == 1) {
+      if (good && r < kGroup * T) {
+        const float inv = 1.0f / L;
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          uint4 u;
+          u.x = pack_bf16(O[c] * inv, O[c + 1] * inv);
+          u.y = pack_bf16(O[c + 2] * inv, O[c + 3] * inv);
+          u.z = pack_bf16(O[c + 4] * inv, O[c + 5] * inv);
+          u.w = pack_bf16(O[c + 6] * inv, O[c + 7] * inv);
+          *reinterpret_cast<uint4*>(dst + c) = u;
+        }
+      }
+    } else {
+      // the split's partial (every split writes one, so the counts add up), then the merge
+      const long long slot = blockIdx.x;
+      float* po = p.ws_o + (slot * kTcRows + r) * kD + 32 * w;
+#pragma unroll
+      for (int c = 0; c < 32; c += 4) *reinterpret_cast<float4*>(po + c) = make_float4(O[c], O[c + 1], O[c + 2], O[c + 3]);
+      if (w == 0) p.ws_ml[slot * kTcRows + r] = make_float2(good ? m : kNegBig, good ? L : 0.f);
+      __threadfence();
+      mbar_arrive(smem_u32(&s.partbar));
+      if (threadIdx.x == 0) {
+        s.last = mbar_wait(smem_u32(&s.partbar), 0, s, p.ws_err, false) &&
+                 atomicAdd(&p.ws_cnt[pair], 1) == p.nsplit - 1;
+        if (s.last) __threadfence();   // acquire the other splits' partials
+        mbar_arrive(smem_u32(&s.lastbar));
+      }
+      const bool merge = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.lastbar), 0, s, p.ws_err, false)) && s.last;
+      if (merge) {   // online log-sum-exp over every split's partial
+        const long long first = blockIdx.x - split;
+        float Mm = kNegBig, Lm = 0.f;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) O[c] = 0.f;
+        for (int sp = 0; sp < p.nsplit; ++sp) {
+          const long long sl = first + sp;
+          const float2 ml = __ldcg(&p.ws_ml[sl * kTcRows + r]);
+          const float mn = fmaxf(Mm, ml.x);
+          const float a = exp2f(Mm - mn), f = exp2f(ml.x - mn);
+          Lm = Lm * a + ml.y * f;
+          const float* src = p.ws_o + (sl * kTcRows + r) * kD + 32 * w;
+#pragma unroll
+          for (int c = 0; c < 32; c += 4) {
+            const float4 x = __ldcg(reinterpret_cast<const float4*>(src + c));
+            O[c] = O[c] * a + x.x * f;
+            O[c + 1] = O[c + 1] * a + x.y * f;
+            O[c + 2] = O[c + 2] * a + x.z * f;
+            O[c + 3] = O[c + 3] * a + x.w * f;
+          }
+          Mm = mn;
+        }
+        if (r < kGroup * T) {
+          const float inv = 1.0f / Lm;
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            uint4 u;
+            u.x = pack_bf16(O[c] * inv, O[c + 1] * inv);
+            u.y = pack_bf16(O[c + 2] * inv, O[c + 3] * inv);
+            u.z = pack_bf16(O[c + 4] * inv, O[c + 5] * inv);
+            u.w = pack_bf16(O[c + 6] * inv, O[c + 7] * inv);
+            *reinterpret_cast<uint4*>(dst + c) = u;
+          }
+        }
+        if (threadIdx.x == 0) atomicExch(&p.ws_cnt[pair], 0);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTcCols);
+  }
+}
+
 // ------------------------------------------------------------------------------ host side
 
 struct WsLayout {
@@ -1578,7 +2002,30 @@ int verify_occupancy(int device, int* blocks_per_sm) {
     return KOPT_ERR_CUDA;
   return KOPT_OK;
 }
+template <bool PAGED>
+int verify_tc_occupancy(int device, int* blocks_per_sm) {
+  static int configured[64] = {0};
+  if (device < 0 || device >= 64) return KOPT_ERR_ARG;
+  auto kern = verify_tc_kernel<PAGED>;
+  if (!configured[device]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kTcSmemBytes)) != cudaSuccess)
+      return KOPT_ERR_CUDA;
+    configured[device] = 1;
+  }
+  if (blocks_per_sm &&
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kern, kTcThreads, kTcSmemBytes) !=
+          cudaSuccess)
+    return KOPT_ERR_CUDA;
+  return KOPT_OK;
+}
+// T > 4 runs on the tensor-memory kernel (verify_tc_kernel), T <= 4 on verify_attn_kernel
+inline bool verify_on_tc(int T) { return T > 4; }
 int verify_configure(int device, int T, int* blocks_per_sm) {
+  if (verify_on_tc(T)) {
+    const int rc = verify_tc_occupancy<true>(device, blocks_per_sm);
+    return rc ? rc : verify_tc_occupancy<false>(device, nullptr);
+  }
   int rc = verify_tiles(T) == 1 ? verify_occupancy<true, 1>(device, blocks_per_sm)
                                 : verify_occupancy<true, 2>(device, blocks_per_sm);
   if (rc) return rc;
@@ -1600,6 +2047,12 @@ int launch_verify(const kopt_plan* plan, Params& p, void* stream) {
   if (rc) return rc;
   p.tblocks = 1;
   p.nsplit = plan->grid / (plan->B * plan->nkv);
+  if (verify_on_tc(plan->T)) {
+    rc = verify_tc_occupancy<PAGED>(plan->device, nullptr);
+    if (rc) return rc;
+    verify_tc_kernel<PAGED><<<plan->grid, kTcThreads, kTcSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
+    return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+  }
   return verify_tiles(plan->T) == 1 ? launch_verify_t<PAGED, 1>(plan, p, stream)
                                     : launch_verify_t<PAGED, 2>(plan, p, stream);
 }
