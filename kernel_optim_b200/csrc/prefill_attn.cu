@@ -143,91 +143,78 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
   const uint32_t tmem = s.tmem;
 
   if (warp == kPProducer) {
-    if (lane == 0) {
-      // ---- TMA producer: each item's two query tiles, then its K and V tiles through the 2-deep
-      // ring; tiles are counted across items (t), so the ring never drains between items.
-      // Queries are read once (evict first); K/V tiles are read again by the other head pair of
-      // the kv head and the later query tiles of the sequence (evict last).
-      const uint64_t pol_q = evict_first_policy();
-      uint64_t pol;
-      asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-      const int npg_all = (p.S + kPPage - 1) / kPPage;
-      int t = 0, i = 0;
-      bool ok = true;
-      // A tile's page ids are read one tile ahead, all together (one memory round trip, not one
-      // per page, and off the path of the copies), and serve both its K and its V.
-      constexpr int kTilePages = kPKeys / kPPage;
-      int rows[kTilePages], nxt[kTilePages];
-      auto fetch_pids = [&](int b, int j) {
-        const int* bt = p.bt + static_cast<long long>(b) * p.bt_stride + j * kTilePages;
-        const int npg = min(kTilePages, npg_all - j * kTilePages);
-#pragma unroll
-        for (int pg = 0; pg < kTilePages; ++pg) nxt[pg] = pg < npg ? __ldg(bt + pg) : 0;
-      };
-      auto page_rows = [&](const Item& it) {   // rows of the fetched ids; nxt is free again
-#pragma unroll
-        for (int pg = 0; pg < kTilePages; ++pg) {
-          int pid = nxt[pg];
-          if (pid < 0 || pid >= p.num_pages) {   // recorded; a valid page keeps the byte count
+    // ---- TMA producer warp: each item's two query tiles, then its K and V tiles through the
+    // 2-deep ring, lane i copying page i of a tile (its id read one tile ahead) while lane 0 waits
+    // for the slots and sets the byte counts; tiles are counted across items (t), so the ring
+    // never drains between items. Queries are read once (evict first); K/V tiles are read again by
+    // the other head pair of the kv head and the later query tiles of the sequence (evict last).
+    const uint64_t pol_q = evict_first_policy();
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    const int npg_all = (p.S + kPPage - 1) / kPPage;
+    constexpr int kTilePages = kPKeys / kPPage;
+    auto fetch = [&](int b, int j) {   // this lane's page id of tile j of sequence b
+      const int pg = j * kTilePages + lane;
+      return (PAGED && lane < kTilePages && pg < npg_all)
+                 ? __ldg(p.bt + static_cast<long long>(b) * p.bt_stride + pg) : 0;
+    };
+    int nxt = static_cast<int>(blockIdx.x) < p.items ? fetch(item_of(p, blockIdx.x).b, 0) : 0;
+    int t = 0, i = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < p.items; w += G, ++i) {
+      const Item it = item_of(p, w);
+      // the previous item's last scores are computed: its query tiles may be replaced
+      ok = __all_sync(0xffffffffu, i == 0 || mbar_wait(smem_u32(&s.qempty), (i - 1) & 1, s, p.err, true));
+      if (!ok) break;
+      if (lane == 0) mbar_arrive_expect_tx(smem_u32(&s.qfull), 4 * kPHalfBytes);
+      __syncwarp();
+      if (lane < 4)
+        tma_load_4d(smem_u32(&s.q[lane >> 1][lane & 1][0]), &p.tmq, 64 * (lane & 1), it.h0 + (lane >> 1),
+                    it.q0, it.b, smem_u32(&s.qfull), pol_q);
+      for (int j = 0; j < it.nt; ++j) {
+        const int st = t & 1, use = t >> 1;
+        const int npg = PAGED ? min(kTilePages, npg_all - j * kTilePages) : 0;
+        int row = 0;
+        if (PAGED) {
+          int pid = nxt;
+          if (lane < npg && (pid < 0 || pid >= p.num_pages)) {   // recorded; a valid page keeps the count
             atomicOr(p.err, KOPT_DEV_ERR_PAGE);
             pid = 0;
           }
-          rows[pg] = (pid * p.nkv + it.kvh) * kPPage;
+          row = (pid * p.nkv + it.kvh) * kPPage;
+          if (j + 1 < it.nt) nxt = fetch(it.b, j + 1);
+          else if (w + G < p.items) nxt = fetch(item_of(p, w + G).b, 0);
         }
-      };
-      if (PAGED && static_cast<int>(blockIdx.x) < p.items) fetch_pids(item_of(p, blockIdx.x).b, 0);
-      auto load_tile = [&](const CUtensorMap* map, bf16 (*dst)[kPHalf], uint32_t bar, const Item& it, int j) {
-        if (PAGED) {
-          const int npg = min(kTilePages, npg_all - j * kTilePages);
-          mbar_arrive_expect_tx(bar, static_cast<uint32_t>(npg) * 2u * kPPage * 64u * 2u);
-#pragma unroll
-          for (int pg = 0; pg < kTilePages; ++pg) {
-            if (pg < npg) {
-              tma_load_2d(smem_u32(&dst[0][pg * kPPage * 64]), map, 0, rows[pg], bar, pol);
-              tma_load_2d(smem_u32(&dst[1][pg * kPPage * 64]), map, 64, rows[pg], bar, pol);
-            }
-          }
-        } else {
-          mbar_arrive_expect_tx(bar, 2 * kPHalfBytes);
-          tma_load_4d(smem_u32(&dst[0][0]), map, 0, j * kPKeys, it.kvh, it.b, bar, pol);
-          tma_load_4d(smem_u32(&dst[1][0]), map, 64, j * kPKeys, it.kvh, it.b, bar, pol);
-        }
-      };
-      for (int w = blockIdx.x; ok && w < p.items; w += G, ++i) {
-        const Item it = item_of(p, w);
-        // the previous item's last scores are computed: its query tiles may be replaced
-        if (i >= 1 && !mbar_wait(smem_u32(&s.qempty), (i - 1) & 1, s, p.err, true)) break;
-        mbar_arrive_expect_tx(smem_u32(&s.qfull), 4 * kPHalfBytes);
-#pragma unroll
-        for (int x = 0; x < kPHeads; ++x)
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh)
-            tma_load_4d(smem_u32(&s.q[x][hh][0]), &p.tmq, 64 * hh, it.h0 + x, it.q0, it.b,
-                        smem_u32(&s.qfull), pol_q);
-        for (int j = 0; j < it.nt; ++j) {
-          const int st = t & 1, use = t >> 1;
+        for (int kv = 0; kv < 2; ++kv) {
+          unsigned long long* empty = kv == 0 ? s.kempty : s.vempty;
+          unsigned long long* full = kv == 0 ? s.kfull : s.vfull;
+          ok = __all_sync(0xffffffffu, t < kPStages ||
+                          mbar_wait(smem_u32(&empty[st]), (use - 1) & 1, s, p.err, true));
+          if (!ok) break;
+          const CUtensorMap* map = kv == 0 ? &p.tmk : &p.tmv;
+          bf16 (*dst)[kPHalf] = kv == 0 ? s.k[st] : s.v[st];
+          const uint32_t fb = smem_u32(&full[st]);
+          if (lane == 0)
+            mbar_arrive_expect_tx(fb, PAGED ? static_cast<uint32_t>(npg) * 2u * kPPage * 64u * 2u : 2 * kPHalfBytes);
+          __syncwarp();
           if (PAGED) {
-            page_rows(it);
-            if (j + 1 < it.nt) fetch_pids(it.b, j + 1);
-            else if (w + G < p.items) fetch_pids(item_of(p, w + G).b, 0);
+            if (lane < npg) {
+              tma_load_2d(smem_u32(&dst[0][lane * kPPage * 64]), map, 0, row, fb, pol);
+              tma_load_2d(smem_u32(&dst[1][lane * kPPage * 64]), map, 64, row, fb, pol);
+            }
+          } else if (lane < 2) {
+            tma_load_4d(smem_u32(&dst[lane][0]), map, 64 * lane, j * kPKeys, it.kvh, it.b, fb, pol);
           }
-          if (t >= kPStages && !mbar_wait(smem_u32(&s.kempty[st]), (use - 1) & 1, s, p.err, true)) {
-            ok = false;
-            break;
-          }
-          load_tile(&p.tmk, s.k[st], smem_u32(&s.kfull[st]), it, j);
-          if (t >= kPStages && !mbar_wait(smem_u32(&s.vempty[st]), (use - 1) & 1, s, p.err, true)) {
-            ++t;   // its K is in flight: drained below
-            ok = false;
-            break;
-          }
-          load_tile(&p.tmv, s.v[st], smem_u32(&s.vfull[st]), it, j);
-          ++t;
         }
+        if (!ok) break;
+        ++t;
       }
-      // every copy issued has landed before the CTA ends (the newest phase of each barrier)
+    }
+    // every copy issued has landed before the CTA ends (the newest phase of each barrier; after
+    // an abort a copy that was never issued waits out its bound)
+    if (lane == 0) {
       if (i > 0) mbar_wait(smem_u32(&s.qfull), (i - 1) & 1, s, p.err, false);
-      for (int k = max(t - kPStages, 0); k < t; ++k) {
+      for (int k = max(t - kPStages, 0); k < t + (ok ? 0 : 1); ++k) {
         mbar_wait(smem_u32(&s.kfull[k & 1]), (k >> 1) & 1, s, p.err, false);
         mbar_wait(smem_u32(&s.vfull[k & 1]), (k >> 1) & 1, s, p.err, false);
       }
