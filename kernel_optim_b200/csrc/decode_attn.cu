@@ -1407,15 +1407,18 @@ __global__ void __launch_bounds__(verify_threads<MT>()) verify_attn_kernel(const
 // lanes 32w ..) takes keys 32w .. 32w + 31 of each 128-key tile for its copy of the rows, with a
 // row maximum shared through shared memory, and writes P for those keys only (zero elsewhere), so
 // copy w's O and l are sums over its quarter of the keys; the four are added at the end. Keys go
-// in tiles of 128 (8 pages) through a 3-deep TMA ring; two S buffers, so the scores of tile j + 1
+// in tiles of 128 (8 pages) through a TMA ring; two S buffers, so the scores of tile j + 1
 // are ready when the softmax of tile j ends. Per tile j the MMA order is O += P(j) V_j, then
 // S(j + 2) into the buffer P(j) came from (the MMAs of one thread execute in issue order, and a
-// commit tracks every MMA issued before it). The running maximum moves only when a row's maximum
+// commit tracks every MMA issued before it). K tiles are read two tiles before their V tiles, so
+// the ring holds 2 K slots and 4 V slots: each copy then starts two to four tiles ahead of its use.
+// The running maximum moves only when a row's maximum
 // grows by more than 2^8. The epilogue writes the output when the pair has one split, else the
 // split's partial (m, l, O), and the split that finishes last merges them.
 //   warps 0-3  softmax, epilogue, merge;   warp 4  TMA producer;   warp 5  tensor memory + MMAs.
 constexpr int kTcKeys = 128;
-constexpr int kTcStages = 3;
+constexpr int kTcKStages = 2;                // K slots (a K tile is done with after its S)
+constexpr int kTcVStages = 4;                // V slots (held until the P V two tiles later)
 constexpr int kTcRows = 32;                  // query rows held (4 T <= 32)
 constexpr int kTcSoft = 4;                   // softmax warps = row copies
 constexpr int kTcThreads = 6 * 32;
@@ -1430,11 +1433,11 @@ constexpr uint32_t kTcIdescO = kTcIdescS | (1u << 16);
 
 struct __align__(1024) TcSmem {
   bf16 q[2][kTcHalf];                        // query tile: [dims half][128 rows][64], swizzled
-  bf16 k[kTcStages][2][kTcHalf];             // key tiles: [dims half][128 keys][64]
-  bf16 v[kTcStages][2][kTcHalf];             // value tiles, same layout (MN-major operand)
+  bf16 k[kTcKStages][2][kTcHalf];            // key tiles: [dims half][128 keys][64]
+  bf16 v[kTcVStages][2][kTcHalf];            // value tiles, same layout (MN-major operand)
   float red[2][kTcSoft][kTcRows];            // per tile parity: each copy's row maxima
   float lsum[kTcSoft][kTcRows];              // each copy's row sums at the end
-  unsigned long long kfull[kTcStages], vfull[kTcStages], kempty[kTcStages], vempty[kTcStages];
+  unsigned long long kfull[kTcKStages], kempty[kTcKStages], vfull[kTcVStages], vempty[kTcVStages];
   unsigned long long sfull[2], pfull[2], pvdone[2], odone, drain;
   unsigned long long redbar[2], epibar, partbar, lastbar;   // among the softmax warps (bounded)
   uint32_t tmem;
@@ -1443,7 +1446,7 @@ struct __align__(1024) TcSmem {
 };
 constexpr size_t kTcSmemBytes = sizeof(TcSmem) + 1024;
 static_assert(kTcSmemBytes <= 232448, "verify (tcgen05) shared memory above the per-CTA limit");
-static_assert(sizeof(float) * kTcSoft * kTcRows * kD <= sizeof(bf16) * kTcStages * 2 * kTcHalf,
+static_assert(sizeof(float) * kTcSoft * kTcRows * kD <= sizeof(bf16) * kTcKStages * 2 * kTcHalf,
               "the copies' outputs do not fit in the key ring");
 
 template <bool PAGED>
@@ -1470,10 +1473,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_c
   const int nt = ceil_div_i(pg1 - pg0, kTcKeys / kPage);   // key tiles
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kTcStages; ++i) {
+    for (int i = 0; i < kTcKStages; ++i) {
       mbar_init(smem_u32(&s.kfull[i]), 1);
-      mbar_init(smem_u32(&s.vfull[i]), 1);
       mbar_init(smem_u32(&s.kempty[i]), 1);
+    }
+    for (int i = 0; i < kTcVStages; ++i) {
+      mbar_init(smem_u32(&s.vfull[i]), 1);
       mbar_init(smem_u32(&s.vempty[i]), 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -1515,7 +1520,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_c
 
   if (warp == 4) {
     // ---- producer warp: K and V tiles of 8 pages, lane i copying page i of the tile (its id read
-    // one tile ahead); lane 0 waits for the slots and sets the byte counts
+    // two tiles ahead, so the id loads are off the path of the copies); lane 0 waits for the slots
+    // and sets the byte counts
     const uint64_t pol = evict_first_policy();
     constexpr int kTP = kTcKeys / kPage;
     const int* bt_row = PAGED ? p.bt + static_cast<long long>(b) * p.bt_stride : nullptr;
@@ -1523,11 +1529,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_c
       const int pg = pg0 + j * kTP + lane;
       return (PAGED && lane < kTP && pg < pg1) ? __ldg(bt_row + pg) : 0;
     };
-    int nxt = nt > 0 ? fetch(0) : 0;
+    int nxt = nt > 0 ? fetch(0) : 0, nxt2 = nt > 1 ? fetch(1) : 0;
     int t = 0;
     bool ok = true;
     for (; t < nt; ++t) {
-      const int st = t % kTcStages, use = t / kTcStages;
       const int npg = min(kTP, pg1 - pg0 - t * kTP);
       int row = 0;
       if (PAGED) {
@@ -1537,13 +1542,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_c
           pid = 0;
         }
         row = (pid * p.nkv + kvh) * kPage;
-        if (t + 1 < nt) nxt = fetch(t + 1);
+        nxt = nxt2;
+        if (t + 2 < nt) nxt2 = fetch(t + 2);
       }
       const int key = (pg0 + t * kTP + lane) * kPage;
       for (int kv = 0; kv < 2; ++kv) {
         unsigned long long* empty = kv == 0 ? s.kempty : s.vempty;
         unsigned long long* full = kv == 0 ? s.kfull : s.vfull;
-        ok = __all_sync(0xffffffffu, t < kTcStages ||
+        const int ns = kv == 0 ? kTcKStages : kTcVStages, st = t % ns, use = t / ns;
+        ok = __all_sync(0xffffffffu, t < ns ||
                         mbar_wait(smem_u32(&empty[st]), (use - 1) & 1, s, p.ws_err, true));
         if (!ok) break;
         if (lane == 0) mbar_arrive_expect_tx(smem_u32(&full[st]), static_cast<uint32_t>(npg) * 2u * kBoxBytes);
@@ -1564,27 +1571,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_c
     // every copy issued has landed (the newest phase of each slot; after an abort the tile whose
     // V was not issued waits out its bound)
     if (lane == 0) {
-      for (int k = max(t + (ok ? 0 : 1) - kTcStages, 0); k < t + (ok ? 0 : 1) && k < nt; ++k) {
-        mbar_wait(smem_u32(&s.kfull[k % kTcStages]), (k / kTcStages) & 1, s, p.ws_err, false);
-        mbar_wait(smem_u32(&s.vfull[k % kTcStages]), (k / kTcStages) & 1, s, p.ws_err, false);
-      }
+      const int te = min(t + (ok ? 0 : 1), nt);
+      for (int k = max(te - kTcKStages, 0); k < te; ++k)
+        mbar_wait(smem_u32(&s.kfull[k % kTcKStages]), (k / kTcKStages) & 1, s, p.ws_err, false);
+      for (int k = max(te - kTcVStages, 0); k < te; ++k)
+        mbar_wait(smem_u32(&s.vfull[k % kTcVStages]), (k / kTcVStages) & 1, s, p.ws_err, false);
     }
   } else if (warp == 5) {
     if (lane == 0) {
       // ---- MMAs: S(0), S(1), then per tile j: O += P(j) V_j, S(j + 2)
       auto issue_s = [&](int j) {
-        const uint32_t qa = smem_u32(&s.q[0][0]), ka = smem_u32(&s.k[j % kTcStages][0][0]);
+        const uint32_t qa = smem_u32(&s.q[0][0]), ka = smem_u32(&s.k[j % kTcKStages][0][0]);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kTcHalfBytes + (kk & 3) * 32;
           umma_bf16(tmem + 128u * (j & 1), sw128_desc(qa + off), sw128_desc(ka + off), kTcIdescS, kk > 0);
         }
         umma_commit(smem_u32(&s.sfull[j & 1]));
-        umma_commit(smem_u32(&s.kempty[j % kTcStages]));
+        umma_commit(smem_u32(&s.kempty[j % kTcKStages]));
       };
       bool ok = true;
       for (int j = 0; j < 2 && j < nt; ++j) {
-        if (!mbar_wait(smem_u32(&s.kfull[j]), 0, s, p.ws_err, true)) {
+        if (!mbar_wait(smem_u32(&s.kfull[j % kTcKStages]), (j / kTcKStages) & 1, s, p.ws_err, true)) {
           ok = false;
           break;
         }
@@ -1593,20 +1601,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_c
       }
       for (int j = 0; ok && j < nt; ++j) {
         if (!mbar_wait(smem_u32(&s.pfull[j & 1]), (j >> 1) & 1, s, p.ws_err, true) ||
-            !mbar_wait(smem_u32(&s.vfull[j % kTcStages]), (j / kTcStages) & 1, s, p.ws_err, true))
+            !mbar_wait(smem_u32(&s.vfull[j % kTcVStages]), (j / kTcVStages) & 1, s, p.ws_err, true))
           break;
         tc_fence_after();
-        const uint32_t va = smem_u32(&s.v[j % kTcStages][0][0]);
+        const uint32_t va = smem_u32(&s.v[j % kTcVStages][0][0]);
 #pragma unroll
         for (int kk = 0; kk < kTcKeys / 16; ++kk)
           umma_bf16_ts(tmem + 256u, tmem + 128u * (j & 1) + 8 * kk,
                        sw128_mn_desc(va + kk * 16 * 128, kTcHalfBytes, 1024), kTcIdescO,
                        (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(smem_u32(&s.pvdone[j & 1]));
-        umma_commit(smem_u32(&s.vempty[j % kTcStages]));
+        umma_commit(smem_u32(&s.vempty[j % kTcVStages]));
         if (j == nt - 1) umma_commit(smem_u32(&s.odone));
         if (j + 2 < nt) {
-          if (!mbar_wait(smem_u32(&s.kfull[(j + 2) % kTcStages]), ((j + 2) / kTcStages) & 1, s, p.ws_err, true))
+          if (!mbar_wait(smem_u32(&s.kfull[(j + 2) % kTcKStages]), ((j + 2) / kTcKStages) & 1, s, p.ws_err, true))
             break;
           tc_fence_after();
           issue_s(j + 2);
@@ -1691,12 +1699,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_c
       }
       if (s0 + (j + 1) * kTcKeys > s1) {
         // V rows past the split's keys may hold anything: zero them so 0 * V stays 0
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.vfull[j % kTcStages]), (j / kTcStages) & 1, s, p.ws_err, true));
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.vfull[j % kTcVStages]), (j / kTcVStages) & 1, s, p.ws_err, true));
         if (!ok) break;
         const int nv = s1 - (s0 + j * kTcKeys);
         for (int i = nv * 16 + 32 * w + lane; i < kTcKeys * 16; i += 32 * kTcSoft) {
           const int rr = i >> 4, part = i & 15;
-          const uint32_t a = smem_u32(&s.v[j % kTcStages][part >> 3][0]) + rr * 128 + ((part & 7) << 4);
+          const uint32_t a = smem_u32(&s.v[j % kTcVStages][part >> 3][0]) + rr * 128 + ((part & 7) << 4);
           asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

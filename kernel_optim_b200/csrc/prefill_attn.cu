@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
 
   if (warp == kPProducer) {
     // ---- TMA producer warp: each item's two query tiles, then its K and V tiles through the
-    // 2-deep ring, lane i copying page i of a tile (its id read one tile ahead) while lane 0 waits
+    // 2-deep ring, lane i copying page i of a tile (its id read two tiles ahead) while lane 0 waits
     // for the slots and sets the byte counts; tiles are counted across items (t), so the ring
     // never drains between items. Queries are read once (evict first); K/V tiles are read again by
     // the other head pair of the kv head and the later query tiles of the sequence (evict last).
@@ -158,7 +158,23 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
       return (PAGED && lane < kTilePages && pg < npg_all)
                  ? __ldg(p.bt + static_cast<long long>(b) * p.bt_stride + pg) : 0;
     };
-    int nxt = static_cast<int>(blockIdx.x) < p.items ? fetch(item_of(p, blockIdx.x).b, 0) : 0;
+    // the (sequence, tile) after (b, j) in this CTA's order, or b = -1 past its last item
+    auto after = [&](int w, int j, int& b2, int& j2, int& w2) {
+      const Item it = item_of(p, w);
+      if (j + 1 < it.nt) {
+        b2 = it.b; j2 = j + 1; w2 = w;
+      } else if (w + G < p.items) {
+        b2 = item_of(p, w + G).b; j2 = 0; w2 = w + G;
+      } else {
+        b2 = -1; j2 = 0; w2 = w;
+      }
+    };
+    int nxt = 0, nxt2 = 0, fb2 = -1, fj2 = 0, fw2 = 0;   // ids of the next two tiles; where nxt2 is
+    if (static_cast<int>(blockIdx.x) < p.items) {
+      nxt = fetch(item_of(p, blockIdx.x).b, 0);
+      after(blockIdx.x, 0, fb2, fj2, fw2);
+      if (fb2 >= 0) nxt2 = fetch(fb2, fj2);
+    }
     int t = 0, i = 0;
     bool ok = true;
     for (int w = blockIdx.x; ok && w < p.items; w += G, ++i) {
@@ -182,8 +198,11 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
             pid = 0;
           }
           row = (pid * p.nkv + it.kvh) * kPPage;
-          if (j + 1 < it.nt) nxt = fetch(it.b, j + 1);
-          else if (w + G < p.items) nxt = fetch(item_of(p, w + G).b, 0);
+          nxt = nxt2;
+          if (fb2 >= 0) {   // the ids of the tile after the next one
+            after(fw2, fj2, fb2, fj2, fw2);
+            if (fb2 >= 0) nxt2 = fetch(fb2, fj2);
+          }
         }
         for (int kv = 0; kv < 2; ++kv) {
           unsigned long long* empty = kv == 0 ? s.kempty : s.vempty;
