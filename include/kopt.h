@@ -93,10 +93,11 @@ typedef struct kopt_plan {
  * CTAs take the SMs that the kernel before it on the stream leaves, and lay out the work split and
  * issue the first K/V page copies before waiting for that kernel to complete. Set it only when the
  * kernel right before the call on its stream writes none of pos, the block table and the cache
- * rows [0, pos[b]) of this call (the fused entry points; the unfused one waits before reading
- * anything): e.g. the QKV projection GEMM of a decode step, or another decode-attention call for a
- * different layer. qkv, the norm weights, the RoPE tables, the workspace and the outputs are only
- * touched after the wait. */
+ * rows [0, pos[b]) of this call (the fused entry points, and kopt_decode_attn for T > 4; the
+ * unfused T = 1 kernel waits before reading anything, and T = 2 .. 4 launches without it): e.g.
+ * the QKV projection GEMM of a decode step, the kopt_qk_norm_rope before a verify step, or another
+ * decode-attention call for a different layer. q / qkv, the norm weights, the RoPE tables, the rows
+ * from pos[b] on, the workspace and the outputs are only touched after the wait. */
 #define KOPT_PLAN_OVERLAP_PREV 1
 
 /* Plan a decode-attention launch: B sequences of at most max_len keys, T query tokens each

@@ -1414,7 +1414,10 @@ __global__ void __launch_bounds__(verify_threads<MT>()) verify_attn_kernel(const
 // the ring holds 2 K slots and 4 V slots: each copy then starts two to four tiles ahead of its use.
 // The running maximum moves only when a row's maximum
 // grows by more than 2^8. The epilogue writes the output when the pair has one split, else the
-// split's partial (m, l, O), and the split that finishes last merges them.
+// split's partial (m, l, O), and the split that finishes last merges them. Launched with
+// programmatic dependent launch (KOPT_PLAN_OVERLAP_PREV), the producer copies the tiles whose keys
+// are all below pos before it waits for the previous kernel; the query rows, the rows at pos ..
+// pos + T - 1 and the outputs are only touched after the wait.
 //   warps 0-3  softmax, epilogue, merge;   warp 4  TMA producer;   warp 5  tensor memory + MMAs.
 constexpr int kTcKeys = 128;
 constexpr int kTcKStages = 2;                // K slots (a K tile is done with after its S)
@@ -1440,6 +1443,7 @@ struct __align__(1024) TcSmem {
   unsigned long long kfull[kTcKStages], kempty[kTcKStages], vfull[kTcVStages], vempty[kTcVStages];
   unsigned long long sfull[2], pfull[2], pvdone[2], odone, drain;
   unsigned long long redbar[2], epibar, partbar, lastbar;   // among the softmax warps (bounded)
+  unsigned long long qready;                                // the query tile is in
   uint32_t tmem;
   int last;
   volatile int abort;
@@ -1493,6 +1497,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_c
     mbar_init(smem_u32(&s.epibar), 32 * kTcSoft);
     mbar_init(smem_u32(&s.partbar), 32 * kTcSoft);
     mbar_init(smem_u32(&s.lastbar), 1);
+    mbar_init(smem_u32(&s.qready), 32 * kTcSoft);
     s.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1500,23 +1505,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_c
     tmem_alloc(smem_u32(&s.tmem), kTcCols);
     tmem_relinquish();
   }
-  // the query tile in the 128-byte-swizzled K-major layout (16-byte chunk c of row r at
-  // c ^ (r % 8)): row r holds query row r % 32 (zero past 4 T)
-  for (int i = threadIdx.x; i < 128 * 16; i += kTcThreads) {
-    const int r = i >> 4, c = i & 15;              // row, 16-byte chunk of its 256 bytes
-    const int qr = r % kTcRows, t = qr / kGroup, g = qr % kGroup;
-    uint4 val = make_uint4(0u, 0u, 0u, 0u);
-    if (qr < kGroup * T)
-      val = *reinterpret_cast<const uint4*>(p.q + (static_cast<long long>(b) * T + t) * nq * kD +
-                                            (kvh * kGroup + g) * kD + c * 8);
-    const int h = c >> 3, cc = c & 7;
-    *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&s.q[h][0]) + r * 128 + ((cc ^ (r & 7)) << 4)) = val;
-  }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the MMA reads it
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem;
+  if (warp < kTcSoft) {
+    griddep_wait();   // q and the rows at pos .. are the previous kernel's
+    // the query tile in the 128-byte-swizzled K-major layout (16-byte chunk c of row r at
+    // c ^ (r % 8)): row r holds query row r % 32 (zero past 4 T)
+    for (int i = threadIdx.x; i < 128 * 16; i += 32 * kTcSoft) {
+      const int r = i >> 4, c = i & 15;              // row, 16-byte chunk of its 256 bytes
+      const int qr = r % kTcRows, t = qr / kGroup, g = qr % kGroup;
+      uint4 val = make_uint4(0u, 0u, 0u, 0u);
+      if (qr < kGroup * T)
+        val = *reinterpret_cast<const uint4*>(p.q + (static_cast<long long>(b) * T + t) * nq * kD +
+                                              (kvh * kGroup + g) * kD + c * 8);
+      const int h = c >> 3, cc = c & 7;
+      *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&s.q[h][0]) + r * 128 + ((cc ^ (r & 7)) << 4)) = val;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the MMA reads it
+    mbar_arrive(smem_u32(&s.qready));
+  }
+  griddep_launch_dependents();
 
   if (warp == 4) {
     // ---- producer warp: K and V tiles of 8 pages, lane i copying page i of the tile (its id read
@@ -1531,8 +1541,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_c
     };
     int nxt = nt > 0 ? fetch(0) : 0, nxt2 = nt > 1 ? fetch(1) : 0;
     int t = 0;
-    bool ok = true;
+    bool ok = true, waited = false;
     for (; t < nt; ++t) {
+      if (!waited && min(s1, s0 + (t + 1) * kTcKeys) > p0) {   // rows at pos and past: after the wait
+        griddep_wait();
+        waited = true;
+      }
       const int npg = min(kTP, pg1 - pg0 - t * kTP);
       int row = 0;
       if (PAGED) {
@@ -1590,8 +1604,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) verify_tc_kernel(const __grid_c
         umma_commit(smem_u32(&s.sfull[j & 1]));
         umma_commit(smem_u32(&s.kempty[j % kTcKStages]));
       };
-      bool ok = true;
-      for (int j = 0; j < 2 && j < nt; ++j) {
+      bool ok = nt == 0 || mbar_wait(smem_u32(&s.qready), 0, s, p.ws_err, true);
+      for (int j = 0; ok && j < 2 && j < nt; ++j) {
         if (!mbar_wait(smem_u32(&s.kfull[j % kTcKStages]), (j / kTcKStages) & 1, s, p.ws_err, true)) {
           ok = false;
           break;
@@ -2058,8 +2072,21 @@ int launch_verify(const kopt_plan* plan, Params& p, void* stream) {
   if (verify_on_tc(plan->T)) {
     rc = verify_tc_occupancy<PAGED>(plan->device, nullptr);
     if (rc) return rc;
-    verify_tc_kernel<PAGED><<<plan->grid, kTcThreads, kTcSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
-    return cudaGetLastError() == cudaSuccess ? KOPT_OK : KOPT_ERR_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan->grid);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = kTcSmemBytes;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (plan->flags & KOPT_PLAN_OVERLAP_PREV) ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, verify_tc_kernel<PAGED>, p) != cudaSuccess) {
+      cudaGetLastError();
+      return KOPT_ERR_CUDA;
+    }
+    return KOPT_OK;
   }
   return verify_tiles(plan->T) == 1 ? launch_verify_t<PAGED, 1>(plan, p, stream)
                                     : launch_verify_t<PAGED, 2>(plan, p, stream);
