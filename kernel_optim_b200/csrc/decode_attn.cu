@@ -127,6 +127,7 @@ struct __align__(1024) Smem {
   int late;                             // the last kLateCtas pieces are shortened (see chunk_range)
   int parts;                            // > 0: every pair has npg_eq pages and is cut into this
   int npg_eq;                           //   many pieces of its own (see compute_plan)
+  int group;                            // > 0: pieces of `group` whole pairs of npg_eq pages
   volatile int nclaimed;                // ring entries 0 .. nclaimed-1 are valid
   int npend;                            // partial units written, not yet released
   int pend[kMaxPend][5];                // their (pair, first chunk, chunks, sequence, kv head)
@@ -241,14 +242,26 @@ __device__ void compute_plan(const Params& p, Smem& s, int lane) {
     // 45.6 us; c4, k = 4: 347 -> 318 us). Only when the CTAs so used are >= 80% of the grid, a
     // part has at least one page, and the whole line is split statically; the CTAs beyond
     // pairs * k (the last ones, which start last under programmatic launch) get no pages.
+    // More pairs than CTAs, all of one length: pieces of m whole pairs instead (m the smallest
+    // that fits the grid and divides the pair count), under the same 80% rule, so that no pair is
+    // split and nothing is merged.
     s.parts = 0;
+    s.group = 0;
     s.npg_eq = nmin;
     const int pairs = p.B * p.nkv;
-    if (nmin == nmax && pairs <= G && P == carry) {
-      const int k = min(G / pairs, nmin);
-      if (5 * pairs * k >= 4 * G) {
-        s.parts = k;
-        s.late = 0;
+    if (nmin == nmax && P == carry) {
+      if (pairs <= G) {
+        const int k = min(G / pairs, nmin);
+        if (5 * pairs * k >= 4 * G) {
+          s.parts = k;
+          s.late = 0;
+        }
+      } else {
+        const int m = ceil_div_i(pairs, G);
+        if (pairs % m == 0 && 5 * (pairs / m) >= 4 * G) {
+          s.group = m;
+          s.late = 0;
+        }
       }
     }
   }
@@ -281,6 +294,12 @@ __device__ __forceinline__ void chunk_range(const Smem& s, int k, int& x0, int& 
     }
     return;
   }
+  if (s.group > 0) {   // pairs [k m, (k + 1) m), or nothing past the last pair
+    const long long w = static_cast<long long>(s.group) * s.npg_eq;
+    x0 = static_cast<int>(min(static_cast<long long>(k) * w, static_cast<long long>(s.total_pages)));
+    x1 = static_cast<int>(min(static_cast<long long>(k + 1) * w, static_cast<long long>(s.total_pages)));
+    return;
+  }
   if (k < G && s.late) {
     const int G4 = G - kLateCtas, F = late_front(s), q = s.static_pages / G;
     if (k < G4) {
@@ -309,6 +328,7 @@ __device__ __forceinline__ int chunk_of(const Smem& s, int y) {
     return q * s.parts +
            static_cast<int>((static_cast<long long>(off + 1) * s.parts - 1) / s.npg_eq);
   }
+  if (s.group > 0) return y / (s.npg_eq * s.group);   // the piece of the pair holding page y
   if (y < P && s.late) {
     const int G4 = static_cast<int>(G) - kLateCtas, F = late_front(s);
     const int q = s.static_pages / static_cast<int>(G);

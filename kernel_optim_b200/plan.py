@@ -18,7 +18,9 @@ without a GPU:
 * when every pair has the same page count np, there are no more pairs than CTAs and the whole line
   is static, each pair is cut into k = min(grid // pairs, np) parts of its own instead (piece c =
   part c % k of pair c // k, [floor(i np / k), floor((i + 1) np / k)) within it), provided
-  pairs * k >= 0.8 grid; the CTAs past pairs * k get nothing and the late-start allowance is off.
+  pairs * k >= 0.8 grid; the CTAs past pairs * k get nothing and the late-start allowance is off;
+  with more pairs than CTAs, piece c is pairs [c m, (c + 1) m) instead, m = ceil(pairs / grid)
+  when it divides the pair count and pairs / m >= 0.8 grid (no pair split, nothing merged).
 """
 
 from __future__ import annotations
@@ -60,6 +62,7 @@ class Plan:
     late: bool = False
     parts: int = 0       # > 0: pair-aligned pieces, `parts` per pair of npg_eq pages
     npg_eq: int = 0
+    group: int = 0       # > 0: pieces of `group` whole pairs of npg_eq pages
 
     def _late_front(self) -> int:
         q = self.static_pages // self.grid
@@ -73,6 +76,9 @@ class Plan:
             if q * np_ >= self.total_pages:
                 return self.total_pages, self.total_pages
             return q * np_ + i * np_ // self.parts, q * np_ + (i + 1) * np_ // self.parts
+        if self.group:
+            w = self.group * self.npg_eq
+            return min(k * w, self.total_pages), min((k + 1) * w, self.total_pages)
         if k < G and self.late:
             G4, F, q = G - LATE_CTAS, self._late_front(), P // G
             if k < G4:
@@ -89,6 +95,8 @@ class Plan:
         if self.parts:
             q, off = divmod(y, self.npg_eq)
             return q * self.parts + ((off + 1) * self.parts - 1) // self.npg_eq
+        if self.group:
+            return y // (self.npg_eq * self.group)
         if y < P and self.late:
             G4, F, q = G - LATE_CTAS, self._late_front(), P // G
             if y < F:
@@ -113,13 +121,18 @@ def plan(lengths, nkv: int, grid: int, fused: bool, static_pct: int = STATIC_PCT
     if P < grid:
         P = 0
     late = skew and grid > 2 * LATE_CTAS and P // grid >= 4 * LATE_PAGES[0]
-    parts, pairs = 0, len(lengths) * nkv
-    if min(npages) == max(npages) and pairs <= grid and P == T:
-        k = min(grid // pairs, npages[0])
-        if 5 * pairs * k >= 4 * grid:
-            parts, late = k, False
+    parts, group, pairs = 0, 0, len(lengths) * nkv
+    if min(npages) == max(npages) and P == T:
+        if pairs <= grid:
+            k = min(grid // pairs, npages[0])
+            if 5 * pairs * k >= 4 * grid:
+                parts, late = k, False
+        else:
+            m = -(-pairs // grid)
+            if pairs % m == 0 and 5 * (pairs // m) >= 4 * grid:
+                group, late = m, False
     return Plan(npages, pstart, T, P, grid + -(-(T - P) // CHUNK_PAGES), grid, late, parts,
-                npages[0])
+                npages[0], group)
 
 
 def units_of_chunk(pl: Plan, lengths, nkv: int, fused: bool, k: int) -> list[Unit]:

@@ -20,10 +20,14 @@ def check_plan(lengths, nkv, grid, fused, max_len=None, static_pct=100, skew=Fal
     # pairs * parts in the pair-aligned layout
     for k in range(pl.total_chunks):
         x0, x1 = pl.chunk_range(k)
-        assert x1 > x0 or (k < grid and pl.static_pages == 0) or (pl.parts and k >= B * nkv * pl.parts)
+        assert (x1 > x0 or (k < grid and pl.static_pages == 0) or (pl.parts and k >= B * nkv * pl.parts)
+                or (pl.group and k * pl.group >= B * nkv))
     if pl.parts:   # one unit per CTA, each pair cut into exactly `parts` pieces of its own
         assert all(sum(1 for u in us if u.chunk == k) <= 1 for k in range(grid))
         assert all(u.n == pl.parts for u in us)
+    if pl.group:   # whole pairs, `group` of them per CTA: nothing split, nothing merged
+        assert all(u.n == 1 for u in us)
+        assert all(sum(1 for u in us if u.chunk == k) <= pl.group for k in range(grid))
     by_pair = defaultdict(list)
     for u in us:
         by_pair[u.q].append(u)
@@ -90,6 +94,18 @@ def test_late_start_allowance():
     assert lens[-4:] == [q - d for d in reversed(LATE_PAGES)]
     assert min(lens[:-4]) >= q
     check_plan([5, 130, 77], 8, 148, True, skew=True)      # too short: no allowance
+
+
+def test_whole_pair_groups():
+    """Equal lengths, more pairs than CTAs: pieces of m whole pairs each (c5's decode step:
+    32 x 8 = 256 pairs on 148 CTAs -> 128 pieces of 2 pairs), only when m divides the pair count
+    and >= 80% of the grid is used."""
+    pl, us = check_plan([1153] * 32, 8, 148, True)
+    assert pl.group == 2 and pl.parts == 0 and not pl.late and len(us) == 256
+    assert check_plan([1153] * 37, 8, 148, True)[0].group == 2     # 296 pairs: 148 pieces
+    assert check_plan([1153] * 19, 8, 148, True)[0].group == 0     # 152 pairs: m = 2 leaves 76
+    assert check_plan([1153] * 40, 8, 148, True)[0].group == 0     # 320 pairs: 3 does not divide
+    assert check_plan([1153, 1000] * 16, 8, 148, True)[0].group == 0   # unequal lengths
 
 
 def test_pair_aligned_pieces():
