@@ -415,26 +415,25 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
       ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.odone[x]), i & 1, s, p.err, true));
       if (!ok) break;
       tc_fence_after();
-      const float inv = 1.0f / l;
-      bf16* dst = p.out + (static_cast<long long>(it.b) * p.S + row) * p.nq * kPD + (it.h0 + x) * kPD;
-#pragma unroll
-      for (int c = 0; c < kPD; c += 32) {
-        float o[32];
-        tmem_ld32(lrow + col_o(x) + c, o);
-        if (row < p.S) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 u;
-            u.x = pack_bf16(o[e] * inv, o[e + 1] * inv);
-            u.y = pack_bf16(o[e + 2] * inv, o[e + 3] * inv);
-            u.z = pack_bf16(o[e + 4] * inv, o[e + 5] * inv);
-            u.w = pack_bf16(o[e + 6] * inv, o[e + 7] * inv);
-            *reinterpret_cast<uint4*>(dst + c + e) = u;
-          }
-        }
-      }
+      // the whole row in one load; O_x is handed back before the stores, so the next item's
+      // first P V may start while they go out
+      float o[kPD];
+      tmem_ld128(lrow + col_o(x), o);
       tc_fence_before();
       mbar_arrive(smem_u32(&s.oempty[x]));
+      const float inv = 1.0f / l;
+      bf16* dst = p.out + (static_cast<long long>(it.b) * p.S + row) * p.nq * kPD + (it.h0 + x) * kPD;
+      if (row < p.S) {
+#pragma unroll
+        for (int e = 0; e < kPD; e += 8) {
+          uint4 u;
+          u.x = pack_bf16(o[e] * inv, o[e + 1] * inv);
+          u.y = pack_bf16(o[e + 2] * inv, o[e + 3] * inv);
+          u.z = pack_bf16(o[e + 4] * inv, o[e + 5] * inv);
+          u.w = pack_bf16(o[e + 6] * inv, o[e + 7] * inv);
+          *reinterpret_cast<uint4*>(dst + e) = u;
+        }
+      }
     }
   }
   tc_fence_before();
