@@ -332,7 +332,8 @@ def run_ours(args):
                 "frac": round(achieved / peak, 4), "frac_of_8TBs_nominal": round(achieved / 8000, 4),
                 "traffic": traffic, "peak_source": peak_src,
                 "kernel": ("decode_attn_kernel<PAGED=1,FUSED=1>" if case.fused else
-                           f"verify_attn_kernel<PAGED=1> (T={case.T})"),
+                           (f"verify_tc_kernel<PAGED=1> (T={case.T}, tcgen05)" if case.T > 4
+                            else f"verify_attn_kernel<PAGED=1> (T={case.T})")),
                 "kernel_us": round(kern_ms * 1e3, 2),
                 "algorithmic_bytes_per_launch": bytes_rank}
 
