@@ -109,6 +109,20 @@ def test_lengths_and_split_plans(target_ctas):
         within(got[b], ref[b], f"L={L} target_ctas={target_ctas}")
 
 
+@pytest.mark.parametrize("B", [32, 37])
+def test_whole_pair_pieces_when_pairs_outnumber_ctas(B):
+    """Equal lengths and more (sequence, kv head) pairs than CTAs (c5's decode step: 256 pairs):
+    each CTA takes whole pairs, nothing is split or merged; B = 37 fills all 148 CTAs."""
+    g = torch.Generator().manual_seed(12)
+    L = 1153
+    q = torch.randn(B, NQ, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, NKV, L, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, NKV, L, D, generator=g).to(torch.bfloat16)
+    ref = decode_attn_fp32(q, k, v, [L] * B)
+    got = run_contiguous(q, k, v, [L] * B)
+    within(got, ref, f"B={B} L={L}")
+
+
 def test_repeated_calls_bitwise_identical():
     """The split counters are reset by the merging CTA, so replays see a clean workspace."""
     g = torch.Generator().manual_seed(12)
