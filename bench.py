@@ -925,7 +925,8 @@ def run_engine(args):
         "data": "synthetic: random-init Qwen3-4B (std 0.02, seed 0), uniform random prompt ids",
         "config": {"workload": "c5 engine generate", "B": B, "prompt": S, "new_tokens": N,
                    "overlap_prev": not args.no_overlap,
-                   "projections": "cuBLAS" if eng.gemv is None else "kopt_gemv (fused epilogues)",
+                   "projections": "cuBLAS" if eng.gemv is None else
+                                  "kopt_gemv (fused epilogues) for qkv, gate|up, down, lm_head; cuBLAS o_proj",
                    "prefill": args.prefill,
                    "parallelism": (f"kv-head shard x{world}, all-gather fused into the attention "
                                    "kernel (NVLink stores)" if world > 1 else "single GPU")},
