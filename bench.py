@@ -33,7 +33,6 @@ from __future__ import annotations
 
 import argparse
 import ctypes
-import datetime
 import json
 import os
 import statistics
@@ -95,11 +94,13 @@ def dist_env():
 
 
 def init_dist(world, local):
+    """NCCL group with a bounded timeout on every collective (kernel_optim_b200.comm)."""
     if world > 1:
         import torch.distributed as dist
+
+        from kernel_optim_b200.comm import init_group
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        init_group("nccl", timeout_s=120, device=torch.device("cuda", local))
         return dist
     return None
 
@@ -237,6 +238,7 @@ class StepLauncher:
 
 
 def run_ours(args):
+    from kernel_optim_b200.comm import collective
     from kernel_optim_b200.paged import PagedDecodeAttention
     from kernel_optim_b200.workloads import build_case
     world, rank, local = dist_env()
@@ -269,7 +271,8 @@ def run_ours(args):
     def step(i):
         step_launch(i)
         if nccl_gather:
-            dist.all_gather_into_tensor(gathered.view(-1, gathered.shape[-1]), out)
+            collective(dist.all_gather_into_tensor, gathered.view(-1, gathered.shape[-1]), out,
+                       what="all-gather of the head outputs")
 
     for i in range(args.warmup):
         step(i)
@@ -389,6 +392,7 @@ def run_strong_c4(args, dist, n, rank, dev):
     all-gathered inside the kernel over NVLink (N > 1). Back-to-back calls over two layer caches,
     CUDA events on the launching stream, max over ranks; value = the job's algorithmic bytes
     (2 GiB of K/V per call, whatever N) over that time."""
+    from kernel_optim_b200.comm import collective
     from kernel_optim_b200.paged import PagedDecodeAttention
     from kernel_optim_b200.workloads import build_case
     layers = 2
@@ -478,7 +482,8 @@ def run_e2e(args, case, attn, out, gathered, pg, dist, bytes_job):
             compute.wait_event(out_free[1 - j])
         launchers[j](i)
         if gath is not None:
-            dist.all_gather_into_tensor(gath[j].view(-1, gath[j].shape[-1]), outs[j])
+            collective(dist.all_gather_into_tensor, gath[j].view(-1, gath[j].shape[-1]), outs[j],
+                       what="all-gather of the head outputs")
         res = gath[j] if gath is not None else launchers[j].result(outs[j])
         done[j].record(compute)
         with torch.cuda.stream(d2h):

@@ -169,7 +169,9 @@ KOPT_API int kopt_decode_attn_fused(const kopt_plan* plan, const void* qkv, cons
  * mappings), at column offset r * nq_local * 128. When all its CTAs are done, the last one raises
  * flags[w][r] = epoch + 1 on every rank w, then waits until every rank's flag in its own array has
  * reached epoch + 1 (bounded by wait_ns, 1 s by default; KOPT_DEV_ERR_TIMEOUT in the workspace
- * error word on expiry, after which the call still completes and its own rows are in place) and
+ * error word on expiry, after which the call still completes and its own rows are in place; while
+ * that bit stays unread in the error word, later calls through the same workspace raise their
+ * flags but do not wait) and
  * advances the epoch: once the call completes on a stream, the gathered rows of all ranks are in
  * this rank's buffer. Every rank must make the same calls in the same order. This takes the place
  * of a separate all-gather (NCCL) of the head outputs between attention and o_proj, which the

@@ -406,7 +406,10 @@ __device__ __forceinline__ long long row_offset(const Params& p, int b, int kvh,
 // other CTAs ordered before their counter increment), then wait until every rank's flag for this
 // call is up here (acquire; bounded by p.wait_ns, KOPT_DEV_ERR_TIMEOUT on expiry), so that this
 // kernel's completion means the whole gathered row block has landed in local memory. The peers are
-// other GPUs running the same kernel; nothing here waits on work of this GPU.
+// other GPUs running the same kernel; nothing here waits on work of this GPU. When the error word
+// already holds KOPT_DEV_ERR_TIMEOUT (an earlier call through this workspace gave up, and the host
+// has not read the word since), the peers are taken as gone and the call does not wait again: a
+// decode step after a peer's failure costs one bound, not one per layer.
 __device__ __noinline__ void gather_signal_and_wait(const Params& p) {
   __threadfence_system();
   const int e = *p.epoch + 1;
@@ -414,8 +417,9 @@ __device__ __noinline__ void gather_signal_and_wait(const Params& p) {
     asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p.flag_peer[w] + p.rank), "r"(e)
                  : "memory");
   const int* mine = p.flag_peer[p.rank];
+  const bool gone = (*reinterpret_cast<volatile int*>(p.ws_err) & KOPT_DEV_ERR_TIMEOUT) != 0;
   const unsigned long long t0 = globaltimer();
-  for (int w = 0; w < p.world; ++w) {
+  for (int w = 0; !gone && w < p.world; ++w) {
     while (true) {
       int f;
       asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(f) : "l"(mine + w) : "memory");

@@ -13,24 +13,28 @@ What changes is the decode step (engine.py:313-341, 388-401): the per-layer ``qk
 is captured once per shape in a CUDA graph and replayed, pipelined one step ahead of the host as in
 engine.py:509-533. Around it the layer runs as engine.py:325-340 does, on the tcgen05 skinny GEMM
 (``Gemv``, engine.py:259-263) against fused weights (q/k/v; gate and up): each RMSNorm a row kernel
-(``add_rms_norm``), the residual adds, SwiGLU and the LM head's greedy pick as epilogues, all in
-Transformers' cast order (batches above 64 rows: cuBLAS GEMMs, ``add_rms_norm`` and
-``silu_mul``). Prefill (``prefill="native"``) runs the same row kernels over the whole prompt with
-cuBLAS GEMMs and torch SDPA for the causal attention, the prologue kernel writing the prompt's K/V,
-which are copied into the pages; ``prefill="transformers"`` uses the native Transformers forward.
+(``add_rms_norm``), the down_proj residual add, SwiGLU and the LM head's greedy pick as epilogues,
+o_proj a cuBLAS GEMM whose residual add the next norm takes, all in Transformers' cast order
+(batches above 64 rows: cuBLAS GEMMs, ``add_rms_norm`` and ``silu_mul``). Prefill
+(``prefill="native"``) runs the same row kernels over the whole prompt with cuBLAS GEMMs; the
+prologue kernel writes the prompt's K/V into the pages and the tcgen05 prefill kernel attends from
+there (sharded: torch SDPA over all heads); ``prefill="transformers"`` uses the native
+Transformers forward.
 
 Multi-GPU (``group`` = a torch.distributed process group of G ranks, one GPU each, one node): rank r
 keeps kv heads [r*nkv/G, (r+1)*nkv/G) — their QKV weight rows and their pages — and runs attention
 for them with the all-gather fused into the kernel (kernel_optim_b200/gather.py): every rank's rows
 land in every rank's [B, nq*128] buffer over NVLink, which feeds o_proj directly; everything after
-attention is replicated, so every rank emits the same tokens.
+attention is replicated, so every rank emits the same tokens. Failures are handled on the host
+between steps (comm.PeerWatch in ``generate``) and by the kernel's bounded flag wait.
 """
 
 from __future__ import annotations
 
 import torch
 
-from ._lib import KoptError
+from ._lib import KoptError, dev_error_text
+from .comm import PeerFailure, PeerWatch
 from .paged import PAGE, PagedDecodeAttention, PagedKVCache, qk_norm_rope_paged
 from .fused import add_rms_norm, qk_norm_rope, silu_mul
 from .prefill import prefill_attention
@@ -77,6 +81,7 @@ class Engine:
         self.use_gemv = gemv
         self.world = 1 if group is None else torch.distributed.get_world_size(group)
         self.rank = 0 if group is None else torch.distributed.get_rank(group)
+        self.watch = PeerWatch(group) if self.world > 1 else None
         h0, _ = head_range(self.nkv, self.rank, self.world)
         self.nkv_l = self.nkv // self.world
         self.nq_l = 4 * self.nkv_l
@@ -164,6 +169,9 @@ class Engine:
         if self.world > 1:
             self.pg = PeerGather(B, self.nq * self.d, dev, self.group)
         self.pin_ids = torch.empty(N + 1, B, dtype=torch.int64, pin_memory=True)
+        # sharded: the attention's error word after each step, read back beside the token ids
+        self.pin_err = (torch.zeros(N + 1, dtype=torch.int32, pin_memory=True)
+                        if self.watch is not None else None)
         self.events = [torch.cuda.Event() for _ in range(N + 1)]
         self.graph = self._capture(self._step)
         self._shape = (B, S, N)
@@ -308,6 +316,25 @@ class Engine:
     # ---------------------------------------------------------------------- generate
     @torch.inference_mode()
     def generate(self, input_ids: list[list[int]], max_new_tokens: int):
+        """Greedy tokens, one list of B ids per step. Sharded, every rank checks the group's
+        failure record and heartbeats (comm.PeerWatch) before each decode step, records its own
+        failure there when it raises, and at the end reads the attention's device error word
+        (a peer that stopped mid-step shows as KOPT_DEV_ERR_TIMEOUT of the fused gather)."""
+        if self.watch is None:
+            yield from self._generate(input_ids, max_new_tokens)
+            return
+        try:
+            self.watch.check()
+            yield from self._generate(input_ids, max_new_tokens)
+            bits = self.attn.read_error()
+            if bits:
+                raise KoptError(f"rank {self.rank}: device error bits {bits} ({dev_error_text(bits)})")
+        except (Exception, KeyboardInterrupt) as e:
+            if not isinstance(e, PeerFailure):
+                self.watch.fail(f"{type(e).__name__}: {e}")
+            raise
+
+    def _generate(self, input_ids: list[list[int]], max_new_tokens: int):
         N = max_new_tokens
         if N <= 0:
             return
@@ -322,11 +349,20 @@ class Engine:
         ids_h[0].copy_(self.ids, non_blocking=True)
         ev[0].record(stream)
         # queue the next step before waiting on the current one (engine.py:509-533)
+        err_h = self.pin_err
         for j in range(1, N):
+            if self.watch is not None:
+                self.watch.check()
             self.graph.replay()
             ids_h[j].copy_(self.ids, non_blocking=True)
+            if err_h is not None:
+                err_h[j:j + 1].copy_(self.attn.ws[:4].view(torch.int32), non_blocking=True)
             ev[j].record(stream)
             ev[j - 1].synchronize()
+            if err_h is not None and int(err_h[j - 1]):
+                bits = int(err_h[j - 1])
+                raise KoptError(f"rank {self.rank}: device error bits {bits} ({dev_error_text(bits)}) "
+                                f"by decode step {j - 1}")
             yield ids_h[j - 1].tolist()
         ev[N - 1].synchronize()
         yield ids_h[N - 1].tolist()

@@ -11,6 +11,8 @@ from __future__ import annotations
 
 import torch
 
+from .comm import collective
+
 
 def head_range(nkv: int, rank: int, world: int) -> tuple[int, int]:
     """kv heads [h0, h1) of `rank`."""
@@ -29,9 +31,11 @@ def shard_qkv_weight(q_w: torch.Tensor, k_w: torch.Tensor, v_w: torch.Tensor, nk
                      0).contiguous()
 
 
-def gather_heads(local: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
+def gather_heads(local: torch.Tensor, out: torch.Tensor, group=None, watch=None) -> torch.Tensor:
     """All-gather [B, heads_l*d] from every rank into `out` [G, B, heads_l*d]; returns the
-    [B, G*heads_l*d] head-ordered view."""
+    [B, G*heads_l*d] head-ordered view. A failed or timed-out all-gather aborts the group and
+    raises comm.CollectiveError (recorded in `watch`, a comm.PeerWatch, when given)."""
     G, B, W = out.shape
-    torch.distributed.all_gather_into_tensor(out.view(G * B, W), local.contiguous(), group=group)
+    collective(torch.distributed.all_gather_into_tensor, out.view(G * B, W), local.contiguous(),
+               group=group, watch=watch, what="all-gather of the head outputs")
     return out.permute(1, 0, 2).reshape(B, G * W)

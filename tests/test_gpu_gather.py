@@ -172,8 +172,10 @@ def test_gather_flag_wait_runs_out_on_one_gpu():
     world-2 descriptor whose "peer" buffers are a second local allocation that no kernel ever
     signals. The call must complete, set KOPT_DEV_ERR_TIMEOUT (and nothing else), still store this
     rank's rows into both buffers and raise its flag in both flag arrays; after the error word is
-    read and cleared, a world-1 call on the same workspace is correct again. Nothing hangs: the
-    wait is bounded at 5 ms here (the descriptor's wait_ns)."""
+    read and cleared, a world-1 call on the same workspace is correct again. While the timeout bit
+    is still unread, a further call (bound 1 s) raises its flags but does not wait: it ends in far
+    less than its bound. Nothing hangs: the waits are bounded at 5 ms and 1 s (the descriptor's
+    wait_ns)."""
     import ctypes
 
     from kernel_optim_b200 import _lib
@@ -210,11 +212,17 @@ def test_gather_flag_wait_runs_out_on_one_gpu():
 
     call(2, 5_000_000)
     torch.cuda.synchronize(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record()
+    call(2, 1_000_000_000)   # the unread timeout bit: flags raised, no second wait
+    ev[1].record()
+    torch.cuda.synchronize(dev)
+    assert ev[0].elapsed_time(ev[1]) < 100.0, f"{ev[0].elapsed_time(ev[1]):.1f} ms"
     assert attn.read_error() == _lib.DEV_ERR_TIMEOUT   # read_error also clears the word
     for w in range(2):
         assert torch.equal(outs[w][:, : nq_l * 128], plain), f"rows missing in buffer {w}"
-        assert int(flags[w][0]) == 1, f"flag not raised in array {w}"
-    assert int(flags[0][1]) == 0 and int(epoch[0]) == 1
+        assert int(flags[w][0]) == 2, f"flag not raised in array {w}"
+    assert int(flags[0][1]) == 0 and int(epoch[0]) == 2
     outs[0].zero_()
     flags[0].zero_()
     epoch.zero_()
