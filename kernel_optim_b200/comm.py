@@ -95,10 +95,12 @@ class PeerWatch:
     ``beat`` stamps this rank's heartbeat (wall-clock seconds); ``fail`` records this rank's
     failure; ``check`` raises ``PeerFailure`` when any rank recorded one or, at most every
     ``period_s`` seconds, when a peer's heartbeat is older than ``stale_s`` (a peer that stamped
-    none yet is not judged). One store round trip per ``check`` in between.
+    none yet is not judged; ``stale_s=None`` judges none: for ranks that may legitimately sit
+    idle between their checks for longer than any fixed limit). One store round trip per
+    ``check`` in between.
     """
 
-    def __init__(self, group=None, stale_s: float = DEFAULT_STALE_S, period_s: float = 0.5,
+    def __init__(self, group=None, stale_s: float | None = DEFAULT_STALE_S, period_s: float = 0.5,
                  store=None, rank: int | None = None, world: int | None = None):
         pg = _pg(group)
         self.store = store if store is not None else pg.get_group_store()
@@ -128,14 +130,14 @@ class PeerWatch:
 
     def check(self) -> None:
         """Raise ``PeerFailure`` if a rank recorded a failure or a peer went silent; otherwise
-        stamp this rank's heartbeat. A store that cannot be reached counts as a failure of the
-        rank that hosts it (rank 0)."""
+        stamp this rank's heartbeat (when heartbeats are judged). A store that cannot be reached
+        counts as a failure of the rank that hosts it (rank 0)."""
         try:
             rec = self.failed()
             if rec is not None:
                 raise PeerFailure(*rec)
             now = time.time()
-            if now >= self._next_scan and self.world > 1:
+            if self.stale_s is not None and now >= self._next_scan and self.world > 1:
                 self._next_scan = now + self.period_s
                 peers = [w for w in range(self.world) if w != self.rank]
                 keys = [_BEAT + str(w) for w in peers]
@@ -146,7 +148,8 @@ class PeerWatch:
                         age = now - float(t.decode())
                         if age > self.stale_s:
                             raise PeerFailure(w, f"no heartbeat for {age:.1f} s")
-            self.beat()
+            if self.stale_s is not None:
+                self.beat()
         except PeerFailure:
             raise
         except Exception as e:

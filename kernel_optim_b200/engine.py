@@ -81,7 +81,9 @@ class Engine:
         self.use_gemv = gemv
         self.world = 1 if group is None else torch.distributed.get_world_size(group)
         self.rank = 0 if group is None else torch.distributed.get_rank(group)
-        self.watch = PeerWatch(group) if self.world > 1 else None
+        # failure records only: between generate calls a live rank may sit idle for any time, so
+        # a peer that is gone shows instead as the fused gather's timeout in the error word
+        self.watch = PeerWatch(group, stale_s=None) if self.world > 1 else None
         h0, _ = head_range(self.nkv, self.rank, self.world)
         self.nkv_l = self.nkv // self.world
         self.nq_l = 4 * self.nkv_l
@@ -317,9 +319,9 @@ class Engine:
     @torch.inference_mode()
     def generate(self, input_ids: list[list[int]], max_new_tokens: int):
         """Greedy tokens, one list of B ids per step. Sharded, every rank checks the group's
-        failure record and heartbeats (comm.PeerWatch) before each decode step, records its own
-        failure there when it raises, and at the end reads the attention's device error word
-        (a peer that stopped mid-step shows as KOPT_DEV_ERR_TIMEOUT of the fused gather)."""
+        failure record (comm.PeerWatch) before each decode step, records its own failure there
+        when it raises, and reads the attention's device error word after every step and at the
+        end (a peer that stopped shows as KOPT_DEV_ERR_TIMEOUT of the fused gather)."""
         if self.watch is None:
             yield from self._generate(input_ids, max_new_tokens)
             return
