@@ -15,15 +15,17 @@
 //   warp 9   allocates all 512 tensor-memory columns (S_A, S_B, O_A, O_B, fp32) and one thread
 //            issues the MMAs in the order S_A(0) S_B(0), then per j: O_A += P_A(j) V_j,
 //            S_A(j+1), O_B += P_B(j) V_j, S_B(j+1): while one softmax group works on its scores,
-//            the tensor core computes the other group's. S = Q K^T has M = 128 query rows,
+//            the tensor core computes the other group's. Each P V goes in two halves of 64 keys,
+//            the first issued as soon as its half of P is written. S = Q K^T has M = 128 query rows,
 //            N = 128 keys, K-major operands from shared memory; P V takes P from tensor memory
 //            (the A operand) and V from shared memory as an MN-major operand;
 //   warps 0-3 / 4-7: the softmax of tile A / B, one thread per query row (tensor-memory lane):
 //            the row of S_j by tcgen05.ld, the diagonal tile masked, online softmax in fp32 in the
-//            exp2 domain, and P_j written back as bf16 pairs over the first 64 columns of its S
-//            buffer by tcgen05.st. The running maximum only moves when a row's maximum grows by
-//            more than 2^8, so O is rescaled rarely, by the thread that needs it; at the end of
-//            the item O / l goes to the output as bf16.
+//            exp2 domain (packed two-lane FFMA / FADD), and P_j written back as bf16 pairs over
+//            the first 64 columns of its S buffer by tcgen05.st, keys 0-63 handed over first.
+//            The running maximum only moves when a row's maximum grows by more than 2^8, so O
+//            is rescaled rarely, by the thread that needs it, before P_j is handed over; at the
+//            end of the item O / l goes to the output as bf16.
 // The MMAs of one thread execute in issue order, and a commit tracks every MMA issued before it:
 // S_x(j+1) is issued after O_x += P_x(j) V_j, so when a softmax thread sees S_x(j+1) complete, the
 // P V that read P_x(j) (same columns) is complete too, and O_x may be rescaled. Every wait is
@@ -72,7 +74,8 @@ struct __align__(1024) PSmem {
   bf16 v[kPStages][2][kPHalf];      // value tiles, same layout (read as an MN-major operand)
   unsigned long long qfull, qempty;
   unsigned long long kfull[kPStages], vfull[kPStages], kempty[kPStages], vempty[kPStages];
-  unsigned long long sfull[kPHeads], pfull[kPHeads], odone[kPHeads], oempty[kPHeads], drain;
+  unsigned long long sfull[kPHeads], plo[kPHeads], pfull[kPHeads], odone[kPHeads], oempty[kPHeads];
+  unsigned long long drain;
   uint32_t tmem;
   volatile int abort;
 };
@@ -106,6 +109,22 @@ __device__ __forceinline__ Item item_of(const PrefillParams& p, int w) {
   return it;
 }
 
+// Two fp32 lanes per instruction (sm_100 packed FFMA / FADD).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 template <bool PAGED>
 __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid_constant__ PrefillParams p) {
   extern __shared__ unsigned char smem_raw[];
@@ -125,6 +144,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
     }
     for (int x = 0; x < kPHeads; ++x) {
       mbar_init(smem_u32(&s.sfull[x]), 1);
+      mbar_init(smem_u32(&s.plo[x]), kPRows);
       mbar_init(smem_u32(&s.pfull[x]), kPRows);
       mbar_init(smem_u32(&s.odone[x]), 1);
       mbar_init(smem_u32(&s.oempty[x]), kPRows);
@@ -241,7 +261,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
   } else if (warp == kPMma) {
     if (lane == 0) {
       // ---- MMA issuer. Per item: S_A(0), S_B(0); then per key tile j: O_A += P_A(j) V_j,
-      // S_A(j+1), O_B += P_B(j) V_j, S_B(j+1). Tiles are counted across items (T).
+      // S_A(j+1), O_B += P_B(j) V_j, S_B(j+1), each P V in two halves of 64 keys (plo: the
+      // first half of P is written; pfull: all of it). Tiles are counted across items (T).
       auto issue_s = [&](int x, int st) {   // S_x = Q_x K^T
         const uint32_t qa = smem_u32(&s.q[x][0][0]), ka = smem_u32(&s.k[st][0][0]);
 #pragma unroll
@@ -250,10 +271,10 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
           umma_bf16(tmem + col_s(x), sw128_desc(qa + off), sw128_desc(ka + off), kIdescS, kk > 0);
         }
       };
-      auto issue_pv = [&](int x, int st, bool acc) {   // O_x (+)= P_x V, P_x from tensor memory
+      auto issue_pv = [&](int x, int st, bool acc, int half) {   // O_x (+)= P_x V (keys of one half)
         const uint32_t va = smem_u32(&s.v[st][0][0]);
 #pragma unroll
-        for (int kk = 0; kk < kPKeys / 16; ++kk) {
+        for (int kk = half * kPKeys / 32; kk < (half + 1) * kPKeys / 32; ++kk) {
           const uint64_t bdesc = sw128_mn_desc(va + kk * 16 * 128, kPHalfBytes, 1024);
           umma_bf16_ts(tmem + col_o(x), tmem + col_s(x) + 8 * kk, bdesc, kIdescO,
                        (acc || kk > 0) ? 1u : 0u);
@@ -278,14 +299,20 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
           const bool more = j + 1 < nt;
           // O_A += P_A(j) V_j (the first P V of an item overwrites O_A, once the previous item's
           // output has been read out of it)
-          if (!mbar_wait(smem_u32(&s.pfull[0]), T & 1, s, p.err, true) ||
+          if (!mbar_wait(smem_u32(&s.plo[0]), T & 1, s, p.err, true) ||
               !mbar_wait(smem_u32(&s.vfull[st]), (T >> 1) & 1, s, p.err, true) ||
               (j == 0 && i > 0 && !mbar_wait(smem_u32(&s.oempty[0]), (i - 1) & 1, s, p.err, true))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(0, st, j > 0);
+          issue_pv(0, st, j > 0, 0);
+          if (!mbar_wait(smem_u32(&s.pfull[0]), T & 1, s, p.err, true)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(0, st, true, 1);
           if (!more) umma_commit(smem_u32(&s.odone[0]));
           if (more) {   // S_A(j+1): after the P V that read P_A(j) from the same columns
             if (!mbar_wait(smem_u32(&s.kfull[st1]), ((T + 1) >> 1) & 1, s, p.err, true)) {
@@ -297,13 +324,19 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
             umma_commit(smem_u32(&s.sfull[0]));
           }
           // O_B += P_B(j) V_j
-          if (!mbar_wait(smem_u32(&s.pfull[1]), T & 1, s, p.err, true) ||
+          if (!mbar_wait(smem_u32(&s.plo[1]), T & 1, s, p.err, true) ||
               (j == 0 && i > 0 && !mbar_wait(smem_u32(&s.oempty[1]), (i - 1) & 1, s, p.err, true))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(1, st, j > 0);
+          issue_pv(1, st, j > 0, 0);
+          if (!mbar_wait(smem_u32(&s.pfull[1]), T & 1, s, p.err, true)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(1, st, true, 1);
           umma_commit(smem_u32(&s.vempty[st]));
           if (!more) umma_commit(smem_u32(&s.odone[1]));
           if (more) {   // S_B(j+1); then K_{j+1} has been read by both
@@ -361,33 +394,15 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
           m = mx;
           l *= alpha;
         }
-        // P = 2^(s * scale * log2(e) - m) as bf16 pairs, written over the first 64 columns of
-        // S_x 16 words at a time (word e holds keys 2e, 2e + 1; the scores are all in registers
-        // already); l sums the fp32 p
-        float sum0 = 0.f, sum1 = 0.f;
-        const float nm = -m;
-#pragma unroll
-        for (int ch = 0; ch < kPKeys / 32; ++ch) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float p0 = ex2_fast(fmaf(sv[32 * ch + 2 * e], p.scale_log2, nm));
-            const float p1 = ex2_fast(fmaf(sv[32 * ch + 2 * e + 1], p.scale_log2, nm));
-            sum0 += p0;
-            sum1 += p1;
-            pk[e] = pack_bf16(p0, p1);
-          }
-          tmem_st16u(lrow + col_s(x) + 16 * ch, pk);
-        }
-        l += sum0 + sum1;
         if (__any_sync(0xffffffffu, need) && j > 0) {   // O_x row *= alpha (1 where not needed)
+#pragma unroll 1
+          for (int c = 0; c < kPD; c += 16) {
+            float o[16];
+            uint32_t u[16];
+            tmem_ld16(lrow + col_o(x) + c, o);
 #pragma unroll
-          for (int c = 0; c < kPD; c += 32) {
-            float o[32];
-            tmem_ld32(lrow + col_o(x) + c, o);
-#pragma unroll
-            for (int q = 0; q < 32; ++q) o[q] *= alpha;
-            tmem_st32(lrow + col_o(x) + c, o);
+            for (int q = 0; q < 16; ++q) u[q] = __float_as_uint(o[q] * alpha);
+            tmem_st16u(lrow + col_o(x) + c, u);
           }
         }
         if (x == 0 && diag && (j + 1) * kPKeys > p.S) {
@@ -406,7 +421,31 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_attn_kernel(const __grid
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the MMA
         }
-        tmem_wait_st();   // P_x(j) (and a rescaled O_x row) in tensor memory
+        // P = 2^(s * scale * log2(e) - m) as bf16 pairs, written over the first 64 columns of
+        // S_x 16 words at a time (word e holds keys 2e, 2e + 1; the scores are all in registers
+        // already); l sums the fp32 p. The first 64 keys are handed over before the rest, so
+        // their half of P V runs while the second half is computed.
+        float2 sum = make_float2(0.f, 0.f);
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m, -m);
+#pragma unroll
+        for (int ch = 0; ch < kPKeys / 32; ++ch) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float2 x2 = fma2(make_float2(sv[32 * ch + 2 * e], sv[32 * ch + 2 * e + 1]), sc2, nm2);
+            const float2 p2 = make_float2(ex2_fast(x2.x), ex2_fast(x2.y));
+            sum = add2(sum, p2);
+            pk[e] = pack_bf16(p2.x, p2.y);
+          }
+          tmem_st16u(lrow + col_s(x) + 16 * ch, pk);
+          if (ch == 1) {
+            tmem_wait_st();   // P_x(j) of keys 0-63 (and a rescaled O_x row) in tensor memory
+            tc_fence_before();
+            mbar_arrive(smem_u32(&s.plo[x]));
+          }
+        }
+        l += sum.x + sum.y;
+        tmem_wait_st();   // P_x(j) in tensor memory
         tc_fence_before();
         mbar_arrive(smem_u32(&s.pfull[x]));
       }
