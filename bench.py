@@ -76,6 +76,9 @@ def parse_args():
     ap.add_argument("--no-gemv", action="store_true",
                     help="c5: cuBLAS GEMMs + separate SwiGLU / residual kernels instead of the "
                          "tcgen05 skinny-GEMM projections with fused epilogues (kopt_gemv)")
+    ap.add_argument("--spec", action="store_true",
+                    help="c5: speculative decoding (n-gram drafts + the T > 1 verify step), as the "
+                         "reference's ENGINE_SPEC=1 (which this flag stands for; the variable works too)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-strong", action="store_true",
@@ -904,7 +907,7 @@ def run_engine(args):
                          QWEN3_4B["vocab"], seed=0, device=dev)
     eng = Engine.from_model(model, dev, group=dist.group.WORLD if dist is not None else None,
                             overlap=not args.no_overlap, gemv=not args.no_gemv,
-                            prefill=args.prefill)
+                            prefill=args.prefill, spec=True if args.spec else None)
     g = torch.Generator().manual_seed(5)
     prompts = torch.randint(0, QWEN3_4B["vocab"], (B, S), generator=g).tolist()
     for _ in range(max(1, args.warmup)):
@@ -950,6 +953,11 @@ def run_engine(args):
         "wall_s_per_generate": round(wall, 3), "device_error_bits": err,
         "gpu_launches": None, "tokens_sample": toks[0][:4],
     }
+    if eng.K:
+        line["speculative"] = {"draft_tokens": eng.K, "verify_steps_last_generate": eng.spec_steps,
+                               "one_token_step_ms": round(eng.step_ms, 4),
+                               "verify_step_ms": round(eng.verify_ms, 4),
+                               "breakeven_tokens_per_verify": round(eng.breakeven, 3)}
     if rank == 0:
         print(json.dumps(line), flush=True)
     eng.close()

@@ -31,6 +31,8 @@ between steps (comm.PeerWatch in ``generate``) and by the kernel's bounded flag 
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from ._lib import KoptError, dev_error_text
@@ -41,26 +43,31 @@ from .prefill import prefill_attention
 from .gather import PeerGather, slot_of
 from .gemv import EPI_ARGMAX, EPI_BF16, EPI_RESID, EPI_SWIGLU, Gemv
 from .shard import head_range, shard_qkv_weight
+from .spec import HOST_MS, draft_len, drain_one_token, speculate
 
 
 class Engine:
     def __init__(self, model_path: str, device: str = "cuda:0", group=None, overlap: bool = True,
-                 gemv: bool = True, prefill: str = "native"):
+                 gemv: bool = True, prefill: str = "native", spec: bool | None = None):
         from transformers import AutoModelForCausalLM
         model = AutoModelForCausalLM.from_pretrained(
             model_path, dtype=torch.bfloat16, attn_implementation="sdpa", local_files_only=True)
-        self._init(model.eval().to(device), device, group, overlap, gemv, prefill)
+        self._init(model.eval().to(device), device, group, overlap, gemv, prefill, spec)
 
     @classmethod
-    def from_model(cls, model, device: str = "cuda:0", group=None,
-                   overlap: bool = True, gemv: bool = True, prefill: str = "native") -> "Engine":
+    def from_model(cls, model, device: str = "cuda:0", group=None, overlap: bool = True,
+                   gemv: bool = True, prefill: str = "native", spec: bool | None = None) -> "Engine":
         """Wrap an already loaded Qwen3ForCausalLM (bf16, sdpa) instead of reading a checkpoint."""
         self = cls.__new__(cls)
-        self._init(model.eval().to(device), device, group, overlap, gemv, prefill)
+        self._init(model.eval().to(device), device, group, overlap, gemv, prefill, spec)
         return self
 
     # ------------------------------------------------------------------ construction
-    def _init(self, model, device, group, overlap=True, gemv=True, prefill="native"):
+    def _init(self, model, device, group, overlap=True, gemv=True, prefill="native", spec=None):
+        """spec: speculative decoding with n-gram drafts and the T > 1 verify step (spec.py); by
+        default ENGINE_SPEC=1 turns it on and ENGINE_MIN_ADVANCE overrides the measured
+        break-even, as in the reference (engine.py:38-45). One GPU only (the fused gather is
+        T = 1)."""
         if prefill not in ("native", "transformers"):
             raise KoptError("prefill must be 'native' or 'transformers'")
         self.prefill = prefill
@@ -84,6 +91,10 @@ class Engine:
         # failure records only: between generate calls a live rank may sit idle for any time, so
         # a peer that is gone shows instead as the fused gather's timeout in the error word
         self.watch = PeerWatch(group, stale_s=None) if self.world > 1 else None
+        self.spec = (os.environ.get("ENGINE_SPEC", "0") == "1") if spec is None else bool(spec)
+        self.spec = self.spec and self.world == 1
+        ma = os.environ.get("ENGINE_MIN_ADVANCE")
+        self.min_advance = float(ma) if ma is not None else None
         h0, _ = head_range(self.nkv, self.rank, self.world)
         self.nkv_l = self.nkv // self.world
         self.nq_l = 4 * self.nkv_l
@@ -125,8 +136,11 @@ class Engine:
         if self._shape == (B, S, N):
             return
         self.graph = None
+        self.gk = None
         self._shape = None
-        cap = S + N + 1
+        self.K = draft_len(B) if self.spec and N > 2 else 0
+        # speculating, a sequence can run ahead of the slowest one by up to N + K tokens
+        cap = S + 2 * N + 2 * self.K + 2 if self.K else S + N + 1
         self.cos, self.sin = self._rope(cap)
         pages = B * ((cap + PAGE - 1) // PAGE)
         self.cache = PagedKVCache(self.n_layers, pages, self.nkv_l, self.d, B, cap, self.device)
@@ -175,8 +189,47 @@ class Engine:
         self.pin_err = (torch.zeros(N + 1, dtype=torch.int32, pin_memory=True)
                         if self.watch is not None else None)
         self.events = [torch.cuda.Event() for _ in range(N + 1)]
+        self.pin_pos = torch.empty(B, dtype=torch.int32, pin_memory=True)
         self.graph = self._capture(self._step)
+        if self.K:
+            self._setup_verify(B, S)
         self._shape = (B, S, N)
+
+    def _setup_verify(self, B, S):
+        """The verify step's buffers, plan and graph, and the break-even advance per verify step
+        (engine.py:209-223): measured from the two graphs unless ENGINE_MIN_ADVANCE is set."""
+        T, dev, bf = self.K + 1, self.device, torch.bfloat16
+        M, H = B * T, self.embed.shape[1]
+        self.attnk = PagedDecodeAttention(B, self.nq_l, self.nkv_l, self.d, dev, self.cache.capacity,
+                                          eps=self.eps, T=T)
+        self.vin = torch.zeros(B, T, dtype=torch.int64, device=dev)
+        self.vout = torch.zeros(B, T, dtype=torch.int64, device=dev)
+        self.pin_vin = torch.empty(B, T, dtype=torch.int64, pin_memory=True)
+        self.pin_vout = torch.empty(B, T, dtype=torch.int64, pin_memory=True)
+        self.hid_k = torch.zeros(M, H, dtype=bf, device=dev)
+        self.normed_k = torch.zeros(M, H, dtype=bf, device=dev)
+        self.q_k = torch.zeros(M, self.nq_l * self.d, dtype=bf, device=dev)
+        self.out_k = torch.zeros(M, self.nq_l * self.d, dtype=bf, device=dev)
+        self.act_k = torch.zeros(M, self.inter, dtype=bf, device=dev)
+        self.ev_k = torch.cuda.Event()
+        self.gk = self._capture(self._stepk)
+        t1, tk = self._time_graph(self.graph, S), self._time_graph(self.gk, S)
+        self.breakeven = (tk + HOST_MS) / t1 if self.min_advance is None else self.min_advance
+        self.step_ms, self.verify_ms = t1, tk
+
+    def _time_graph(self, g, S, reps=10):
+        """ms per replay, from a position where every write stays inside the cache."""
+        start = max(0, min(S, self.cap - (reps + 2) - (self.K + 1)))
+        torch.cuda.synchronize(self.device)
+        self.pos.fill_(start)
+        g.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize(self.device)
+        return a.elapsed_time(b) / reps
 
     def _capture(self, fn):
         # warm up on a side stream (cuBLAS handles, kernel attributes), then capture once
@@ -240,6 +293,42 @@ class Engine:
         logits = self.model.lm_head(n)
         torch.argmax(logits, dim=-1, out=self.ids)
         self.pos.add_(1)
+
+    def _stepk(self):
+        """Verify step (engine.py:403-415): rows vin[b] = the last accepted token and K drafts at
+        positions pos[b] .. pos[b] + K; vout[b] = the greedy pick after each. The layer loop of the
+        cuBLAS decode step over B (K + 1) rows, with the prologue appending the K + 1 tokens' K/V
+        to the pages (kopt_qk_norm_rope, T = K + 1) and the T > 1 verify attention
+        (kopt_decode_attn), each query row seeing the keys up to its own position."""
+        T = self.K + 1
+        h, n = self.hid_k, self.normed_k
+        torch.index_select(self.embed, 0, self.vin.view(-1), out=h)
+        delta = None
+        for i, lw in enumerate(self.layers):
+            add_rms_norm(h, delta, lw["w_in"], n, self.eps)
+            qkv = torch.mm(n, lw["qkv"].t())
+            qk_norm_rope_paged(qkv, lw["q_norm"], lw["k_norm"], self.cos, self.sin, self.pos, self.q_k,
+                               self.cache, i, T, self.eps, self.nq_l, self.nkv_l, self.d)
+            self.attnk.attend(self.q_k, self.cache, i, self.pos, self.out_k)
+            add_rms_norm(h, torch.mm(self.out_k, lw["o"].t()), lw["w_post"], n, self.eps)
+            silu_mul(torch.mm(n, lw["gu"].t()), self.act_k)
+            delta = torch.mm(self.act_k, lw["down"].t())
+        add_rms_norm(h, delta, self.final_norm, n, self.eps)
+        torch.argmax(self.model.lm_head(n), dim=-1, out=self.vout.view(-1))
+
+    def _verify(self, rows, positions):
+        """One verify forward from the host: rows [B][K + 1] at positions [B]; the picks back."""
+        stream = torch.cuda.current_stream(self.device)
+        self.pin_vin.copy_(torch.tensor(rows, dtype=torch.int64))
+        self.pin_pos.copy_(torch.tensor(positions, dtype=torch.int32))
+        self.vin.copy_(self.pin_vin, non_blocking=True)
+        self.pos.copy_(self.pin_pos, non_blocking=True)
+        self.gk.replay()
+        self.pin_vout.copy_(self.vout, non_blocking=True)
+        self.ev_k.record(stream)
+        self.ev_k.synchronize()
+        self.spec_steps += 1
+        return self.pin_vout.tolist()
 
     def _qkv_full(self, i):
         """Layer i's QKV weight for all heads (prefill attends with every head on every rank)."""
@@ -350,6 +439,10 @@ class Engine:
         ids_h, ev = self.pin_ids, self.events
         ids_h[0].copy_(self.ids, non_blocking=True)
         ev[0].record(stream)
+        self.spec_steps = 0
+        if self.K:
+            yield from self._generate_spec(input_ids, N, S)
+            return
         # queue the next step before waiting on the current one (engine.py:509-533)
         err_h = self.pin_err
         for j in range(1, N):
@@ -368,6 +461,41 @@ class Engine:
             yield ids_h[j - 1].tolist()
         ev[N - 1].synchronize()
         yield ids_h[N - 1].tolist()
+
+    def _generate_spec(self, input_ids, N, S):
+        """Speculative generate (engine.py:451-508): verify steps while they pay for themselves,
+        then the one-token graph from each sequence's own position."""
+        self.events[0].synchronize()
+        first = self.pin_ids[0].tolist()
+        yield first
+        if N == 1:
+            return
+        outs = yield from speculate(input_ids, first, N, self.K, self._verify, self.breakeven)
+        ready = min(len(o) for o in outs)
+        if ready >= N:
+            return
+        # hand each sequence's last token and position to the one-token graph
+        self.pin_ids[0].copy_(torch.tensor([o[-1] for o in outs], dtype=torch.int64))
+        self.pin_pos.copy_(torch.tensor([S + len(o) - 1 for o in outs], dtype=torch.int32))
+        self.ids.copy_(self.pin_ids[0], non_blocking=True)
+        self.pos.copy_(self.pin_pos, non_blocking=True)
+        yield from drain_one_token(outs, N, self._one_token_steps(N - ready))
+
+    def _one_token_steps(self, n):
+        """n replays of the one-token graph, each queued before the host waits on the one before;
+        yields each step's token ids."""
+        stream = torch.cuda.current_stream(self.device)
+        ids_h, ev = self.pin_ids, self.events
+        for j in range(1, n + 1):
+            self.graph.replay()
+            ids_h[j].copy_(self.ids, non_blocking=True)
+            ev[j].record(stream)
+            if j > 1:
+                ev[j - 1].synchronize()
+                yield ids_h[j - 1].tolist()
+        if n:
+            ev[n].synchronize()
+            yield ids_h[n].tolist()
 
     def read_error(self) -> int:
         """Device error bits of the attention kernel since the last read (synchronises)."""
