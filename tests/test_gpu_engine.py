@@ -58,19 +58,21 @@ def test_generate_passes_the_reference_quality_rule(small_model, gemv, prefill):
     assert float(exact.float().mean()) >= 0.9, f"argmax agreement {float(exact.float().mean()):.3f}"
 
 
-@pytest.mark.parametrize("B,min_advance", [(2, "0"), (4, "0"), (8, "100")],
-                         ids=["B2-always", "B4-always", "B8-falls-back"])
-def test_speculative_generate(small_model, monkeypatch, B, min_advance):
+@pytest.mark.parametrize("B,min_advance,gemv", [(2, "0", False), (4, "0", False), (8, "100", False),
+                                                (4, "0", True)],
+                         ids=["B2-always", "B4-always", "B8-falls-back", "B4-always-kopt_gemv"])
+def test_speculative_generate(small_model, monkeypatch, B, min_advance, gemv):
     """The speculative path (n-gram drafts, the T = K + 1 verify step on the verify attention,
     acceptance, per-sequence positions; spec.py): the tokens pass the quality rule, and they equal
     the non-speculative engine's on the same cuBLAS projections except at near-ties (both are
     greedy over the same model). ENGINE_MIN_ADVANCE 0 speculates to the end; 100 falls back to
-    the one-token graph at the first break-even check."""
+    the one-token graph at the first break-even check. With the skinny-GEMM projections the
+    one-token step runs on them and the verify step on cuBLAS."""
     monkeypatch.setenv("ENGINE_MIN_ADVANCE", min_advance)
     g = torch.Generator().manual_seed(4)
     S, N = 48, 40
     prompts = torch.randint(0, 4096, (B, S), generator=g)
-    eng = Engine(str(small_model), DEV, gemv=False, spec=True)
+    eng = Engine(str(small_model), DEV, gemv=gemv, spec=True)
     steps = list(eng.generate(prompts.tolist(), N))
     assert eng.K == {2: 6, 4: 6, 8: 4}[B]
     assert len(steps) == N and all(len(s) == B for s in steps)
@@ -82,7 +84,7 @@ def test_speculative_generate(small_model, monkeypatch, B, min_advance):
     margins, exact = replay_margins(eng.model, prompts, generated)
     assert float(margins.max()) <= TIE_MARGIN, f"max margin {float(margins.max()):.3f}"
     assert float(exact.float().mean()) >= 0.9, f"argmax agreement {float(exact.float().mean()):.3f}"
-    plain = torch.tensor(list(Engine(str(small_model), DEV, gemv=False, spec=False)
+    plain = torch.tensor(list(Engine(str(small_model), DEV, gemv=gemv, spec=False)
                               .generate(prompts.tolist(), N))).t()
     same = (plain == generated).all(1).float().mean()
     assert float(same) >= 0.5, f"{float(same):.2f} of the sequences identical to the plain engine's"
