@@ -1,6 +1,6 @@
 """Host side of the speculative decode path (the caller of the T > 1 verify attention).
 
-The reference's engine can speculate (engine/engine.py:36-45, 48-90, 451-508; off unless
+The reference's engine can speculate (engine/engine.py:35-43, 48-90, 451-508; off unless
 ENGINE_SPEC=1): each sequence drafts K tokens by looking up its latest n-gram in its own history
 (prompt and generated tokens, longest n-gram first: 3, 2, 1), one verify forward runs the last
 accepted token and the K drafts as T = K + 1 query rows per sequence at positions pos[b] ..
@@ -98,7 +98,7 @@ def speculate(prompts: list[list[int]], first: list[int], N: int, K: int,
 
     ``verify(rows, positions)`` runs rows[b] = [last accepted token] + K drafts at positions
     positions[b] .. positions[b] + K and returns each row's K + 1 greedy picks. A sequence that
-    already has N tokens keeps its position and its picks are ignored (engine.py:486-487)."""
+    already has N tokens keeps its position and its picks are ignored (engine.py:480-481)."""
     B = len(prompts)
     S = len(prompts[0])
     look = [Lookup(list(p) + [first[b]]) for b, p in enumerate(prompts)]
