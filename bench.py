@@ -891,6 +891,26 @@ def run_prefill(args):
 
 
 # --------------------------------------------------------------------------- c5: the engine
+def engine_launches(eng, N):
+    """This library's kernels launched by one generate() of N tokens (without speculation, whose
+    count depends on the drafts): the native prefill's five per layer (two norms, the q/k norm +
+    RoPE prologue, the prefill attention, SwiGLU) and its final norm, four with the sharded
+    prefill (SDPA attends), none with the Transformers prefill; then N - 1 decode steps of six per
+    layer with the skinny-GEMM projections (two norms, QKV, attention, gate|up, down_proj) and the
+    final norm and LM head, or four per layer with cuBLAS projections (two norms, attention,
+    SwiGLU) and the final norm."""
+    if eng.K:
+        return None
+    L = eng.n_layers
+    if eng.prefill != "native":
+        pre = 0
+    else:
+        pre = (5 if eng.world == 1 else 4) * L + 1
+    step = 6 * L + 2 if eng.gemv is not None and "lm" in eng.gemv else \
+        (6 * L + 1 if eng.gemv is not None else 4 * L + 1)
+    return pre + (N - 1) * step
+
+
 def run_engine(args):
     """BASELINE config c5: random-init Qwen3-4B (std 0.02, seeded), B=32 prompts of 1024 uniform
     ids, 256 new tokens, CUDA-graph decode; KV heads sharded over the torchrun ranks. One step =
@@ -951,7 +971,9 @@ def run_engine(args):
                                    "kernel (NVLink stores)" if world > 1 else "single GPU")},
         "decode_tokens_s": round(B / (step_ms * 1e-3), 1), "decode_step_ms": round(step_ms, 4),
         "wall_s_per_generate": round(wall, 3), "device_error_bits": err,
-        "gpu_launches": None, "tokens_sample": toks[0][:4],
+        "gpu_launches": (None if engine_launches(eng, N) is None
+                         else engine_launches(eng, N) * steps),
+        "tokens_sample": toks[0][:4],
     }
     if eng.K:
         line["speculative"] = {"draft_tokens": eng.K, "verify_steps_last_generate": eng.spec_steps,
