@@ -222,7 +222,8 @@ def dev_error_text(bits: int) -> str:
     if bits & DEV_ERR_LEN:
         names.append("position outside the cache capacity (clamped)")
     if bits & DEV_ERR_TIMEOUT:
-        names.append("mbarrier wait timed out")
+        names.append("a bounded wait timed out (a copy that did not land, or a peer that did "
+                     "not raise its gather flag)")
     if bits & DEV_ERR_ROPE:
         names.append("position outside the RoPE table (clamped)")
     if bits & DEV_ERR_PLAN:
